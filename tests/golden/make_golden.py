@@ -1,0 +1,377 @@
+"""Generate the golden fixtures in this directory by running the reference's own code.
+
+Usage::
+
+    python tests/golden/make_golden.py --reference <mini-inference checkout>
+
+It imports ``engine.kv_cache`` and ``engine.model`` from a checkout of
+Ham12-3/mini-inference (pure Python + PyTorch, run on the CPU) and records:
+
+* ``allocator_traces.json`` -- seeded sequences of allocator calls
+  (``allocate`` with and without token ids, ``register_prefix``,
+  ``ensure_capacity``, ``free`` including double frees, ``can_allocate``, and
+  writes to ``lengths`` as a prefill commit does) with the result of every
+  call and the allocator state after it: block tables, lengths, free-block
+  order, free slot count, refcounts, cached blocks and ``prefix_hit_tokens``
+  (``engine/kv_cache.py:411-560``). The reference's own known-answer test
+  ``tests/test_kv_cache.py:210-243`` is one of the traces.
+* ``write_index.json`` -- ``PagedKVCache.write_index`` on scattered tables
+  (``engine/kv_cache.py:562-573``).
+* ``decode_<name>.npz`` -- ``PagedDecodeContext(...).attend`` on seeded pools
+  filled through ``packed_prefill_context`` (``engine/kv_cache.py:592-620``):
+  the pool before, tables, positions, q, new k/v, the output and the pool after.
+* ``prefill_<name>.npz`` -- ``PackedPrefillContext(...).attend`` without a prefix
+  (several prompts and one prompt alone) and with prefix-cache hits
+  (``engine/kv_cache.py:252-297``).
+
+The reference does not travel with this repository, so the fixtures are
+committed and this script is only rerun by hand.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import random
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def _state(cache) -> dict:
+    return {
+        "block_tables": {str(s): list(t) for s, t in sorted(cache.block_tables.items())},
+        "lengths": {str(s): n for s, n in sorted(cache.lengths.items())},
+        "free_blocks": list(cache._free_blocks),
+        "num_free_slots": cache.num_free_slots,
+        "prefix_hit_tokens": cache.prefix_hit_tokens,
+        "ref_counts": list(cache._ref_counts),
+        "cached_blocks": sorted(cache._block_key),
+    }
+
+
+def _apply(cache, op: dict):
+    kind = op["op"]
+    try:
+        if kind == "allocate":
+            return cache.allocate(op["num_tokens"], token_ids=op["token_ids"])
+        if kind == "register_prefix":
+            return cache.register_prefix(op["slot"], op["token_ids"])
+        if kind == "ensure_capacity":
+            return cache.ensure_capacity(op["slot"], op["num_tokens"])
+        if kind == "free":
+            return cache.free(op["slot"])
+        if kind == "can_allocate":
+            return cache.can_allocate(op["num_tokens"])
+        if kind == "set_length":
+            cache.lengths[op["slot"]] = op["value"]
+            return None
+    except RuntimeError as e:
+        return {"error": "RuntimeError", "message": str(e)}
+    raise ValueError(kind)
+
+
+def _run_trace(PagedKVCache, config: dict, ops: list[dict]) -> dict:
+    cache = PagedKVCache(num_layers=1, num_kv_heads=1, head_dim=4, num_blocks=config["num_blocks"],
+                         block_size=config["block_size"], max_seqs=config["max_seqs"], max_len=config["max_len"],
+                         dtype=torch.float32, device="cpu",
+                         enable_prefix_caching=config["enable_prefix_caching"])
+    steps = []
+    for op in ops:
+        result = _apply(cache, op)
+        steps.append({"op": op, "result": result, "state": _state(cache)})
+    return {"config": config, "steps": steps}
+
+
+def _known_answer_ops() -> tuple[dict, list[dict]]:
+    """The call sequence of the reference's ``test_prefix_blocks_are_shared_refcounted_and_evicted_lru``."""
+    shared = list(range(100, 116))
+    a_tokens = shared + [1, 2, 3]
+    b_tokens = shared + [7, 8]
+    ops = [
+        {"op": "allocate", "num_tokens": len(a_tokens), "token_ids": a_tokens},
+        {"op": "set_length", "slot": 0, "value": len(a_tokens)},
+        {"op": "register_prefix", "slot": 0, "token_ids": a_tokens},
+        {"op": "allocate", "num_tokens": len(b_tokens), "token_ids": b_tokens},
+        {"op": "allocate", "num_tokens": 16, "token_ids": shared},
+        {"op": "free", "slot": 0},
+        {"op": "free", "slot": 1},
+        {"op": "free", "slot": 2},
+        {"op": "allocate", "num_tokens": 18, "token_ids": shared + [5, 6]},
+        {"op": "free", "slot": 2},
+        {"op": "allocate", "num_tokens": 64, "token_ids": list(range(64))},
+        {"op": "free", "slot": 2},
+        {"op": "allocate", "num_tokens": 18, "token_ids": shared + [5, 6]},
+    ]
+    config = {"num_blocks": 16, "block_size": 4, "max_seqs": 4, "max_len": 64, "enable_prefix_caching": True}
+    return config, ops
+
+
+def _bookkeeping_ops() -> tuple[dict, list[dict]]:
+    """The call sequence of the reference's ``test_paged_block_bookkeeping``, plus its double free."""
+    ops = [
+        {"op": "allocate", "num_tokens": 5, "token_ids": None},
+        {"op": "ensure_capacity", "slot": 0, "num_tokens": 8},
+        {"op": "ensure_capacity", "slot": 0, "num_tokens": 9},
+        {"op": "allocate", "num_tokens": 12, "token_ids": None},
+        {"op": "can_allocate", "num_tokens": 1},
+        {"op": "ensure_capacity", "slot": 1, "num_tokens": 13},
+        {"op": "free", "slot": 0},
+        {"op": "can_allocate", "num_tokens": 12},
+        {"op": "free", "slot": 0},
+    ]
+    config = {"num_blocks": 6, "block_size": 4, "max_seqs": 4, "max_len": 32, "enable_prefix_caching": False}
+    return config, ops
+
+
+def _random_ops(seed: int, config: dict, n_ops: int) -> list[dict]:
+    """A serving-like random workload: shared prompt prefixes, prefill commits, decode growth, frees."""
+    rng = random.Random(seed)
+    bs, max_len = config["block_size"], config["max_len"]
+    prefixes = [[rng.randrange(50) for _ in range(rng.randrange(bs, 4 * bs + 3))] for _ in range(3)]
+    live: dict[int, list[int]] = {}  # slot -> token ids (as the test harness believes)
+    # Slot ids mirror the reference's rule so the generator can address them.
+    stack = list(range(config["max_seqs"] - 1, -1, -1))
+    lengths: dict[int, int] = {}
+    ops = []
+    for _ in range(n_ops):
+        r = rng.random()
+        if r < 0.35 or not live:
+            base = list(rng.choice(prefixes)) if rng.random() < 0.7 else []
+            toks = base + [rng.randrange(50) for _ in range(rng.randrange(1, 2 * bs + 2))]
+            toks = toks[: max_len]
+            ids = toks if rng.random() < 0.9 else None
+            n = len(toks) if rng.random() < 0.9 else rng.randrange(0, max_len + 4)
+            ops.append({"op": "allocate", "num_tokens": n, "token_ids": ids})
+            # The generator cannot know whether it succeeded; it is recorded in the trace.
+            # Track optimistically; failed ones are cleaned up by later frees raising errors.
+            if stack:
+                s = stack[-1]
+                live[s] = toks
+        elif r < 0.55:
+            s = rng.choice(sorted(live))
+            n = len(live[s])
+            ops.append({"op": "set_length", "slot": s, "value": n})
+            ops.append({"op": "register_prefix", "slot": s, "token_ids": live[s]})
+            lengths[s] = n
+        elif r < 0.75:
+            s = rng.choice(sorted(live))
+            grow = live[s] + [rng.randrange(50) for _ in range(rng.randrange(1, bs + 2))]
+            live[s] = grow[: max_len + 1]
+            ops.append({"op": "ensure_capacity", "slot": s, "num_tokens": len(live[s])})
+        elif r < 0.8:
+            ops.append({"op": "can_allocate", "num_tokens": rng.randrange(0, max_len + 3)})
+        else:
+            s = rng.choice(sorted(live)) if rng.random() < 0.9 else rng.randrange(config["max_seqs"])
+            ops.append({"op": "free", "slot": s})
+            live.pop(s, None)
+    return ops
+
+
+def _fix_trace_slots(PagedKVCache, config: dict, ops: list[dict]) -> list[dict]:
+    """Drop ops that address slots the reference never handed out (a KeyError is not part of the API)."""
+    cache = PagedKVCache(num_layers=1, num_kv_heads=1, head_dim=4, num_blocks=config["num_blocks"],
+                         block_size=config["block_size"], max_seqs=config["max_seqs"], max_len=config["max_len"],
+                         dtype=torch.float32, device="cpu", enable_prefix_caching=config["enable_prefix_caching"])
+    kept = []
+    for op in ops:
+        if op["op"] in ("register_prefix", "ensure_capacity", "set_length") and op["slot"] not in cache.block_tables:
+            continue
+        if op["op"] == "set_length":  # a prefill commit never exceeds the blocks it was given
+            op = dict(op, value=min(op["value"], len(cache.block_tables[op["slot"]]) * cache.block_size))
+        _apply(cache, op)
+        kept.append(op)
+    return kept
+
+
+def make_allocator_traces(PagedKVCache) -> None:
+    traces = []
+    for cfg, ops in (_known_answer_ops(), _bookkeeping_ops()):
+        traces.append(_run_trace(PagedKVCache, cfg, ops))
+    random_cfgs = [
+        {"num_blocks": 24, "block_size": 4, "max_seqs": 6, "max_len": 48, "enable_prefix_caching": True},
+        {"num_blocks": 40, "block_size": 16, "max_seqs": 5, "max_len": 160, "enable_prefix_caching": True},
+        {"num_blocks": 12, "block_size": 4, "max_seqs": 4, "max_len": 32, "enable_prefix_caching": False},
+        {"num_blocks": 9, "block_size": 2, "max_seqs": 8, "max_len": 16, "enable_prefix_caching": True},
+    ]
+    for seed, cfg in enumerate(random_cfgs):
+        ops = _fix_trace_slots(PagedKVCache, cfg, _random_ops(seed, cfg, 160))
+        traces.append(_run_trace(PagedKVCache, cfg, ops))
+    (HERE / "allocator_traces.json").write_text(json.dumps(traces, separators=(",", ":")))
+
+
+def make_write_index(PagedKVCache) -> None:
+    cache = PagedKVCache(num_layers=1, num_kv_heads=1, head_dim=4, num_blocks=32, block_size=4, max_seqs=4,
+                         max_len=64, dtype=torch.float32, device="cpu")
+    slots = [cache.allocate(0) for _ in range(3)]
+    for grow in range(1, 6):
+        for s in slots:
+            cache.ensure_capacity(s, grow * 4 + s)
+    cases = []
+    for starts, counts in (([0, 0, 0], [5, 9, 3]), ([3, 7, 0], [4, 1, 13]), ([19, 0, 4], [1, 20, 0])):
+        b, o = cache.write_index(slots, starts, counts)
+        cases.append({"slots": slots, "starts": starts, "counts": counts, "blocks": b.tolist(), "offsets": o.tolist()})
+    out = {"block_size": 4, "tables": {str(s): cache.block_tables[s] for s in slots}, "cases": cases}
+    (HERE / "write_index.json").write_text(json.dumps(out, separators=(",", ":")))
+
+
+def _written_rows(before: torch.Tensor, after: torch.Tensor) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Rows ``[block, :, offset]`` of one layer that the call changed, and their new contents.
+
+    Storing only these keeps the fixtures small; the full after-state is
+    ``before`` with exactly these rows replaced.
+    """
+    diff = (before != after).any(dim=(1, 3))  # [blocks, block_size]
+    blocks, offsets = torch.nonzero(diff, as_tuple=True)
+    return blocks.numpy(), offsets.numpy(), _np(after[blocks, :, offsets])
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.bfloat16:  # numpy has no bfloat16: keep the bit pattern
+        return t.view(torch.int16).numpy().copy()
+    return t.numpy().copy()
+
+
+def make_decode_case(PagedKVCache, name: str, dtype, hq: int, hkv: int, d: int, bs: int, num_blocks: int,
+                     lengths: list[int], layers: int, layer: int, seed: int) -> None:
+    torch.manual_seed(seed)
+    cache = PagedKVCache(num_layers=layers, num_kv_heads=hkv, head_dim=d, num_blocks=num_blocks, block_size=bs,
+                         max_seqs=len(lengths) + 1, max_len=num_blocks * bs, dtype=dtype, device="cpu")
+    # Stale data everywhere: the kernel must never read outside a sequence's table and length.
+    cache.k.normal_()
+    cache.v.normal_()
+    slots = [cache.allocate(0) for _ in lengths]
+    # Interleaved growth scatters each sequence's blocks over the pool.
+    most = max(lengths) + 1
+    for n in range(1, most + bs, bs):
+        for s, ln in zip(slots, lengths):
+            cache.ensure_capacity(s, min(ln + 1, n))
+    with torch.inference_mode():
+        for s, ln in zip(slots, lengths):
+            if ln == 0:
+                continue
+            ctx = cache.packed_prefill_context([s], [ln])
+            for li in range(layers):
+                ctx.attend(li, torch.randn(1, hq, ln, d).to(dtype), torch.randn(1, hkv, ln, d).to(dtype),
+                           torch.randn(1, hkv, ln, d).to(dtype))
+            ctx.commit()
+        k_before, v_before = cache.k.clone(), cache.v.clone()
+        batch = len(slots)
+        q = torch.randn(batch, hq, 1, d).to(dtype)
+        k_new = torch.randn(batch, hkv, 1, d).to(dtype)
+        v_new = torch.randn(batch, hkv, 1, d).to(dtype)
+        ctx = cache.decode_context(slots)
+        positions = ctx.positions.tolist()
+        tables = [list(cache.block_tables[s]) for s in slots]
+        out = ctx.attend(layer, q, k_new, v_new)
+        ctx.commit()
+    width = max(len(t) for t in tables)
+    tab = np.full((batch, width), -1, np.int64)
+    for i, t in enumerate(tables):
+        tab[i, : len(t)] = t
+    others = [li for li in range(layers) if li != layer]
+    assert all(torch.equal(k_before[li], cache.k[li]) and torch.equal(v_before[li], cache.v[li]) for li in others)
+    kb, ko, k_rows = _written_rows(k_before[layer], cache.k[layer])
+    vb, vo, v_rows = _written_rows(v_before[layer], cache.v[layer])
+    np.savez_compressed(
+        HERE / f"decode_{name}.npz",
+        dtype=np.array(str(dtype).replace("torch.", "")), layer=np.array(layer), block_size=np.array(bs),
+        k_before=_np(k_before), v_before=_np(v_before),
+        k_written_at=np.stack([kb, ko]), k_written=k_rows, v_written_at=np.stack([vb, vo]), v_written=v_rows,
+        tables=tab, table_lens=np.array([len(t) for t in tables]), positions=np.array(positions),
+        q=_np(q[:, :, 0]), k_new=_np(k_new[:, :, 0]), v_new=_np(v_new[:, :, 0]), out=_np(out[:, :, 0]),
+        slots=np.array(slots),
+    )
+
+
+def make_prefill_case(PagedKVCache, name: str, dtype, hq: int, hkv: int, d: int, bs: int, num_blocks: int,
+                      prompt_lens: list[int], prefix_len: int, seed: int) -> None:
+    """Packed prefill; with ``prefix_len`` > 0 the first prompt is prefilled alone and registered first."""
+    torch.manual_seed(seed)
+    g = torch.Generator().manual_seed(seed)
+    caching = prefix_len > 0
+    cache = PagedKVCache(num_layers=1, num_kv_heads=hkv, head_dim=d, num_blocks=num_blocks, block_size=bs,
+                         max_seqs=len(prompt_lens) + 2, max_len=num_blocks * bs, dtype=dtype, device="cpu",
+                         enable_prefix_caching=caching)
+    cache.k.normal_()
+    cache.v.normal_()
+    common = torch.randint(0, 1000, (prefix_len,), generator=g).tolist()
+    prompts = [common + torch.randint(0, 1000, (n,), generator=g).tolist() for n in prompt_lens]
+    with torch.inference_mode():
+        if caching:
+            first = cache.allocate(len(prompts[0]), token_ids=prompts[0])
+            n0 = len(prompts[0])
+            ctx = cache.packed_prefill_context([first], [n0])
+            ctx.attend(0, torch.randn(1, hq, n0, d).to(dtype), torch.randn(1, hkv, n0, d).to(dtype),
+                       torch.randn(1, hkv, n0, d).to(dtype))
+            ctx.commit()
+            cache.register_prefix(first, prompts[0])
+            rest = prompts[1:]
+        else:
+            rest = prompts
+        slots = [cache.allocate(len(p), token_ids=p) for p in rest]
+        starts = [cache.lengths[s] for s in slots]
+        new = [len(p) - a for p, a in zip(rest, starts)]
+        total = sum(new)
+        q = torch.randn(1, hq, total, d).to(dtype)
+        k = torch.randn(1, hkv, total, d).to(dtype)
+        v = torch.randn(1, hkv, total, d).to(dtype)
+        k_before, v_before = cache.k.clone(), cache.v.clone()
+        ctx = cache.packed_prefill_context(slots, new)
+        positions = ctx.positions.tolist()
+        last_index = ctx.last_index.tolist()
+        tables = [list(cache.block_tables[s]) for s in slots]
+        out = ctx.attend(0, q, k, v)
+        ctx.commit()
+    width = max(len(t) for t in tables)
+    tab = np.full((len(slots), width), -1, np.int64)
+    for i, t in enumerate(tables):
+        tab[i, : len(t)] = t
+    kb, ko, k_rows = _written_rows(k_before[0], cache.k[0])
+    vb, vo, v_rows = _written_rows(v_before[0], cache.v[0])
+    np.savez_compressed(
+        HERE / f"prefill_{name}.npz",
+        dtype=np.array(str(dtype).replace("torch.", "")), block_size=np.array(bs),
+        k_before=_np(k_before[0]), v_before=_np(v_before[0]),
+        k_written_at=np.stack([kb, ko]), k_written=k_rows, v_written_at=np.stack([vb, vo]), v_written=v_rows,
+        tables=tab, table_lens=np.array([len(t) for t in tables]), starts=np.array(starts), lengths=np.array(new),
+        positions=np.array(positions), last_index=np.array(last_index),
+        q=_np(q[0]), k=_np(k[0]), v=_np(v[0]), out=_np(out[0]), prefix_hit_tokens=np.array(cache.prefix_hit_tokens),
+    )
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--reference", required=True, help="path of a Ham12-3/mini-inference checkout")
+    args = ap.parse_args()
+    sys.path.insert(0, str(Path(args.reference).resolve()))
+    from engine.kv_cache import PagedKVCache  # noqa: E402  (the reference's own class)
+
+    torch.set_num_threads(4)
+    make_allocator_traces(PagedKVCache)
+    make_write_index(PagedKVCache)
+    # The reference's own tiny test shapes (tests/test_kv_cache.py:158-160,179-207): 4 / 2 heads, dim 8, blocks of 4.
+    make_decode_case(PagedKVCache, "fp32_tiny", torch.float32, 4, 2, 8, 4, 12, [6, 9, 3], layers=1, layer=0, seed=1)
+    # Micro-benchmark head shape (Qwen2.5-0.5B): 14 / 2 heads, head_dim 64, blocks of 16.
+    make_decode_case(PagedKVCache, "fp16_h14_d64", torch.float16, 14, 2, 64, 16, 16,
+                     [70, 16, 47, 3, 31, 0], layers=2, layer=1, seed=2)
+    # Qwen2.5-7B head shape: 28 / 4 heads, head_dim 128.
+    make_decode_case(PagedKVCache, "bf16_h28_d128", torch.bfloat16, 28, 4, 128, 16, 8,
+                     [40, 17, 2], layers=1, layer=0, seed=3)
+    make_decode_case(PagedKVCache, "fp16_h28_d128", torch.float16, 28, 4, 128, 16, 9,
+                     [33, 15, 48], layers=1, layer=0, seed=4)
+    make_prefill_case(PagedKVCache, "fp32_tiny_packed", torch.float32, 4, 2, 8, 4, 12, [5, 3, 7], 0, seed=5)
+    make_prefill_case(PagedKVCache, "fp16_single", torch.float16, 14, 2, 64, 16, 5, [50], 0, seed=6)
+    make_prefill_case(PagedKVCache, "fp16_packed", torch.float16, 14, 2, 64, 16, 8, [23, 5, 40], 0, seed=10)
+    make_prefill_case(PagedKVCache, "fp16_prefix", torch.float16, 14, 2, 64, 16, 12, [9, 20, 1, 16], 40, seed=7)
+    make_prefill_case(PagedKVCache, "fp32_tiny_prefix", torch.float32, 4, 2, 8, 4, 24, [3, 10, 7], 9, seed=8)
+    make_prefill_case(PagedKVCache, "bf16_prefix_d128", torch.bfloat16, 28, 4, 128, 16, 8, [12, 9], 32, seed=9)
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

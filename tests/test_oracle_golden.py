@@ -1,0 +1,175 @@
+"""Pin the CPU oracle to the reference: replay every golden fixture through ``oracle/``.
+
+The fixtures were produced by the reference's own ``PagedKVCache`` and
+attention contexts (``tests/golden/make_golden.py``). Allocator state and KV
+writes must match bit for bit; attention outputs within the tolerance below.
+"""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from oracle.block_manager import OracleBlockManager
+from oracle.numerics import round_to, to_compute
+from oracle.paged_kv import decode_attend, packed_prefill_attend, write_index
+
+# fp32 fixtures: the reference computes in float32, the oracle in float64.
+# fp16: the oracle's exact result rounded to fp16 against the reference's (CPU SDPA)
+# result, within the north-star bar of 2e-3 absolute. bf16 values are spaced 2^-8
+# apart already in [0.5, 1), so 2e-3 absolute cannot hold there even for exact
+# arithmetic, and the reference's bf16 CPU SDPA rounds its intermediates to bf16:
+# measured on these fixtures it sits up to 3.9e-3 (4 bf16 steps) from the exact
+# result. The bf16 fixtures therefore pin layout and head mapping at 8e-3
+# absolute plus one bf16 step (2^-7) relative; fp32 and fp16 pin the arithmetic.
+TOL = {"float32": (1e-5, 0.0), "float16": (2e-3, 0.0), "bfloat16": (8e-3, 2.0 ** -7)}
+
+
+def within(got: np.ndarray, ref: np.ndarray, dtype: str) -> float:
+    """Largest excess of |got - ref| over the tolerance (<= 0 means within)."""
+    atol, rtol = TOL[dtype]
+    return float((np.abs(got - ref) - (atol + rtol * np.abs(ref))).max(initial=-1.0))
+
+
+def replay(manager, op: dict):
+    kind = op["op"]
+    try:
+        if kind == "allocate":
+            return manager.allocate(op["num_tokens"], token_ids=op["token_ids"])
+        if kind == "register_prefix":
+            return manager.register_prefix(op["slot"], op["token_ids"])
+        if kind == "ensure_capacity":
+            return manager.ensure_capacity(op["slot"], op["num_tokens"])
+        if kind == "free":
+            return manager.free(op["slot"])
+        if kind == "can_allocate":
+            return manager.can_allocate(op["num_tokens"])
+        if kind == "set_length":
+            manager.lengths[op["slot"]] = op["value"]
+            return None
+    except RuntimeError as e:
+        return {"error": "RuntimeError", "message": str(e)}
+    raise ValueError(kind)
+
+
+def load_traces(golden_dir):
+    return json.loads((golden_dir / "allocator_traces.json").read_text())
+
+
+def test_allocator_traces_match_reference(golden_dir):
+    traces = load_traces(golden_dir)
+    assert len(traces) >= 6
+    for t, trace in enumerate(traces):
+        cfg = trace["config"]
+        m = OracleBlockManager(cfg["num_blocks"], cfg["block_size"], cfg["max_seqs"], cfg["max_len"],
+                               cfg["enable_prefix_caching"])
+        for i, step in enumerate(trace["steps"]):
+            got = replay(m, step["op"])
+            assert got == step["result"], (t, i, step["op"])
+            assert m.state() == step["state"], (t, i, step["op"])
+
+
+def test_allocator_traces_exercise_the_interesting_paths(golden_dir):
+    """The traces must cover prefix hits, LRU eviction of cached blocks, exhaustion and double frees."""
+    seen = {"hit": False, "double_free": False, "exhausted": False, "evicted": False}
+    for trace in load_traces(golden_dir):
+        prev_cached: set[int] = set()
+        for step in trace["steps"]:
+            op, res, st = step["op"], step["result"], step["state"]
+            if isinstance(res, dict) and "freed twice" in res["message"]:
+                seen["double_free"] = True
+            if isinstance(res, dict) and "not enough" in res["message"]:
+                seen["exhausted"] = True
+            if op["op"] == "allocate" and isinstance(res, int) and st["lengths"][str(res)] > 0:
+                seen["hit"] = True
+            if op["op"] in ("allocate", "ensure_capacity") and prev_cached - set(st["cached_blocks"]):
+                seen["evicted"] = True
+            prev_cached = set(st["cached_blocks"])
+    assert all(seen.values()), seen
+
+
+def test_write_index_matches_reference(golden_dir):
+    data = json.loads((golden_dir / "write_index.json").read_text())
+    for case in data["cases"]:
+        tables = [data["tables"][str(s)] for s in case["slots"]]
+        b, o = write_index(tables, case["starts"], case["counts"], data["block_size"])
+        assert b.tolist() == case["blocks"] and o.tolist() == case["offsets"]
+
+
+def _tables(z) -> list[list[int]]:
+    return [list(map(int, row[:n])) for row, n in zip(z["tables"], z["table_lens"])]
+
+
+def _after(before_layer: np.ndarray, at: np.ndarray, rows: np.ndarray) -> np.ndarray:
+    out = before_layer.copy()
+    out[at[0], :, at[1]] = rows
+    return out
+
+
+def _bits(a: np.ndarray, dtype: str) -> np.ndarray:
+    """Bit patterns, so that equality is exact (and NaN-safe)."""
+    a = np.ascontiguousarray(a)
+    if dtype == "float32":
+        return a.astype(np.float32).view(np.uint32)
+    if dtype == "float16":
+        return a.astype(np.float16).view(np.uint16)
+    from oracle.numerics import f32_to_bf16_bits
+
+    return f32_to_bf16_bits(a.astype(np.float32))
+
+
+def decode_cases(golden_dir):
+    return sorted(golden_dir.glob("decode_*.npz"))
+
+
+def prefill_cases(golden_dir):
+    return sorted(golden_dir.glob("prefill_*.npz"))
+
+
+@pytest.mark.parametrize("name", ["fp32_tiny", "fp16_h14_d64", "bf16_h28_d128", "fp16_h28_d128"])
+def test_decode_oracle_matches_reference(golden_dir, name):
+    z = np.load(golden_dir / f"decode_{name}.npz")
+    dt = str(z["dtype"])
+    layer = int(z["layer"])
+    k_pool = to_compute(z["k_before"], dt)[layer].copy()
+    v_pool = to_compute(z["v_before"], dt)[layer].copy()
+    out = decode_attend(k_pool, v_pool, _tables(z), z["positions"].tolist(), to_compute(z["q"], dt),
+                        to_compute(z["k_new"], dt), to_compute(z["v_new"], dt))
+    ref = to_compute(z["out"], dt).astype(np.float64)
+    excess = within(round_to(out, dt), ref, dt)
+    assert excess <= 0, excess
+    # The append: bit-exact against the reference's pool after the call.
+    k_ref = _after(to_compute(z["k_before"], dt)[layer], z["k_written_at"], to_compute(z["k_written"], dt))
+    v_ref = _after(to_compute(z["v_before"], dt)[layer], z["v_written_at"], to_compute(z["v_written"], dt))
+    assert np.array_equal(_bits(k_pool, dt), _bits(k_ref, dt))
+    assert np.array_equal(_bits(v_pool, dt), _bits(v_ref, dt))
+
+
+@pytest.mark.parametrize("name", ["fp32_tiny_packed", "fp16_single", "fp16_packed", "fp16_prefix",
+                                  "fp32_tiny_prefix", "bf16_prefix_d128"])
+def test_prefill_oracle_matches_reference(golden_dir, name):
+    z = np.load(golden_dir / f"prefill_{name}.npz")
+    dt = str(z["dtype"])
+    k_pool = to_compute(z["k_before"], dt).copy()
+    v_pool = to_compute(z["v_before"], dt).copy()
+    out = packed_prefill_attend(k_pool, v_pool, _tables(z), z["starts"].tolist(), z["lengths"].tolist(),
+                                to_compute(z["q"], dt), to_compute(z["k"], dt), to_compute(z["v"], dt))
+    ref = to_compute(z["out"], dt).astype(np.float64)
+    excess = within(round_to(out, dt), ref, dt)
+    assert excess <= 0, excess
+    k_ref = _after(to_compute(z["k_before"], dt), z["k_written_at"], to_compute(z["k_written"], dt))
+    v_ref = _after(to_compute(z["v_before"], dt), z["v_written_at"], to_compute(z["v_written"], dt))
+    assert np.array_equal(_bits(k_pool, dt), _bits(k_ref, dt))
+    assert np.array_equal(_bits(v_pool, dt), _bits(v_ref, dt))
+    # Positions and last-token indices are the reference's exactly.
+    pos = np.concatenate([np.arange(a, a + n) for a, n in zip(z["starts"], z["lengths"])])
+    assert pos.tolist() == z["positions"].tolist()
+    assert (np.cumsum(z["lengths"]) - 1).tolist() == z["last_index"].tolist()
+
+
+def test_prefix_fixtures_really_hit_the_cache(golden_dir):
+    for name in ("fp16_prefix", "fp32_tiny_prefix", "bf16_prefix_d128"):
+        z = np.load(golden_dir / f"prefill_{name}.npz")
+        assert int(z["prefix_hit_tokens"]) > 0 and all(int(a) > 0 for a in z["starts"])
