@@ -1,0 +1,250 @@
+/*
+ * pkv.h -- C ABI of the B200 (sm_100a) paged-KV hot path for mini-inference.
+ *
+ * Every entry point takes plain pointers, sizes and strides (in elements),
+ * returns an int status (PKV_OK == 0) and never allocates device memory:
+ * the caller owns the KV pool, the inputs, the outputs and any workspace.
+ * Kernels are enqueued on the given stream and never synchronise the host,
+ * so every launch can be captured in a CUDA graph.
+ *
+ * The reference (Ham12-3/mini-inference) is pure Python/PyTorch; each entry
+ * point names the reference code it replaces. A Python binding (ctypes) is
+ * in mini_inference_b200/_lib.py.
+ */
+#ifndef PKV_H_
+#define PKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PKV_API __attribute__((visibility("default")))
+#else
+#define PKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* pkv_stream_t; /* same type as cudaStream_t; NULL = legacy default stream */
+
+/* ------------------------------------------------------------------ status */
+enum pkv_status {
+  PKV_OK = 0,
+  PKV_ERR_INVALID_ARGUMENT = 1,   /* null pointer, bad size, stride, alignment or dtype */
+  PKV_ERR_OUT_OF_RANGE = 2,       /* block id, slot or position outside the pool / table */
+  PKV_ERR_WORKSPACE = 3,          /* workspace smaller than pkv_decode_workspace_bytes() */
+  PKV_ERR_CUDA = 4,               /* a CUDA runtime call failed (see pkv_last_cuda_error) */
+  PKV_ERR_NO_BLOCKS = 5,          /* "not enough free KV cache blocks" (engine/kv_cache.py:520) */
+  PKV_ERR_DOUBLE_FREE = 6,        /* "slot freed twice" (engine/kv_cache.py:556) */
+  PKV_ERR_UNKNOWN_SLOT = 7,       /* slot id that does not own a block table */
+  PKV_ERR_UNSUPPORTED = 8,        /* head_dim / group size / dtype combination not built */
+  PKV_ERR_TIMEOUT = 9             /* a bounded device-side wait gave up */
+};
+
+/* Human-readable name of a status code (static string). */
+PKV_API const char* pkv_status_string(int status);
+/* Text of the last CUDA error seen by this library on the calling thread. */
+PKV_API const char* pkv_last_cuda_error(void);
+/* Library version, e.g. 0x000100 for 0.1.0. */
+PKV_API int pkv_version(void);
+
+/* ------------------------------------------------------------------ KV pool */
+enum pkv_dtype { PKV_F16 = 0, PKV_BF16 = 1 };
+
+/*
+ * One KV pool, the reference's layout (engine/kv_cache.py:411-443):
+ *   k, v: [num_layers, num_blocks_total, num_kv_heads, block_size, head_dim], contiguous,
+ * where num_blocks_total includes the scratch block that CUDA-graph padding
+ * rows write to (engine/kv_cache.py:426-429).
+ */
+typedef struct pkv_pool {
+  void* k;
+  void* v;
+  int32_t num_layers;
+  int32_t num_blocks_total;
+  int32_t num_kv_heads;
+  int32_t block_size;
+  int32_t head_dim;
+  int32_t dtype; /* enum pkv_dtype */
+} pkv_pool;
+
+/*
+ * Block tables as the kernels read them: int32 block ids, row r at
+ * block_tables + r * stride, `cols` entries per row. With seq_rows == NULL,
+ * batch entry b reads row b (a padded [batch, cols] table, as the reference
+ * builds at engine/kv_cache.py:606-607). With seq_rows, batch entry b reads row
+ * seq_rows[b] of a device-resident mirror indexed by slot; seq_rows[b] < 0 marks
+ * a CUDA-graph padding row, which reads and writes only the scratch block.
+ */
+typedef struct pkv_tables {
+  const int32_t* block_tables;
+  int64_t stride;
+  int32_t rows;
+  int32_t cols;
+  const int32_t* seq_rows;
+} pkv_tables;
+
+/*
+ * KV append: scatter n_tokens new K/V rows into the pool through slot_mapping
+ * (slot = block * block_size + offset; a negative slot skips the row).
+ * Row t, head h of k_new starts at k_new + t * tok_stride + h * head_stride
+ * (head_dim elements contiguous); v_new uses the same strides.
+ * Replaces the index_put scatters `k_layer[write_blocks, :, write_offsets] = k`
+ * of engine/kv_cache.py:613-614 (decode) and :288-289 (packed prefill), and
+ * engine/cuda_graphs.py:82-83.
+ * status_dev (optional) receives PKV_ERR_OUT_OF_RANGE if a slot is past the pool.
+ */
+PKV_API int pkv_kv_append(const pkv_pool* pool, int32_t layer, const void* k_new, const void* v_new,
+                  int64_t n_tokens, int64_t tok_stride, int64_t head_stride, const int64_t* slot_mapping,
+                  int32_t* status_dev, pkv_stream_t stream);
+
+/*
+ * Paged decode attention, one new token per sequence, optionally fused with
+ * its KV append. Replaces PagedDecodeContext.attend (engine/kv_cache.py:611-620)
+ * = append + block gather + decode_attention (engine/model.py:126-147), and
+ * _GraphDecodeContext.attend (engine/cuda_graphs.py:79-92).
+ *
+ *   q       : row b, query head h at q + b*q_stride_b + h*q_stride_h (head_dim contiguous)
+ *   out     : row b, query head h at out + b*out_stride_b + h*out_stride_h
+ *   k_new/v_new (both NULL = no append): row b, kv head j at k_new + b*kv_stride_b + j*kv_stride_h;
+ *             written to slot_mapping[b] and attended at position context_lens[b]-1
+ *   tables  : see pkv_tables
+ *   context_lens[b]: keys row b attends to (its position + 1), 1..tables->cols*block_size
+ *   scale   : softmax scale (the reference uses 1/sqrt(head_dim))
+ *   workspace: >= pkv_decode_workspace_bytes(...) bytes, 256-byte aligned, zeroed once
+ *             before first use; the kernel leaves it ready for the next call, whatever
+ *             the next call's batch or table width. Calls that share a workspace must
+ *             not overlap on the GPU. batch * num_kv_heads <= 65536.
+ * Query head h reads KV head h / (num_q_heads / num_kv_heads), as the reference's regrouping.
+ */
+PKV_API int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
+                         int32_t num_q_heads, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                         const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_new,
+                         const void* v_new, int64_t kv_stride_b, int64_t kv_stride_h,
+                         const int64_t* slot_mapping, const int32_t* context_lens, float scale,
+                         void* workspace, int64_t workspace_bytes, int32_t* status_dev, pkv_stream_t stream);
+
+/* Workspace bytes pkv_decode_attention needs for these sizes. */
+PKV_API int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
+                                   int32_t block_size, int32_t head_dim, int32_t num_q_heads);
+
+/*
+ * Packed (varlen) prefill attention over the paged cache, prefix-cache hits included.
+ * Replaces PackedPrefillContext.attend (engine/kv_cache.py:283-297) after its append:
+ * sequence s owns packed tokens cu_seqlens[s]..cu_seqlens[s+1]-1, which sit at
+ * positions starts[s] + i; each attends to its own sequence's keys 0..position,
+ * read from the pool (the new tokens must already be appended, pkv_kv_append).
+ *   q   : token t, query head h at q + t*q_stride_t + h*q_stride_h
+ *   out : token t, query head h at out + t*out_stride_t + h*out_stride_h
+ *   tables : see pkv_tables (one row per sequence)
+ */
+PKV_API int pkv_prefill_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t num_seqs,
+                          const int32_t* cu_seqlens, const int32_t* starts, int32_t max_new_tokens,
+                          int32_t num_q_heads, void* out, int64_t out_stride_t, int64_t out_stride_h,
+                          const void* q, int64_t q_stride_t, int64_t q_stride_h, float scale,
+                          int32_t* status_dev, pkv_stream_t stream);
+
+/* ------------------------------------------------------------------ metadata builder (GPU) */
+/*
+ * Decode metadata from a device-resident table mirror, instead of host lists
+ * and an H2D copy per step (engine/kv_cache.py:597-609, engine/cuda_graphs.py:64-77):
+ * (tables->seq_rows is required; lengths[b] = tokens batch entry b already holds)
+ *   positions[b]    = lengths[b]                           (int64, the RoPE position)
+ *   slot_mapping[b] = table[p / bs] * bs + p % bs          (int64, the append target)
+ *   context_lens[b] = p + 1                                (int32)
+ * Rows with seq_rows[b] < 0 are CUDA-graph padding: position 0, slot of the scratch block.
+ */
+PKV_API int pkv_build_decode_metadata(const pkv_tables* tables, int32_t batch, const int32_t* lengths,
+                              int32_t block_size, int32_t scratch_block, int64_t* positions,
+                              int64_t* slot_mapping, int32_t* context_lens, int32_t* status_dev,
+                              pkv_stream_t stream);
+
+/*
+ * Prefill metadata: for sequence s with starts[s] cached tokens and cu_seqlens
+ * new ones, write per packed token its position and slot (PagedKVCache.write_index,
+ * engine/kv_cache.py:562-573, and the positions of engine/kv_cache.py:262-263).
+ */
+PKV_API int pkv_build_prefill_metadata(const pkv_tables* tables, int32_t num_seqs, const int32_t* cu_seqlens,
+                               const int32_t* starts, int32_t block_size, int64_t total_tokens,
+                               int64_t* positions, int64_t* slot_mapping, int32_t* status_dev,
+                               pkv_stream_t stream);
+
+/* lengths[seq_rows[b]] += 1 for every b with seq_rows[b] >= 0: PagedDecodeContext.commit
+ * (engine/kv_cache.py:622-624) for callers that keep per-slot lengths on the device. */
+PKV_API int pkv_commit_decode(const int32_t* seq_rows, int32_t batch, int32_t* lengths, pkv_stream_t stream);
+
+/* Apply (row, column, block) updates to the device table mirror: block_tables[row*stride+col] = block.
+ * Mirrors the host allocator's table edits (engine/kv_cache.py:524-526,550). */
+PKV_API int pkv_update_tables(int32_t* block_tables, int64_t table_stride, int32_t rows, int32_t cols,
+                      const int32_t* updates, int32_t n_updates, int32_t* status_dev, pkv_stream_t stream);
+
+/* Copy whole blocks src[i] -> dst[i], every layer, K and V: copy-on-write of a shared block.
+ * The reference never writes a shared block, so it has no counterpart (engine/kv_cache.py:499-501). */
+PKV_API int pkv_copy_blocks(const pkv_pool* pool, const int32_t* src, const int32_t* dst, int32_t n,
+                    int32_t* status_dev, pkv_stream_t stream);
+
+/* ------------------------------------------------------------------ block manager (host) */
+/*
+ * The reference's allocator and prefix cache (PagedKVCache host bookkeeping,
+ * engine/kv_cache.py:411-560) in C++. Host-only: no CUDA calls.
+ * Blocks are handed out least-recently-freed first; a released block keeps its
+ * prefix key and goes to the tail, a released block without a key goes to the head;
+ * slot ids are taken lowest first and reused last-in first-out.
+ */
+typedef struct pkv_block_manager pkv_block_manager;
+
+PKV_API int pkv_bm_create(int32_t num_blocks, int32_t block_size, int32_t max_seqs, int32_t max_len,
+                  int32_t enable_prefix_caching, pkv_block_manager** out);
+PKV_API void pkv_bm_destroy(pkv_block_manager* bm);
+/* engine/kv_cache.py:462-464 */
+PKV_API int pkv_bm_can_allocate(const pkv_block_manager* bm, int64_t num_tokens, int32_t* out);
+/* engine/kv_cache.py:512-529; token_ids may be NULL (n_ids ignored) for no prefix lookup */
+PKV_API int pkv_bm_allocate(pkv_block_manager* bm, int64_t num_tokens, const int64_t* token_ids, int64_t n_ids,
+                    int32_t* out_slot);
+/* engine/kv_cache.py:531-540 */
+PKV_API int pkv_bm_register_prefix(pkv_block_manager* bm, int32_t slot, const int64_t* token_ids, int64_t n_ids);
+/* engine/kv_cache.py:542-551; *out = 0 when the pool (or max_len) cannot hold num_tokens */
+PKV_API int pkv_bm_ensure_capacity(pkv_block_manager* bm, int32_t slot, int64_t num_tokens, int32_t* out);
+/* engine/kv_cache.py:553-560; PKV_ERR_DOUBLE_FREE for a slot without a table */
+PKV_API int pkv_bm_free(pkv_block_manager* bm, int32_t slot);
+/*
+ * Positions of the next token of each of n slots (= lengths[slot]), checking that each
+ * slot's table holds a block for it: PKV_ERR_OUT_OF_RANGE is the reference's
+ * "a sequence has no block for its next token" (engine/kv_cache.py:597-600),
+ * PKV_ERR_UNKNOWN_SLOT a slot without a table.
+ */
+PKV_API int pkv_bm_decode_positions(const pkv_block_manager* bm, const int32_t* slots, int32_t n, int32_t* out);
+/* lengths[slots[i]] += 1 for each i: PagedDecodeContext.commit (engine/kv_cache.py:622-624). */
+PKV_API int pkv_bm_commit_decode(pkv_block_manager* bm, const int32_t* slots, int32_t n);
+/* lengths[slot] read / write (the reference's public `lengths` dict, engine/kv_cache.py:431) */
+PKV_API int pkv_bm_get_length(const pkv_block_manager* bm, int32_t slot, int64_t* out);
+PKV_API int pkv_bm_set_length(pkv_block_manager* bm, int32_t slot, int64_t value);
+/* the reference's public `block_tables[slot]`: copies up to cap entries, *out_len = table length */
+PKV_API int pkv_bm_get_table(const pkv_block_manager* bm, int32_t slot, int32_t* out, int32_t cap, int32_t* out_len);
+/* live slots in ascending order */
+PKV_API int pkv_bm_live_slots(const pkv_block_manager* bm, int32_t* out, int32_t cap, int32_t* out_len);
+PKV_API int pkv_bm_num_free_blocks(const pkv_block_manager* bm, int32_t* out);
+PKV_API int pkv_bm_num_free_slots(const pkv_block_manager* bm, int32_t* out);
+PKV_API int pkv_bm_prefix_hit_tokens(const pkv_block_manager* bm, int64_t* out);
+/* free-pool order (head first), per-block refcounts, and blocks holding a prefix key (ascending) */
+PKV_API int pkv_bm_free_order(const pkv_block_manager* bm, int32_t* out, int32_t cap, int32_t* out_len);
+PKV_API int pkv_bm_ref_counts(const pkv_block_manager* bm, int32_t* out, int32_t cap);
+PKV_API int pkv_bm_cached_blocks(const pkv_block_manager* bm, int32_t* out, int32_t cap, int32_t* out_len);
+/* Start (1) or stop (0) recording table edits for pkv_bm_drain_table_edits; off by default. */
+PKV_API int pkv_bm_set_journal(pkv_block_manager* bm, int32_t enable);
+/*
+ * Table edits since the last drain as (slot, column, block) triples, for
+ * pkv_update_tables on a device mirror; *out_len = number of triples copied.
+ * The journal is cleared by the drain. *overflow = 1 if triples were dropped
+ * because cap was too small (the caller should then rebuild its mirror).
+ */
+PKV_API int pkv_bm_drain_table_edits(pkv_block_manager* bm, int32_t* out, int32_t cap_triples, int32_t* out_len,
+                             int32_t* overflow);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKV_H_ */

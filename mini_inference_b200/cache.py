@@ -1,0 +1,491 @@
+"""Drop-in paged KV cache for mini-inference, backed by libpkv (C++ allocator + sm_100a kernels).
+
+Mirrors the reference's ``engine/kv_cache.py`` interface for the paged path:
+
+* :class:`PagedKVCache` -- same constructor, ``for_model``, allocator methods
+  (``allocate``, ``ensure_capacity``, ``free``, ``register_prefix``,
+  ``can_allocate``, ``blocks_for``), properties (``num_free_slots``,
+  ``num_free_blocks``) and public attributes (``k``, ``v``, ``lengths``,
+  ``block_tables``, ``block_size``, ``max_len``, ``num_blocks``,
+  ``scratch_block``, ``prefix_hit_tokens``, ``enable_prefix_caching``) as
+  ``engine/kv_cache.py:377-579``. Errors are the reference's: ``RuntimeError``
+  when the pool is out of blocks (``:520``) or a slot is freed twice (``:556``),
+  ``ValueError`` when a sequence has no block for its next token (``:600``) or a
+  packed prefill has no room (``:259``), ``KeyError`` for an unknown slot.
+* :class:`PagedDecodeContext` / :class:`PackedPrefillContext` -- the
+  ``AttentionContext`` objects ``Attention.forward`` calls
+  (``engine/model.py:89-98,250``) with ``attend(layer_idx, q, k, v)`` and
+  ``commit()``, plus ``positions`` / ``last_index`` as the runner reads them
+  (``engine/engine.py:102-106,119-123``).
+
+The block bookkeeping runs in C++ (``csrc/block_manager.cpp``) with the
+reference's exact decisions. Block tables are also kept on the GPU as a
+mirror indexed by slot, updated from a journal of the allocator's edits, so a
+step sends only its slot ids and positions to the device. Attention and the
+KV append are sm_100a kernels; there is no CPU path: a cache on a CPU device
+supports the allocator only, and its contexts raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Iterator, Mapping, MutableMapping, Sequence
+
+import numpy as np
+import torch
+
+from . import ops
+from ._lib import (PKV_ERR_DOUBLE_FREE, PKV_ERR_NO_BLOCKS, PKV_ERR_OUT_OF_RANGE, PKV_ERR_UNKNOWN_SLOT, PkvError,
+                   check, lib)
+
+
+class NativeBlockManager:
+    """Thin owner of a ``pkv_block_manager`` (engine/kv_cache.py:411-560 in C++)."""
+
+    def __init__(self, num_blocks: int, block_size: int, max_seqs: int, max_len: int,
+                 enable_prefix_caching: bool = False) -> None:
+        h = ctypes.c_void_p()
+        check(lib.pkv_bm_create(num_blocks, block_size, max_seqs, max_len, int(enable_prefix_caching),
+                                ctypes.byref(h)), "block manager")
+        self._h = h
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self.max_seqs = max_seqs
+        self.max_len = max_len
+        self._i32 = ctypes.c_int32()
+        self._i64 = ctypes.c_int64()
+
+    def __del__(self) -> None:
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            lib.pkv_bm_destroy(h)
+            self._h = None
+
+    @staticmethod
+    def _ids(token_ids: Sequence[int] | None) -> tuple[np.ndarray | None, int]:
+        if token_ids is None:
+            return None, 0
+        arr = np.ascontiguousarray(np.asarray(token_ids, dtype=np.int64).reshape(-1))
+        return arr, arr.size
+
+    # ------------------------------------------------------------ allocator
+    def can_allocate(self, num_tokens: int) -> bool:
+        check(lib.pkv_bm_can_allocate(self._h, num_tokens, ctypes.byref(self._i32)), "can_allocate")
+        return bool(self._i32.value)
+
+    def allocate(self, num_tokens: int = 0, token_ids: Sequence[int] | None = None) -> int:
+        arr, n = self._ids(token_ids)
+        st = lib.pkv_bm_allocate(self._h, num_tokens, arr.ctypes.data if arr is not None and n else None, n,
+                                 ctypes.byref(self._i32))
+        if st == PKV_ERR_NO_BLOCKS:
+            raise RuntimeError("not enough free KV cache blocks")
+        check(st, "allocate")
+        return self._i32.value
+
+    def register_prefix(self, slot: int, token_ids: Sequence[int]) -> None:
+        arr, n = self._ids(token_ids)
+        st = lib.pkv_bm_register_prefix(self._h, slot, arr.ctypes.data if n else None, n)
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError(slot)
+        if st == PKV_ERR_OUT_OF_RANGE:
+            raise IndexError("list index out of range")
+        check(st, "register_prefix")
+
+    def ensure_capacity(self, slot: int, num_tokens: int) -> bool:
+        st = lib.pkv_bm_ensure_capacity(self._h, slot, num_tokens, ctypes.byref(self._i32))
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError(slot)
+        check(st, "ensure_capacity")
+        return bool(self._i32.value)
+
+    def free(self, slot: int) -> None:
+        st = lib.pkv_bm_free(self._h, slot)
+        if st == PKV_ERR_DOUBLE_FREE:
+            raise RuntimeError(f"slot {slot} freed twice")
+        check(st, "free")
+
+    # ------------------------------------------------------------ state
+    def get_length(self, slot: int) -> int:
+        st = lib.pkv_bm_get_length(self._h, slot, ctypes.byref(self._i64))
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError(slot)
+        check(st, "lengths")
+        return self._i64.value
+
+    def set_length(self, slot: int, value: int) -> None:
+        st = lib.pkv_bm_set_length(self._h, slot, int(value))
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError(slot)
+        check(st, "lengths")
+
+    def table(self, slot: int) -> list[int]:
+        cap = self.blocks_for(self.max_len) + 2
+        buf = (ctypes.c_int32 * cap)()
+        st = lib.pkv_bm_get_table(self._h, slot, buf, cap, ctypes.byref(self._i32))
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError(slot)
+        check(st, "block_tables")
+        n = self._i32.value
+        if n > cap:
+            buf = (ctypes.c_int32 * n)()
+            check(lib.pkv_bm_get_table(self._h, slot, buf, n, ctypes.byref(self._i32)), "block_tables")
+        return list(buf[:n])
+
+    def live_slots(self) -> list[int]:
+        buf = (ctypes.c_int32 * max(self.max_seqs, 1))()
+        check(lib.pkv_bm_live_slots(self._h, buf, self.max_seqs, ctypes.byref(self._i32)), "live slots")
+        return list(buf[: self._i32.value])
+
+    def decode_positions(self, slots: np.ndarray) -> np.ndarray:
+        out = np.empty(len(slots), np.int32)
+        st = lib.pkv_bm_decode_positions(self._h, slots.ctypes.data, len(slots), out.ctypes.data)
+        if st == PKV_ERR_OUT_OF_RANGE:
+            raise ValueError("a sequence has no block for its next token (call ensure_capacity first)")
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError("slot without a block table")
+        check(st, "decode positions")
+        return out
+
+    def commit_decode(self, slots: np.ndarray) -> None:
+        check(lib.pkv_bm_commit_decode(self._h, slots.ctypes.data, len(slots)), "commit")
+
+    @property
+    def num_free_blocks(self) -> int:
+        check(lib.pkv_bm_num_free_blocks(self._h, ctypes.byref(self._i32)), "num_free_blocks")
+        return self._i32.value
+
+    @property
+    def num_free_slots(self) -> int:
+        check(lib.pkv_bm_num_free_slots(self._h, ctypes.byref(self._i32)), "num_free_slots")
+        return self._i32.value
+
+    @property
+    def prefix_hit_tokens(self) -> int:
+        check(lib.pkv_bm_prefix_hit_tokens(self._h, ctypes.byref(self._i64)), "prefix_hit_tokens")
+        return self._i64.value
+
+    def free_block_order(self) -> list[int]:
+        buf = (ctypes.c_int32 * max(self.num_blocks, 1))()
+        check(lib.pkv_bm_free_order(self._h, buf, self.num_blocks, ctypes.byref(self._i32)), "free order")
+        return list(buf[: self._i32.value])
+
+    def ref_counts(self) -> list[int]:
+        buf = (ctypes.c_int32 * max(self.num_blocks, 1))()
+        check(lib.pkv_bm_ref_counts(self._h, buf, self.num_blocks), "ref counts")
+        return list(buf[: self.num_blocks])
+
+    def cached_blocks(self) -> list[int]:
+        buf = (ctypes.c_int32 * max(self.num_blocks, 1))()
+        check(lib.pkv_bm_cached_blocks(self._h, buf, self.num_blocks, ctypes.byref(self._i32)), "cached blocks")
+        return list(buf[: self._i32.value])
+
+    def blocks_for(self, num_tokens: int) -> int:
+        return -(-num_tokens // self.block_size)
+
+    def set_journal(self, on: bool) -> None:
+        check(lib.pkv_bm_set_journal(self._h, int(on)), "journal")
+
+    def drain_edits(self, buf: np.ndarray) -> tuple[int, bool]:
+        """Copy pending (slot, column, block) edits into ``buf`` ([cap, 3] int32); returns (count, overflowed)."""
+        ovf = ctypes.c_int32()
+        check(lib.pkv_bm_drain_table_edits(self._h, buf.ctypes.data, buf.shape[0], ctypes.byref(self._i32),
+                                           ctypes.byref(ovf)), "drain table edits")
+        return self._i32.value, bool(ovf.value)
+
+    def state(self) -> dict:
+        """Everything a caller can observe, in the same form as the oracle's ``state()``."""
+        slots = self.live_slots()
+        return {
+            "block_tables": {str(s): self.table(s) for s in slots},
+            "lengths": {str(s): self.get_length(s) for s in slots},
+            "free_blocks": self.free_block_order(),
+            "num_free_slots": self.num_free_slots,
+            "prefix_hit_tokens": self.prefix_hit_tokens,
+            "ref_counts": self.ref_counts(),
+            "cached_blocks": self.cached_blocks(),
+        }
+
+
+class _LengthsView(MutableMapping):
+    """``cache.lengths``: slot -> tokens stored, read and written through to the native manager."""
+
+    def __init__(self, bm: NativeBlockManager) -> None:
+        self._bm = bm
+
+    def __getitem__(self, slot: int) -> int:
+        return self._bm.get_length(slot)
+
+    def __setitem__(self, slot: int, value: int) -> None:
+        self._bm.set_length(slot, value)
+
+    def __delitem__(self, slot: int) -> None:
+        raise TypeError("lengths entries are removed by free()")
+
+    def __iter__(self) -> Iterator[int]:
+        return iter(self._bm.live_slots())
+
+    def __len__(self) -> int:
+        return len(self._bm.live_slots())
+
+    def __contains__(self, slot: object) -> bool:
+        return isinstance(slot, int) and slot in self._bm.live_slots()
+
+
+class _TablesView(Mapping):
+    """``cache.block_tables``: slot -> list of block ids (a fresh list per access)."""
+
+    def __init__(self, bm: NativeBlockManager) -> None:
+        self._bm = bm
+
+    def __getitem__(self, slot: int) -> list[int]:
+        return self._bm.table(slot)
+
+    def __iter__(self) -> Iterator[int]:
+        return iter(self._bm.live_slots())
+
+    def __len__(self) -> int:
+        return len(self._bm.live_slots())
+
+    def __contains__(self, slot: object) -> bool:
+        return isinstance(slot, int) and slot in self._bm.live_slots()
+
+
+class PagedKVCache:
+    """A KV cache of fixed-size blocks, the reference's ``PagedKVCache`` on libpkv.
+
+    Memory layout is the reference's: ``k, v: [num_layers, num_blocks + 1,
+    num_kv_heads, block_size, head_dim]``, block ``num_blocks`` being the scratch
+    block that CUDA-graph padding rows write to.
+    """
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, num_blocks: int, block_size: int,
+                 max_seqs: int, max_len: int, dtype: torch.dtype, device: torch.device | str,
+                 enable_prefix_caching: bool = False) -> None:
+        shape = (num_layers, num_blocks + 1, num_kv_heads, block_size, head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=device)
+        self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.num_layers = num_layers
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.num_blocks = num_blocks
+        self.scratch_block = num_blocks
+        self.block_size = block_size
+        self.max_seqs = max_seqs
+        self.max_len = max_len
+        self.enable_prefix_caching = enable_prefix_caching
+        self._bm = NativeBlockManager(num_blocks, block_size, max_seqs, max_len, enable_prefix_caching)
+        self.lengths = _LengthsView(self._bm)
+        self.block_tables = _TablesView(self._bm)
+        self.device = self.k.device
+        self.on_gpu = self.k.is_cuda
+        if self.on_gpu:
+            self.max_blocks_per_seq = max(1, self._bm.blocks_for(max_len))
+            # Device mirror of the block tables, one row per slot, plus the status word
+            # the kernels write index errors to.
+            self.tables_dev = torch.full((max_seqs, self.max_blocks_per_seq), -1, dtype=torch.int32,
+                                         device=self.device)
+            self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.pool = ops.make_pool(self.k, self.v)
+            self._edits = np.zeros((max(1024, 2 * num_blocks), 3), np.int32)
+            self._bm.set_journal(True)
+            self._workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+    @classmethod
+    def for_model(cls, cfg, num_blocks: int, block_size: int, max_seqs: int, max_len: int, dtype: torch.dtype,
+                  device: torch.device | str, enable_prefix_caching: bool = False) -> "PagedKVCache":
+        return cls(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, num_blocks, block_size, max_seqs, max_len,
+                   dtype, device, enable_prefix_caching)
+
+    # ------------------------------------------------------------ allocator API (engine/kv_cache.py:455-560)
+    @property
+    def num_free_slots(self) -> int:
+        return self._bm.num_free_slots
+
+    @property
+    def num_free_blocks(self) -> int:
+        return self._bm.num_free_blocks
+
+    @property
+    def prefix_hit_tokens(self) -> int:
+        return self._bm.prefix_hit_tokens
+
+    def blocks_for(self, num_tokens: int) -> int:
+        return -(-num_tokens // self.block_size)
+
+    def can_allocate(self, num_tokens: int) -> bool:
+        return self._bm.can_allocate(num_tokens)
+
+    def allocate(self, num_tokens: int = 0, token_ids: Sequence[int] | None = None) -> int:
+        return self._bm.allocate(num_tokens, token_ids)
+
+    def register_prefix(self, slot: int, token_ids: Sequence[int]) -> None:
+        self._bm.register_prefix(slot, token_ids)
+
+    def ensure_capacity(self, slot: int, num_tokens: int) -> bool:
+        return self._bm.ensure_capacity(slot, num_tokens)
+
+    def free(self, slot: int) -> None:
+        self._bm.free(slot)
+
+    def write_index(self, slots: Sequence[int], starts: Sequence[int], counts: Sequence[int]
+                    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """Where tokens ``start..start+count-1`` of each sequence live: ``(block, offset)`` (engine/kv_cache.py:562-573)."""
+        bs = self.block_size
+        blocks, offsets = [], []
+        for slot, a, n in zip(slots, starts, counts):
+            table = self._bm.table(slot)
+            pos = range(a, a + n)
+            blocks.extend(table[p // bs] for p in pos)
+            offsets.extend(p % bs for p in pos)
+        return (torch.tensor(blocks, dtype=torch.int64, device=self.device),
+                torch.tensor(offsets, dtype=torch.int64, device=self.device))
+
+    # ------------------------------------------------------------ device mirror
+    def sync_tables(self) -> None:
+        """Push the allocator's table edits since the last sync to the device mirror."""
+        if not self.on_gpu:
+            return
+        n, overflow = self._bm.drain_edits(self._edits)
+        if overflow:
+            self._rebuild_mirror()
+            return
+        if n:
+            upd = torch.from_numpy(self._edits[:n].copy()).pin_memory().to(self.device, non_blocking=True)
+            ops.update_tables(self.tables_dev, upd, self.status)
+
+    def _rebuild_mirror(self) -> None:
+        rows = torch.full((self.max_seqs, self.max_blocks_per_seq), -1, dtype=torch.int32)
+        for s in self._bm.live_slots():
+            t = self._bm.table(s)
+            rows[s, : len(t)] = torch.tensor(t, dtype=torch.int32)
+        self.tables_dev.copy_(rows.pin_memory(), non_blocking=True)
+
+    def workspace(self, batch: int, num_q_heads: int) -> torch.Tensor:
+        """Split-K workspace for decode batches up to ``batch`` rows (zeroed once, reused)."""
+        key = (batch, num_q_heads)
+        ws = self._workspaces.get(key)
+        if ws is None:
+            nbytes = ops.decode_workspace_bytes(batch, self.num_kv_heads, self.max_blocks_per_seq, self.block_size,
+                                                self.head_dim, num_q_heads)
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+            self._workspaces[key] = ws
+        return ws
+
+    def raise_device_errors(self) -> None:
+        """Synchronise and raise any index error a kernel recorded for this cache."""
+        if self.on_gpu:
+            ops.raise_device_errors(self.status)
+
+    # ------------------------------------------------------------ contexts
+    def _require_gpu(self) -> None:
+        if not self.on_gpu:
+            raise RuntimeError("PagedKVCache attention runs on the sm_100a kernels only: put the cache on a CUDA device")
+
+    def packed_prefill_context(self, slots: Sequence[int], lengths: Sequence[int]) -> "PackedPrefillContext":
+        return PackedPrefillContext(self, slots, lengths)
+
+    def decode_context(self, slots: Sequence[int]) -> "PagedDecodeContext":
+        return PagedDecodeContext(self, slots)
+
+
+class PagedDecodeContext:
+    """A batched decode step on the paged cache (engine/kv_cache.py:582-624).
+
+    ``positions`` (int64 [B], on the device) is where each new token goes and
+    what RoPE uses. ``attend`` runs the fused append + split-K paged attention
+    kernel; nothing is gathered or padded.
+    """
+
+    def __init__(self, cache: PagedKVCache, slots: Sequence[int]) -> None:
+        cache._require_gpu()
+        self.cache = cache
+        self.slots = list(slots)
+        self._slots_np = np.asarray(self.slots, dtype=np.int32)
+        pos = cache._bm.decode_positions(self._slots_np)  # raises the reference's ValueError
+        cache.sync_tables()
+        batch = len(self.slots)
+        dev = cache.device
+        staged = torch.from_numpy(np.stack([self._slots_np, pos])).pin_memory().to(dev, non_blocking=True)
+        self.seq_rows = staged[0]
+        self.lengths_in = staged[1]
+        self.positions = torch.empty(batch, dtype=torch.int64, device=dev)
+        self.slot_mapping = torch.empty(batch, dtype=torch.int64, device=dev)
+        self.context_lens = torch.empty(batch, dtype=torch.int32, device=dev)
+        self.tables = ops.make_tables(cache.tables_dev, self.seq_rows)
+        ops.build_decode_metadata(self.tables, self.lengths_in, cache.block_size, cache.scratch_block,
+                                  self.positions, self.slot_mapping, self.context_lens, cache.status)
+
+    @property
+    def write_blocks(self) -> torch.Tensor:
+        return self.slot_mapping // self.cache.block_size
+
+    @property
+    def write_offsets(self) -> torch.Tensor:
+        return self.slot_mapping % self.cache.block_size
+
+    def attend(self, layer_idx: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        """q ``[B, Hq, 1, d]``, k / v ``[B, Hkv, 1, d]`` -> ``[B, Hq, 1, d]``."""
+        batch, hq, _, d = q.shape
+        if q.dtype != self.cache.k.dtype:
+            raise TypeError(f"q is {q.dtype} but the cache holds {self.cache.k.dtype}")
+        ws = self.cache.workspace(self.cache.max_seqs, hq)
+        out = torch.empty(batch, 1, hq, d, dtype=q.dtype, device=q.device)
+        ops.decode_attention(self.cache.pool, layer_idx, self.tables, q[:, :, 0], self.context_lens, ws,
+                             k_new=k[:, :, 0], v_new=v[:, :, 0], slot_mapping=self.slot_mapping,
+                             out=out[:, 0], status=self.cache.status)
+        return out.transpose(1, 2)
+
+    def commit(self) -> None:
+        self.cache._bm.commit_decode(self._slots_np)
+
+
+class PackedPrefillContext:
+    """Prefill of several prompts packed end to end, prefix hits included (engine/kv_cache.py:218-301).
+
+    Each new token's K/V is appended through a slot_mapping built on the GPU,
+    then the varlen paged attention kernel reads each sequence's keys
+    ``0..position`` in place.
+    """
+
+    def __init__(self, cache: PagedKVCache, slots: Sequence[int], lengths: Sequence[int]) -> None:
+        cache._require_gpu()
+        self.cache = cache
+        self.slots = list(slots)
+        self.lengths = list(lengths)
+        self.starts = [cache.lengths[s] for s in self.slots]
+        for s, start, n in zip(self.slots, self.starts, self.lengths):
+            if not cache.ensure_capacity(s, start + n):
+                raise ValueError(f"no room in the KV cache for {start + n} tokens")
+        cache.sync_tables()
+        dev = cache.device
+        cu = np.zeros(len(self.slots) + 1, np.int32)
+        np.cumsum(self.lengths, out=cu[1:])
+        self.total = int(cu[-1])
+        self.max_new = max(self.lengths) if self.lengths else 0
+        host = np.concatenate([np.asarray(self.slots, np.int32), np.asarray(self.starts, np.int32), cu])
+        staged = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)
+        b = len(self.slots)
+        self.seq_rows, self.starts_dev, self.cu_seqlens = staged[:b], staged[b:2 * b], staged[2 * b:]
+        self.tables = ops.make_tables(cache.tables_dev, self.seq_rows)
+        self.positions = torch.empty(self.total, dtype=torch.int64, device=dev)
+        self.slot_mapping = torch.empty(self.total, dtype=torch.int64, device=dev)
+        ops.build_prefill_metadata(self.tables, self.cu_seqlens, self.starts_dev, cache.block_size, self.total,
+                                   self.positions, self.slot_mapping, cache.status)
+        self.has_prefix = any(self.starts)
+        self.last_index = self.cu_seqlens[1:].to(torch.int64) - 1
+
+    def attend(self, layer_idx: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        """q ``[1, Hq, N, d]``, k / v ``[1, Hkv, N, d]`` -> ``[1, Hq, N, d]``."""
+        _, hq, n, d = q.shape
+        if q.dtype != self.cache.k.dtype:
+            raise TypeError(f"q is {q.dtype} but the cache holds {self.cache.k.dtype}")
+        ops.kv_append(self.cache.pool, layer_idx, k[0].transpose(0, 1), v[0].transpose(0, 1), self.slot_mapping,
+                      self.cache.status)
+        out = torch.empty(n, hq, d, dtype=q.dtype, device=q.device)
+        ops.prefill_attention(self.cache.pool, layer_idx, self.tables, q[0].transpose(0, 1), self.cu_seqlens,
+                              self.starts_dev, self.max_new, out=out, status=self.cache.status)
+        return out.unsqueeze(0).transpose(1, 2)
+
+    def commit(self) -> None:
+        for slot, start, n in zip(self.slots, self.starts, self.lengths):
+            self.cache.lengths[slot] = start + n

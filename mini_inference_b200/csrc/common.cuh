@@ -1,0 +1,179 @@
+// Shared device helpers for the sm_100a paged-KV kernels: dtype traits, inline
+// PTX wrappers (mbarrier, bulk tensor copies, ldmatrix, mma.sync, ex2), the
+// device status word, and host-side error plumbing.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/pkv.h"
+
+namespace pkv {
+
+// ---------------------------------------------------------------- host-side error plumbing
+void set_last_cuda_error(cudaError_t e);
+int cuda_status(cudaError_t e);  // PKV_OK or PKV_ERR_CUDA (and records the message)
+
+inline int launch_status() { return cuda_status(cudaGetLastError()); }
+
+// ---------------------------------------------------------------- dtype traits
+template <typename T> struct Dt;
+template <> struct Dt<__half> {
+  static constexpr int code = PKV_F16;
+  __device__ static inline uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ static inline float to_f(__half x) { return __half2float(x); }
+  __device__ static inline __half from_f(float x) { return __float2half_rn(x); }
+};
+template <> struct Dt<__nv_bfloat16> {
+  static constexpr int code = PKV_BF16;
+  __device__ static inline uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ static inline float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  __device__ static inline __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+// ---------------------------------------------------------------- device status word
+// The first error wins; later ones are dropped. Kernels never trap: a bad index is
+// recorded here, the access is skipped or clamped, and the host raises.
+__device__ inline void report(int32_t* status, int32_t code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ inline uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ inline void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ inline void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after `limit` polls (each poll may suspend the thread for a
+// hardware-chosen interval) and returns false; the caller records PKV_ERR_TIMEOUT.
+__device__ inline bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 22)) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
+// 5-D bulk tensor copy global -> shared (no multicast), completion on an mbarrier.
+__device__ inline void tma_load_5d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                   int c4, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
+// Same copy with the default L2 policy.
+__device__ inline void tma_load_5d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                   int c4, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ inline uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ inline void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ inline void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ inline void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <typename T>
+__device__ inline void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+
+template <>
+__device__ inline void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <>
+__device__ inline void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 2^x with the hardware's approximate exponential unit (PTX ex2.approx.ftz.f32).
+__device__ inline float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Byte offset of element `col` (16-bit elements) of row `row` inside a tile whose
+// rows are 128 bytes, stored with the TMA 128-byte swizzle: 16-byte unit u of row r
+// lands at unit u ^ (r % 8). Tiles are 1024-byte aligned.
+__device__ inline uint32_t swz128(uint32_t row, uint32_t col) {
+  const uint32_t unit = (col >> 3) ^ (row & 7);
+  return row * 128 + unit * 16 + (col & 7) * 2;
+}
+
+// ---------------------------------------------------------------- host: tensor maps
+// 5-D tensor map over a [L, NBt, Hkv, bs, D] pool, viewed as {64, bs, D/64, Hkv, L*NBt}
+// (innermost first) with a box of {64, bs, D/64, 1, 1}: one (layer, block, head) tile per
+// copy, 128-byte swizzle. In shared memory the tile is [D/64][bs][64]: element (token t,
+// dim d) sits in 128-byte row (d / 64) * bs + t at column d % 64, so the 8 consecutive keys
+// an ldmatrix reads are 8 distinct swizzle rows (no bank conflicts for D = 64 or 128).
+int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool);
+
+}  // namespace pkv

@@ -1,0 +1,183 @@
+"""Tensor-level wrappers of the C ABI: torch tensors in, kernel launches on the current stream.
+
+Every function here launches sm_100a kernels from ``libpkv.so`` and nothing
+else: there is no PyTorch or CPU fallback. Inputs are validated on the host
+(shape, dtype, device, last-dim contiguity); index errors found on the device
+are written to the caller's status word (see :func:`raise_device_errors`).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from ._lib import PKV_BF16, PKV_F16, PkvPool, PkvTables, check, lib
+
+_DTYPES = {torch.float16: PKV_F16, torch.bfloat16: PKV_BF16}
+
+
+def pkv_dtype(dtype: torch.dtype) -> int:
+    if dtype not in _DTYPES:
+        raise NotImplementedError(f"the sm_100a kernels take float16 or bfloat16 KV caches, not {dtype}")
+    return _DTYPES[dtype]
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("the paged-KV kernels need CUDA tensors (there is no CPU path)")
+
+
+def _rows_last_contiguous(t: torch.Tensor) -> torch.Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def make_pool(k: torch.Tensor, v: torch.Tensor) -> PkvPool:
+    """Describe a ``[layers, blocks + 1, kv_heads, block_size, head_dim]`` K/V pair for the C ABI."""
+    if k.shape != v.shape or k.dtype != v.dtype or k.dim() != 5:
+        raise ValueError("k and v pools must have the same 5-D shape and dtype")
+    if not (k.is_contiguous() and v.is_contiguous()):
+        raise ValueError("the KV pools must be contiguous")
+    layers, nbt, hkv, bs, d = k.shape
+    return PkvPool(k.data_ptr(), v.data_ptr(), layers, nbt, hkv, bs, d, pkv_dtype(k.dtype))
+
+
+def make_tables(block_tables: torch.Tensor, seq_rows: torch.Tensor | None = None) -> PkvTables:
+    """Describe an int32 ``[rows, cols]`` block-table tensor (and optional per-batch row index)."""
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise ValueError("block tables must be a row-major int32 [rows, cols] tensor")
+    if seq_rows is not None and (seq_rows.dtype != torch.int32 or not seq_rows.is_contiguous()):
+        raise ValueError("seq_rows must be a contiguous int32 tensor")
+    rows, cols = block_tables.shape
+    return PkvTables(block_tables.data_ptr(), block_tables.stride(0), rows, cols, _ptr(seq_rows))
+
+
+def kv_append(pool: PkvPool, layer: int, k_rows: torch.Tensor, v_rows: torch.Tensor, slot_mapping: torch.Tensor,
+              status: torch.Tensor | None = None) -> None:
+    """Write rows ``[N, kv_heads, head_dim]`` (any token/head strides) to ``slot_mapping`` (int64 [N])."""
+    _require_cuda(k_rows, v_rows, slot_mapping)
+    if k_rows.shape != v_rows.shape or k_rows.stride() != v_rows.stride():
+        raise ValueError("k and v rows must have the same shape and strides")
+    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be a contiguous int64 tensor")
+    if k_rows.stride(-1) != 1:
+        k_rows, v_rows = k_rows.contiguous(), v_rows.contiguous()
+    n = k_rows.shape[0]
+    check(lib.pkv_kv_append(ctypes.byref(pool), layer, k_rows.data_ptr(), v_rows.data_ptr(), n, k_rows.stride(0),
+                            k_rows.stride(1), slot_mapping.data_ptr(), _ptr(status), _stream()), "kv_append")
+
+
+def decode_workspace_bytes(batch: int, num_kv_heads: int, max_blocks: int, block_size: int, head_dim: int,
+                           num_q_heads: int) -> int:
+    return int(lib.pkv_decode_workspace_bytes(batch, num_kv_heads, max_blocks, block_size, head_dim, num_q_heads))
+
+
+def decode_attention(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tensor, context_lens: torch.Tensor,
+                     workspace: torch.Tensor | None, k_new: torch.Tensor | None = None,
+                     v_new: torch.Tensor | None = None, slot_mapping: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None, scale: float | None = None,
+                     status: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step on one layer: q ``[B, Hq, d]`` (any row/head strides), optional fused append.
+
+    Returns ``out`` of shape ``[B, Hq, d]``. ``context_lens`` (int32 [B]) counts the keys
+    each row attends to, its new token included.
+    """
+    _require_cuda(q, context_lens, k_new, v_new, slot_mapping)
+    batch, hq, d = q.shape
+    q = _rows_last_contiguous(q)
+    if k_new is not None:
+        k_new, v_new = _rows_last_contiguous(k_new), _rows_last_contiguous(v_new)
+        if k_new.stride() != v_new.stride():
+            v_new = v_new.contiguous()
+            k_new = k_new.contiguous()
+    if out is None:
+        out = torch.empty(batch, hq, d, dtype=q.dtype, device=q.device)
+    ws_ptr, ws_bytes = (workspace.data_ptr(), workspace.numel() * workspace.element_size()) if workspace is not None \
+        else (None, 0)
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    check(lib.pkv_decode_attention(
+        ctypes.byref(pool), layer, ctypes.byref(tables), batch, hq, out.data_ptr(), out.stride(0), out.stride(1),
+        q.data_ptr(), q.stride(0), q.stride(1), _ptr(k_new), _ptr(v_new),
+        k_new.stride(0) if k_new is not None else 0, k_new.stride(1) if k_new is not None else 0,
+        _ptr(slot_mapping), context_lens.data_ptr(), scale, ws_ptr, ws_bytes, _ptr(status), _stream()),
+        "decode_attention")
+    return out
+
+
+def prefill_attention(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tensor, cu_seqlens: torch.Tensor,
+                      starts: torch.Tensor, max_new_tokens: int, out: torch.Tensor | None = None,
+                      scale: float | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed prefill on one layer: q ``[N, Hq, d]``; keys come from the pool (append first)."""
+    _require_cuda(q, cu_seqlens, starts)
+    n, hq, d = q.shape
+    q = _rows_last_contiguous(q)
+    if out is None:
+        out = torch.empty(n, hq, d, dtype=q.dtype, device=q.device)
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    check(lib.pkv_prefill_attention(
+        ctypes.byref(pool), layer, ctypes.byref(tables), cu_seqlens.numel() - 1, cu_seqlens.data_ptr(),
+        starts.data_ptr(), max_new_tokens, hq, out.data_ptr(), out.stride(0), out.stride(1), q.data_ptr(),
+        q.stride(0), q.stride(1), scale, _ptr(status), _stream()), "prefill_attention")
+    return out
+
+
+def build_decode_metadata(tables: PkvTables, lengths: torch.Tensor, block_size: int, scratch_block: int,
+                          positions: torch.Tensor, slot_mapping: torch.Tensor, context_lens: torch.Tensor,
+                          status: torch.Tensor | None = None) -> None:
+    """positions / slot_mapping / context_lens of a decode step from the device table mirror."""
+    batch = lengths.numel()
+    check(lib.pkv_build_decode_metadata(ctypes.byref(tables), batch, lengths.data_ptr(), block_size, scratch_block,
+                                        positions.data_ptr(), slot_mapping.data_ptr(), context_lens.data_ptr(),
+                                        _ptr(status), _stream()), "build_decode_metadata")
+
+
+def build_prefill_metadata(tables: PkvTables, cu_seqlens: torch.Tensor, starts: torch.Tensor, block_size: int,
+                           total_tokens: int, positions: torch.Tensor, slot_mapping: torch.Tensor,
+                           status: torch.Tensor | None = None) -> None:
+    check(lib.pkv_build_prefill_metadata(ctypes.byref(tables), cu_seqlens.numel() - 1, cu_seqlens.data_ptr(),
+                                         starts.data_ptr(), block_size, total_tokens, positions.data_ptr(),
+                                         slot_mapping.data_ptr(), _ptr(status), _stream()), "build_prefill_metadata")
+
+
+def update_tables(block_tables: torch.Tensor, updates: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """Apply int32 ``[n, 3]`` (row, column, block) edits to a device table mirror."""
+    rows, cols = block_tables.shape
+    check(lib.pkv_update_tables(block_tables.data_ptr(), block_tables.stride(0), rows, cols, updates.data_ptr(),
+                                updates.shape[0], _ptr(status), _stream()), "update_tables")
+
+
+def commit_decode(seq_rows: torch.Tensor, lengths: torch.Tensor) -> None:
+    check(lib.pkv_commit_decode(seq_rows.data_ptr(), seq_rows.numel(), lengths.data_ptr(), _stream()),
+          "commit_decode")
+
+
+def copy_blocks(pool: PkvPool, src: torch.Tensor, dst: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """Copy whole blocks ``src[i] -> dst[i]`` (int32 device tensors) in every layer, K and V."""
+    _require_cuda(src, dst)
+    check(lib.pkv_copy_blocks(ctypes.byref(pool), src.data_ptr(), dst.data_ptr(), src.numel(), _ptr(status),
+                              _stream()), "copy_blocks")
+
+
+_STATUS_ERRORS = {
+    2: (IndexError, "a block id, slot or position on the device was outside the pool or its table"),
+    9: (RuntimeError, "a device-side wait timed out"),
+}
+
+
+def raise_device_errors(status: torch.Tensor) -> None:
+    """Read a device status word (synchronises), raise what a kernel recorded, and clear it."""
+    code = int(status.item())
+    if code:
+        status.zero_()
+        exc, msg = _STATUS_ERRORS.get(code, (RuntimeError, f"device status {code}"))
+        raise exc(msg)

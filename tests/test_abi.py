@@ -1,0 +1,74 @@
+"""The C ABI: the library loads without a GPU and exports exactly what include/pkv.h declares."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "pkv.h"
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^PKV_API\s+[\w\s\*]+?\b(pkv_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for required in ("pkv_kv_append", "pkv_decode_attention", "pkv_prefill_attention", "pkv_build_decode_metadata",
+                     "pkv_build_prefill_metadata", "pkv_copy_blocks", "pkv_bm_allocate", "pkv_bm_free",
+                     "pkv_bm_register_prefix", "pkv_bm_ensure_capacity"):
+        assert required in names
+    assert len(names) >= 30
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from mini_inference_b200 import _lib
+
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in sorted(declared_functions()) if not hasattr(lib, n)]
+    assert not missing, missing
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert exported == declared_functions(), exported ^ declared_functions()
+
+
+def test_python_binding_covers_the_header():
+    from mini_inference_b200 import _lib
+
+    assert set(_lib.SIGNATURES) == declared_functions()
+
+
+def test_host_calls_work_without_a_gpu():
+    from mini_inference_b200 import _lib
+
+    assert _lib.lib.pkv_version() == 0x000100
+    assert _lib.status_name(_lib.PKV_ERR_NO_BLOCKS) == "not enough free KV cache blocks"
+    # Shape validation happens before any CUDA call.
+    assert _lib.lib.pkv_decode_workspace_bytes(64, 2, 129, 16, 64, 14) > 0
+    assert _lib.lib.pkv_decode_workspace_bytes(64, 2, 129, 8, 64, 14) == 0  # block size 8 is not built
+    pool = _lib.PkvPool(None, None, 1, 4, 2, 16, 96, _lib.PKV_F16)
+    tables = _lib.PkvTables(None, 0, 0, 0, None)
+    assert _lib.lib.pkv_decode_attention(ctypes.byref(pool), 0, ctypes.byref(tables), 1, 14, None, 0, 0, None, 0, 0,
+                                         None, None, 0, 0, None, None, 1.0, None, 0, None, None) \
+        == _lib.PKV_ERR_INVALID_ARGUMENT
+
+
+def test_import_fails_loudly_without_the_library(tmp_path, monkeypatch):
+    """Without libpkv.so the package cannot be imported: there is no silent fallback."""
+    import importlib.util
+    import sys
+
+    src = (ROOT / "mini_inference_b200" / "_lib.py").read_text()
+    fake = tmp_path / "_lib.py"
+    fake.write_text(src)
+    spec = importlib.util.spec_from_file_location("pkv_lib_without_so", fake)
+    mod = importlib.util.module_from_spec(spec)
+    with pytest.raises(ImportError, match="not built"):
+        spec.loader.exec_module(mod)
+    sys.modules.pop("pkv_lib_without_so", None)
