@@ -1,0 +1,442 @@
+"""Benchmark of the paged-KV hot path on B200: the paged decode attention micro-benchmark.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+Workload (the configuration the "paged-attn KV GB/s" half of
+the metric is quoted on): 64 sequences with context lengths uniform in
+128..2048, 14 query / 2 KV heads, head_dim 64, blocks of 16 tokens, fp16,
+K/V/Q ~ N(0, 1), block tables = consecutive slices of a seeded permutation of a
+16384-block pool, and a one-token KV append per sequence through slot_mapping
+in the same call. Data are synthetic (seeded), as the reference's benchmark
+has no dataset for this path.
+
+A step is one decode step of that batch through all 24 layers of a
+Qwen2.5-0.5B-shaped pool ([24, 16385, 2, 16, 64] for K and for V, 3.2 GB in all,
+far above the 126 MB L2, so every layer call reads its KV from HBM): the GPU
+metadata builder, then 24 fused append + paged attention calls. ``value`` is
+algorithmic KV-path bytes moved per second over the whole job (all ranks);
+``e2e`` is the same metric through the C ABI with host buffers (the step's
+q / new k / new v and tables copied from pinned host memory, the outputs
+copied back, all inside the timed region).
+
+Multi-GPU: one process per GPU, each with its own batch and pool (weak scaling,
+requests sharded by rank, no collective on the data path); the timed region is
+bracketed by barriers and timed on each device with CUDA events, and the job
+time is the maximum over ranks.
+
+``--impl reference`` times the reference's own algorithm on the host cores:
+``oracle/paged_kv_torch.py``, the reference's PyTorch ops for this step
+restated on the CPU, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s on 200-req mixed workload; paged-attn KV GB/s vs HBM peak"
+UNIT = "GB/s"
+LAYERS, BATCH, CTX_LO, CTX_HI = 24, 64, 128, 2048
+HQ, HKV, D, BS, NUM_BLOCKS = 14, 2, 64, 16, 16384
+ELT = 2  # fp16 bytes
+
+
+def workload(seed: int):
+    """Context lengths and block tables of config 2 (seeded per rank)."""
+    g = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(CTX_LO, CTX_HI + 1, (BATCH,), generator=g).tolist()
+    perm = torch.randperm(NUM_BLOCKS, generator=g).tolist()
+    tables, at = [], 0
+    for c in ctx:
+        n = (c + 1 + BS - 1) // BS  # room for the appended token
+        tables.append(perm[at:at + n])
+        at += n
+    return ctx, tables
+
+
+def bytes_per_layer_call(ctx: list[int]) -> int:
+    """Algorithmic bytes of one fused append + decode attention call over the batch.
+
+    K+V read for ctx+1 keys per sequence and KV head, Q read and O write, the
+    appended K/V rows written, and the int32 block-table entries read.
+    """
+    kv = sum(c + 1 for c in ctx) * HKV * D * ELT * 2
+    qo = len(ctx) * HQ * D * ELT * 2
+    append = len(ctx) * HKV * D * ELT * 2
+    table = sum(math.ceil((c + 1) / BS) for c in ctx) * 4
+    return kv + qo + append + table
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def ncu_traffic_per_launch() -> float | None:
+    """DRAM bytes per decode launch from the committed ncu summary, if one exists."""
+    f = ROOT / "profiles" / "decode_attention_config2.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi samples (every 100 ms) of SM clock and throttle reasons while the GPU works."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.file.flush()
+        rows = [r.split(", ") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        rows = [r for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    """Job time = the slowest rank's device time (a host-side reduction, outside any timed region)."""
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------------------- our arm
+
+
+def run_ours(args, rank: int, world: int, local: int) -> dict | None:
+    from mini_inference_b200 import ops
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ctx, tables = workload(seed=rank)
+    call_bytes = bytes_per_layer_call(ctx)
+    step_bytes = call_bytes * LAYERS
+    cols = max(len(t) for t in tables)
+
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    shape = (LAYERS, NUM_BLOCKS + 1, HKV, BS, D)
+    k_pool = torch.randn(shape, generator=g, device=dev, dtype=torch.float16)
+    v_pool = torch.randn(shape, generator=g, device=dev, dtype=torch.float16)
+    q = torch.randn(LAYERS, BATCH, HQ, D, generator=g, device=dev, dtype=torch.float16)
+    kn = torch.randn(LAYERS, BATCH, HKV, D, generator=g, device=dev, dtype=torch.float16)
+    vn = torch.randn(LAYERS, BATCH, HKV, D, generator=g, device=dev, dtype=torch.float16)
+    out = torch.empty(LAYERS, BATCH, HQ, D, device=dev, dtype=torch.float16)
+
+    # Device table mirror (one row per sequence) + the per-step inputs the builder reads.
+    mirror = torch.full((BATCH, cols), -1, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        mirror[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    mirror = mirror.to(dev)
+    rows = torch.arange(BATCH, dtype=torch.int32, device=dev)
+    lengths = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    positions = torch.empty(BATCH, dtype=torch.int64, device=dev)
+    slot_mapping = torch.empty(BATCH, dtype=torch.int64, device=dev)
+    context_lens = torch.empty(BATCH, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    pool = ops.make_pool(k_pool, v_pool)
+    tabs = ops.make_tables(mirror, rows)
+    ws = torch.zeros(ops.decode_workspace_bytes(BATCH, HKV, cols, BS, D, HQ), dtype=torch.uint8, device=dev)
+
+    def attention_layers():
+        for layer in range(LAYERS):
+            ops.decode_attention(pool, layer, tabs, q[layer], context_lens, ws, k_new=kn[layer], v_new=vn[layer],
+                                 slot_mapping=slot_mapping, out=out[layer], status=status)
+
+    def step():
+        ops.build_decode_metadata(tabs, lengths, BS, NUM_BLOCKS, positions, slot_mapping, context_lens, status)
+        attention_layers()
+
+    # Warm-up eagerly (also validates), then capture one step and the attention-only part.
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    ops.raise_device_errors(status)
+    g_step, g_attn = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        step()
+    with torch.cuda.graph(g_attn):
+        attention_layers()
+    stream = torch.cuda.current_stream()
+
+    def timed(graph, k: int) -> float:
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(k):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return start.elapsed_time(end)
+
+    with ClockSampler(local) as clocks:
+        ms_total = timed(g_step, args.steps)
+        ms_attn = timed(g_attn, args.steps)
+        ms_e2e, h2d, d2h, e2e_launches = run_e2e(args, dev, pool, tables, ctx, q, kn, vn, world)
+    ops.raise_device_errors(status)
+
+    ms_job = max_over_ranks(ms_total, world)
+    ms_attn_job = max_over_ranks(ms_attn, world)
+    ms_e2e_job = max_over_ranks(ms_e2e, world)
+    if rank != 0:
+        return None
+    peaks, peak_kind = measured_peaks()
+    per_launch_ms = ms_attn_job / (args.steps * LAYERS)
+    achieved = call_bytes / (per_launch_ms * 1e-3) / 1e9
+    traffic = ncu_traffic_per_launch()
+    line = {
+        "metric": METRIC, "value": round(world * step_bytes * args.steps / (ms_job * 1e-3) / 1e9, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_job / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded; config 2 shapes and distributions)",
+        "config": {"workload": "config 2: paged decode attention micro-benchmark, fused one-token append",
+                   "batch_per_gpu": BATCH, "context": f"U{{{CTX_LO}..{CTX_HI}}}", "q_heads": HQ, "kv_heads": HKV,
+                   "head_dim": D, "block_size": BS, "pool_blocks": NUM_BLOCKS, "layers_per_step": LAYERS,
+                   "bytes_per_step_per_gpu": step_bytes, "tokens_per_step_per_gpu": BATCH,
+                   "l2": "inputs above L2: 24 layer pools of 134 MB (3.2 GB), each read once per step",
+                   "parallelism": f"replicas x{world} (requests sharded by rank, no collective)"},
+        "decode_steps_per_s": round(world * args.steps / (ms_job * 1e-3), 1),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": f"{peak_kind} copy bandwidth",
+                     "traffic": traffic, "algorithmic_bytes_per_launch": call_bytes,
+                     "kernel": "pkv decode_kernel<half,64> (fused append + split-K paged attention)",
+                     "launch_us": round(per_launch_ms * 1e3, 3)},
+        "e2e": {"value": round(world * step_bytes * args.e2e_steps / (ms_e2e_job * 1e-3) / 1e9, 2), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(ms_e2e_job / args.e2e_steps, 4), "steps": args.e2e_steps,
+                "path": "C ABI (pkv_decode_attention via ctypes) on pinned host buffers"},
+        "gpu_launches": args.steps * (LAYERS + 1) + args.steps * LAYERS + e2e_launches,
+        "clocks": clocks.summary(),
+    }
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(args)
+    return line
+
+
+def run_e2e(args, dev, pool, tables, ctx, q_dev, kn_dev, vn_dev, world):
+    """The same step through the C ABI with host buffers: H2D inputs, 24 calls, D2H outputs."""
+    from mini_inference_b200 import ops
+
+    cols = max(len(t) for t in tables)
+    tab_h = torch.full((BATCH, cols), 0, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        tab_h[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    sm_h = torch.tensor([t[c // BS] * BS + c % BS for t, c in zip(tables, ctx)], dtype=torch.int64)
+    cl_h = torch.tensor([c + 1 for c in ctx], dtype=torch.int32)
+    q_h = q_dev.cpu().pin_memory()
+    kn_h, vn_h = kn_dev.cpu().pin_memory(), vn_dev.cpu().pin_memory()
+    tab_h, sm_h, cl_h = tab_h.pin_memory(), sm_h.pin_memory(), cl_h.pin_memory()
+    out_h = torch.empty(LAYERS, BATCH, HQ, D, dtype=torch.float16).pin_memory()
+    q_d, kn_d, vn_d = torch.empty_like(q_dev), torch.empty_like(kn_dev), torch.empty_like(vn_dev)
+    out_d = torch.empty(LAYERS, BATCH, HQ, D, dtype=torch.float16, device=dev)
+    tab_d = torch.empty_like(tab_h, device=dev)
+    sm_d, cl_d = torch.empty_like(sm_h, device=dev), torch.empty_like(cl_h, device=dev)
+    ws = torch.zeros(ops.decode_workspace_bytes(BATCH, HKV, cols, BS, D, HQ), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    tabs = ops.make_tables(tab_d)
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, kn_h, vn_h, tab_h, sm_h, cl_h))
+    d2h = out_h.numel() * out_h.element_size()
+
+    def step():
+        for src, dst in ((tab_h, tab_d), (sm_h, sm_d), (cl_h, cl_d), (q_h, q_d), (kn_h, kn_d), (vn_h, vn_d)):
+            dst.copy_(src, non_blocking=True)
+        for layer in range(LAYERS):
+            ops.decode_attention(pool, layer, tabs, q_d[layer], cl_d, ws, k_new=kn_d[layer], v_new=vn_d[layer],
+                                 slot_mapping=sm_d, out=out_d[layer], status=status)
+        out_h.copy_(out_d, non_blocking=True)
+        torch.cuda.current_stream().synchronize()  # the caller has its result on the host
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.e2e_steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ops.raise_device_errors(status)
+    return start.elapsed_time(end), h2d, d2h, args.e2e_steps * LAYERS
+
+
+# ---------------------------------------------------------------------------------------- CPU legs
+
+
+def cpu_threads() -> int:
+    return torch.get_num_threads()
+
+
+def cpu_sample_run(steps: int, warmup: int, budget_s: float) -> dict:
+    """Time the reference's algorithm (PyTorch CPU ops) on a bounded sample of the config-2 layer call.
+
+    Each step is one layer call over the first ``n_seq`` sequences of the batch;
+    ``n_seq`` is chosen from a timed full call so that all steps fit ``budget_s``.
+    """
+    from oracle.paged_kv_torch import decode_attend_torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    ctx, tables = workload(seed=0)
+    g = torch.Generator().manual_seed(99)
+    k = torch.randn(NUM_BLOCKS + 1, HKV, BS, D, generator=g).half()
+    v = torch.randn(NUM_BLOCKS + 1, HKV, BS, D, generator=g).half()
+    q = torch.randn(BATCH, HQ, D, generator=g).half()
+    kn = torch.randn(BATCH, HKV, D, generator=g).half()
+    t0 = time.perf_counter()
+    decode_attend_torch(k, v, tables, ctx, q, kn, kn)
+    full = time.perf_counter() - t0
+    per_step_budget = budget_s / max(1, steps + warmup)
+    n_seq = max(1, min(BATCH, int(BATCH * per_step_budget / max(full, 1e-6))))
+    sub_ctx, sub_tab = ctx[:n_seq], tables[:n_seq]
+    for _ in range(warmup):
+        decode_attend_torch(k, v, sub_tab, sub_ctx, q[:n_seq], kn[:n_seq], kn[:n_seq])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        decode_attend_torch(k, v, sub_tab, sub_ctx, q[:n_seq], kn[:n_seq], kn[:n_seq])
+    dt = time.perf_counter() - t0
+    gbs = bytes_per_layer_call(sub_ctx) * steps / dt / 1e9
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": f"{steps} layer calls over the first {n_seq} of the 64 config-2 sequences "
+                      f"(fp16, {sum(sub_ctx)} cached tokens), reference PyTorch ops on the host "
+                      f"(oracle/paged_kv_torch.py); one full 64-sequence call took {full:.3f} s",
+            "seconds": round(dt, 2)}
+
+
+def cpu_baseline(args) -> dict:
+    return cpu_sample_run(steps=max(3, min(args.steps, 40)), warmup=1, budget_s=20.0)
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return  # rank 0 alone times the host-core reference
+    res = cpu_sample_run(args.steps, args.warmup, budget_s=120.0)
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded; config 2 shapes and distributions)", "impl": "reference",
+        "config": {"workload": "config 2: paged decode attention micro-benchmark, fused one-token append",
+                   "batch_per_gpu": BATCH, "context": f"U{{{CTX_LO}..{CTX_HI}}}", "q_heads": HQ, "kv_heads": HKV,
+                   "head_dim": D, "block_size": BS, "pool_blocks": NUM_BLOCKS},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        line = run_ours(args, rank, world, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            barrier(world)
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

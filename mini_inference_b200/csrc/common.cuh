@@ -80,13 +80,22 @@ __device__ inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls (each poll may suspend the thread for a
-// hardware-chosen interval) and returns false; the caller records PKV_ERR_TIMEOUT.
-__device__ inline bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 22)) {
-  for (uint32_t i = 0; i < limit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+__device__ inline uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Every wait in a CTA shares one deadline, so a CTA waits at most this long in total.
+constexpr uint64_t kWaitBudgetNs = 2000ull * 1000 * 1000;  // 2 s
+
+// Bounded wait: polls until the phase completes or the global timer passes `deadline`,
+// then returns false; the caller records PKV_ERR_TIMEOUT and stops waiting.
+__device__ inline bool mbar_wait_until(uint64_t* bar, uint32_t parity, uint64_t deadline) {
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() > deadline) return false;
   }
-  return false;
+  return true;
 }
 
 // 5-D bulk tensor copy global -> shared (no multicast), completion on an mbarrier.

@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(kNW * 32) decode_kernel(const __grid_constant_
   }
   const int32_t* table = row >= 0 ? p.tables + row * p.table_stride : nullptr;
 
+  const uint64_t deadline = global_ns() + kWaitBudgetNs;
   if (tid == 0) {
     for (int i = 0; i < nb; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(kNW * 32) decode_kernel(const __grid_constant_
   bool timed_out = false;
 
   for (int lb = warp; lb < nb; lb += kNW) {
-    if (!mbar_wait_bounded(&bars[lb], 0)) {
+    if (!mbar_wait_until(&bars[lb], 0, deadline)) {
       timed_out = true;
       break;
     }
@@ -197,7 +198,10 @@ __global__ void __launch_bounds__(kNW * 32) decode_kernel(const __grid_constant_
   // path every barrier has already completed and this is nb polls.
   if (tid == 0) {
     for (int i = 0; i < nb; ++i) {
-      if (!mbar_wait_bounded(&bars[i], 0)) report(p.status, PKV_ERR_TIMEOUT);
+      if (!mbar_wait_until(&bars[i], 0, deadline)) {
+        report(p.status, PKV_ERR_TIMEOUT);
+        break;
+      }
     }
   }
 

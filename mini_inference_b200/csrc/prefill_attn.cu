@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(512) prefill_kernel(const __grid_constant__ CU
     tma_load_5d(smem + (kStages + st) * TILE, &tmap_v, 0, 0, 0, head, c4, &full[st]);
   };
 
+  const uint64_t deadline = global_ns() + kWaitBudgetNs;
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
     fence_mbar_init();
@@ -120,7 +121,7 @@ __global__ void __launch_bounds__(512) prefill_kernel(const __grid_constant__ CU
   bool ok = true;
   for (int i = 0; i < nkb; ++i) {
     const int st = i % kStages;
-    if (ok && !mbar_wait_bounded(&full[st], (i / kStages) & 1)) {
+    if (ok && !mbar_wait_until(&full[st], (i / kStages) & 1, deadline)) {
       report(p.status, PKV_ERR_TIMEOUT);
       ok = false;
     }

@@ -169,6 +169,32 @@ def test_prefill_oracle_matches_reference(golden_dir, name):
     assert (np.cumsum(z["lengths"]) - 1).tolist() == z["last_index"].tolist()
 
 
+@pytest.mark.parametrize("name", ["fp32_tiny", "fp16_h14_d64", "bf16_h28_d128", "fp16_h28_d128"])
+def test_torch_cpu_restatement_matches_reference(golden_dir, name):
+    """The timed CPU baseline (oracle/paged_kv_torch.py) reproduces the reference's outputs and writes."""
+    import torch
+
+    from oracle.paged_kv_torch import decode_attend_torch
+
+    z = np.load(golden_dir / f"decode_{name}.npz")
+    dt = str(z["dtype"])
+    layer = int(z["layer"])
+    tdt = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}[dt]
+
+    def t(a):
+        if dt == "bfloat16":
+            return torch.from_numpy(np.ascontiguousarray(a).astype(np.int16)).view(torch.bfloat16)
+        return torch.from_numpy(np.ascontiguousarray(a))
+
+    k_pool, v_pool = t(z["k_before"])[layer].clone(), t(z["v_before"])[layer].clone()
+    out = decode_attend_torch(k_pool, v_pool, _tables(z), z["positions"].tolist(), t(z["q"]), t(z["k_new"]),
+                              t(z["v_new"]))
+    assert torch.equal(out.view(torch.int16) if dt != "float32" else out,
+                       t(z["out"]).view(torch.int16) if dt != "float32" else t(z["out"]))
+    k_ref = _after(to_compute(z["k_before"], dt)[layer], z["k_written_at"], to_compute(z["k_written"], dt))
+    assert np.array_equal(_bits(k_pool.float().numpy(), dt), _bits(k_ref, dt))
+
+
 def test_prefix_fixtures_really_hit_the_cache(golden_dir):
     for name in ("fp16_prefix", "fp32_tiny_prefix", "bf16_prefix_d128"):
         z = np.load(golden_dir / f"prefill_{name}.npz")
