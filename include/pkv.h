@@ -113,6 +113,7 @@ PKV_API int pkv_kv_append(const pkv_pool* pool, int32_t layer, const void* k_new
  *   tables  : see pkv_tables
  *   context_lens[b]: keys row b attends to (its position + 1), 1..tables->cols*block_size
  *   scale   : softmax scale (the reference uses 1/sqrt(head_dim))
+ *   flags   : PKV_DECODE_INPUTS_READY or 0 (see below)
  *   workspace: >= pkv_decode_workspace_bytes(...) bytes, 256-byte aligned, zeroed once
  *             before first use; the kernel leaves it ready for the next call, whatever
  *             the next call's batch or table width. Calls that share a workspace must
@@ -124,7 +125,18 @@ PKV_API int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_
                          const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_new,
                          const void* v_new, int64_t kv_stride_b, int64_t kv_stride_h,
                          const int64_t* slot_mapping, const int32_t* context_lens, float scale,
-                         void* workspace, int64_t workspace_bytes, int32_t* status_dev, pkv_stream_t stream);
+                         int32_t flags, void* workspace, int64_t workspace_bytes, int32_t* status_dev,
+                         pkv_stream_t stream);
+
+/* pkv_decode_attention flags */
+enum {
+  /* context_lens, the block tables / seq_rows and every cached K/V row the call reads were
+   * complete before the previous kernel in the stream began (only q, k_new and v_new may come
+   * from it). The kernel then resolves blocks and starts its first K/V copies before waiting
+   * for that kernel (programmatic dependent launch). E.g. layers after the first of a decode
+   * step whose metadata was built at the start of the step. */
+  PKV_DECODE_INPUTS_READY = 1
+};
 
 /* Workspace bytes pkv_decode_attention needs for these sizes. */
 PKV_API int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,

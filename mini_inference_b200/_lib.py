@@ -27,6 +27,8 @@ PKV_ERR_TIMEOUT = 9
 PKV_F16 = 0
 PKV_BF16 = 1
 
+PKV_DECODE_INPUTS_READY = 1
+
 
 class PkvPool(ctypes.Structure):
     _fields_ = [("k", c_void_p), ("v", c_void_p), ("num_layers", c_int32), ("num_blocks_total", c_int32),
@@ -52,7 +54,7 @@ SIGNATURES: dict[str, tuple] = {
                                 c_void_p]),
     "pkv_decode_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64, c_int64,
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
-                                       c_void_p, c_float, c_void_p, c_int64, c_void_p, c_void_p]),
+                                       c_void_p, c_float, c_int32, c_void_p, c_int64, c_void_p, c_void_p]),
     "pkv_decode_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
     "pkv_prefill_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_void_p, c_void_p, c_int32, c_int32,
                                         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_float, c_void_p,

@@ -414,6 +414,7 @@ class PagedDecodeContext:
         self.tables = ops.make_tables(cache.tables_dev, self.seq_rows)
         ops.build_decode_metadata(self.tables, self.lengths_in, cache.block_size, cache.scratch_block,
                                   self.positions, self.slot_mapping, self.context_lens, cache.status)
+        self._attends = 0
 
     @property
     def write_blocks(self) -> torch.Tensor:
@@ -430,9 +431,13 @@ class PagedDecodeContext:
             raise TypeError(f"q is {q.dtype} but the cache holds {self.cache.k.dtype}")
         ws = self.cache.workspace(self.cache.max_seqs, hq)
         out = torch.empty(batch, 1, hq, d, dtype=q.dtype, device=q.device)
+        # The metadata was built when this context was made; once one attend of this step has
+        # run, it is complete before whatever kernel precedes the next one, so the kernel may
+        # start its block lookups early (PKV_DECODE_INPUTS_READY).
         ops.decode_attention(self.cache.pool, layer_idx, self.tables, q[:, :, 0], self.context_lens, ws,
                              k_new=k[:, :, 0], v_new=v[:, :, 0], slot_mapping=self.slot_mapping,
-                             out=out[:, 0], status=self.cache.status)
+                             out=out[:, 0], status=self.cache.status, inputs_ready=self._attends > 0)
+        self._attends += 1
         return out.transpose(1, 2)
 
     def commit(self) -> None:

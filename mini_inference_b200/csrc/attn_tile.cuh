@@ -85,14 +85,31 @@ __device__ inline void attend_tile16(const uint32_t (&qa)[D / 16][4], uint32_t k
     o[j][2] *= alpha[1];
     o[j][3] *= alpha[1];
   }
-  const uint32_t pa[4] = {Dt<T>::pack(s[0][0], s[0][1]), Dt<T>::pack(s[0][2], s[0][3]),
-                          Dt<T>::pack(s[1][0], s[1][1]), Dt<T>::pack(s[1][2], s[1][3])};
+  // P enters the tensor cores in the storage type. fp16 keeps 11 significant bits of
+  // each weight; bf16 only 8, which alone moves short-context outputs by several bf16
+  // steps, so for bf16 P is split as hi + lo (both bf16, ~16 bits together) and V is
+  // multiplied by both. Decode is memory-bound, so the second pass is free there.
+  constexpr bool kSplitP = !Dt<T>::kExactP;
+  uint32_t pa[4], pl[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int n = i >> 1, e = (i & 1) * 2;
+    pa[i] = Dt<T>::pack(s[n][e], s[n][e + 1]);
+    if (kSplitP) {
+      const float2 hi = Dt<T>::unpack(pa[i]);
+      pl[i] = Dt<T>::pack(s[n][e] - hi.x, s[n][e + 1] - hi.y);
+    }
+  }
 #pragma unroll
   for (int jj = 0; jj < D / 16; ++jj) {
     uint32_t b0, b1, b2, b3;
     ldsm_x4_t(tile_addr<D>(vbase, (lane & 7) + 8 * ((lane >> 3) & 1), 2 * jj + (lane >> 4)), b0, b1, b2, b3);
     mma16816<T>(o[2 * jj], pa, b0, b1);
     mma16816<T>(o[2 * jj + 1], pa, b2, b3);
+    if (kSplitP) {
+      mma16816<T>(o[2 * jj], pl, b0, b1);
+      mma16816<T>(o[2 * jj + 1], pl, b2, b3);
+    }
   }
 }
 

@@ -23,18 +23,26 @@ inline int launch_status() { return cuda_status(cudaGetLastError()); }
 template <typename T> struct Dt;
 template <> struct Dt<__half> {
   static constexpr int code = PKV_F16;
+  static constexpr bool kExactP = true;  // softmax weights in [0, 1] keep 11 bits in fp16
   __device__ static inline uint32_t pack(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ static inline float2 unpack(uint32_t u) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
   }
   __device__ static inline float to_f(__half x) { return __half2float(x); }
   __device__ static inline __half from_f(float x) { return __float2half_rn(x); }
 };
 template <> struct Dt<__nv_bfloat16> {
   static constexpr int code = PKV_BF16;
+  static constexpr bool kExactP = false;  // 8 bits: the tile step splits P into hi + lo
   __device__ static inline uint32_t pack(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ static inline float2 unpack(uint32_t u) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
   }
   __device__ static inline float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
   __device__ static inline __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
@@ -119,11 +127,45 @@ __device__ inline void tma_load_5d(void* smem_dst, const CUtensorMap* map, int c
       : "memory");
 }
 
+// Bulk (non-tensor) copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// global -> shared, completing on an mbarrier (no multicast).
+__device__ inline void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// Orders this thread's generic-proxy accesses of global memory before later async-proxy ones.
+__device__ inline void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// 16-byte asynchronous global -> shared copy through L2 only (no registers held), and the
+// wait for all of this thread's outstanding copies.
+__device__ inline void cp_async_16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ inline void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Acquire-release fence at GPU scope (cheaper than the sequentially consistent __threadfence).
+__device__ inline void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+__device__ inline void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ inline uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+
+// Programmatic dependent launch (sm_90+): let the next grid in the stream start its
+// CTAs now / wait until the previous grid has completed and its writes are visible.
+// Both are no-ops for a launch without the programmatic-serialization attribute.
+__device__ inline void grid_dep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ inline void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ inline void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -183,6 +225,12 @@ __device__ inline uint32_t swz128(uint32_t row, uint32_t col) {
 // copy, 128-byte swizzle. In shared memory the tile is [D/64][bs][64]: element (token t,
 // dim d) sits in 128-byte row (d / 64) * bs + t at column d % 64, so the 8 consecutive keys
 // an ldmatrix reads are 8 distinct swizzle rows (no bank conflicts for D = 64 or 128).
-int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool);
+// heads_per_box > 1 widens the box over that many consecutive KV heads of the block:
+// shared-memory layout [heads][D/64][bs][64], head h's tile at h * bs * D * 2 bytes.
+int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool, int heads_per_box);
+// Cached K and V maps of a pool (one encode per pool and box shape).
+bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box = 1);
+// Streaming multiprocessors of the current device (queried once).
+int num_sms();
 
 }  // namespace pkv

@@ -4,24 +4,38 @@
 // (engine/kv_cache.py:611-620): the index_put append, the gather of every
 // sequence's blocks into a padded contiguous copy, and decode_attention's SDPA
 // (engine/model.py:126-147). Here nothing is gathered: K/V blocks are read in
-// place through the block table, each exactly once.
+// place through the block table, each exactly once, straight into shared memory.
 //
-// Work split (split-K "flash decoding"): one CTA per (chunk of CB blocks,
-// kv head, sequence). A chunk's K and V tiles (one 16 x head_dim tile per block
-// and head) are all requested up front with 5-D TMA bulk tensor copies into
-// 128B-swizzled shared memory, so each CTA keeps CB * 2 tiles in flight. Each
-// warp then takes every NW-th block: S = Q K^T and O += P V on mma.sync
-// m16n8k16 (fp32 accumulate), where the M=16 rows are the GQA group's query
-// heads (the reference regroups head h to (h / group, h % group) the same way),
-// so each K/V tile read from HBM serves the whole group. The softmax is the
-// online (running max / running sum) form in base 2, with row reductions by
-// warp shuffles inside each quad of lanes (attn_tile.cuh).
+// Work split: one wave of CTAs that share the batch's blocks evenly. A "tile" is
+// one block of one sequence with all its KV heads (K and V of all heads of a
+// block are adjacent in the pool, so one 5-D TMA box per tensor fetches them).
+// The batch's tiles, sequence after sequence, are cut into equal runs, one per
+// CTA (every CTA computes the prefix sums of the per-sequence block counts from
+// context_lens), so every CTA streams the same number of bytes whatever the mix
+// of lengths.
 //
-// Partial results of a sequence's chunks are combined by the last CTA to
-// finish (an atomic ticket per (sequence, head); no CTA ever waits for
-// another). Chunks are combined in chunk order, so the result does not depend
-// on which CTA finishes last. A sequence with one chunk skips the workspace.
+// Inside a CTA one producer warp walks its run, resolves each tile's block id
+// through the block table (32 at a time, one lookup per lane, the next 32
+// already in flight) and keeps a ring of stages full with TMA copies (128B
+// swizzle, L2 evict-first). 8 consumer warps split the KV heads (8 / Hkv warps
+// per head) and take the run's tiles round-robin, each through stages of the
+// ring that only it consumes, so that it waits on every phase of those stages'
+// mbarriers in turn (a parity wait cannot tell a phase from the one two later).
+// Each consumer runs the 16-key flash
+// step on mma.sync m16n8k16 with the M = 16 rows being the GQA group's query
+// heads (the reference regroups head h to (h / group, h % group) the same
+// way), so a tile read from HBM serves the whole group (attn_tile.cuh), then
+// hands the stage back to the producer through an mbarrier.
+//
+// A run covers pieces of consecutive sequences. At the end of a piece the warps
+// of a head merge their softmax states through shared memory (a named barrier
+// per head). A piece that is a whole sequence is written out directly; only the
+// first and the last piece of a run can be partial, so a CTA keeps at most two
+// partial states per head in the workspace. The last CTA of a split sequence to
+// finish (an atomic ticket per sequence; no CTA ever waits for another) merges
+// its pieces in run order, so the result does not depend on which CTA came last.
 #include <algorithm>
+#include <cstdlib>
 
 #include "attn_tile.cuh"
 #include "common.cuh"
@@ -29,18 +43,37 @@
 namespace pkv {
 namespace {
 
-constexpr int kBS = 16;   // tokens per block handled by this kernel
-constexpr int kNW = 4;    // warps per CTA
+constexpr int kBS = 16;  // tokens per block handled by this kernel
+constexpr int kNC = 8;   // consumer warps
+constexpr int kThreads = (kNC + 1) * 32;
+constexpr int kMaxBatch = 1024;  // the prefix sums live in shared memory
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int64_t kMaxTickets = 65536;
 
-template <int D> struct DecodeShape {
-  static constexpr int CB = D == 64 ? 8 : 4;  // blocks per chunk (32 KB of K+V tiles per CTA)
-  static constexpr int TILE = kBS * D * 2;     // bytes of one (block, head) tile
-  static constexpr int MAXR = 16;              // rows of the mma tile
-  static constexpr int DP = D + 4;             // padded row of the warp-combine buffer (no bank conflicts)
-  static constexpr int COMBINE = 2 * kNW * MAXR * 4 + kNW * MAXR * DP * 4;
-  static constexpr int BARS = (2 * CB * TILE > COMBINE ? 2 * CB * TILE : COMBINE);  // barrier offset
-  static constexpr int SMEM = BARS + CB * 8 + 1024;  // + barriers + alignment slack
+// D: head_dim, NH: KV heads (all in one tile), RK: rows kept per head (8 or 16 >= group),
+// DEEP: one CTA per SM with up to 6 ring stages per consumer warp.
+template <int D, int NH, int RK, bool DEEP = false> struct DecodeShape {
+  static constexpr int TILE = kBS * D * 2;  // one head's K (or V) for one block
+  static constexpr int STAGE = NH * TILE;   // K (or V) of all heads of one block
+  static constexpr int WPH = kNC / NH;      // consumer warps per KV head
+  static constexpr int DP = D + 4;          // padded combine row (no bank conflicts)
+  static constexpr int WARP_COMB = 2 * RK + RK * DP;        // floats: m[RK], l[RK], O[RK][DP]
+  static constexpr int COMB = NH * WPH * WARP_COMB * 4;     // bytes
+  static constexpr int PREFIX = 3 * (kMaxBatch + 1) * 4;    // block prefix sums, context lengths, table rows
+  // Each consumer warp owns PW stages of the ring (see decode_kernel): S = WPH * PW.
+  // Two CTAs per SM when every warp keeps at least 2 stages in half the shared memory,
+  // otherwise one CTA with up to 3 stages per warp.
+  static constexpr int HALF = 113 * 1024 - 1024 - COMB - PREFIX - 256;
+  static constexpr int FULL = 226 * 1024 - 1024 - COMB - PREFIX - 256;
+  static constexpr int PW_HALF = HALF / (2 * STAGE) / WPH;
+  static constexpr int PW_FULL = FULL / (2 * STAGE) / WPH;
+  static constexpr int PW = DEEP ? (PW_FULL > 6 ? 6 : PW_FULL)
+                                 : (PW_HALF >= 2 ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > 3 ? 3 : PW_FULL));
+  static constexpr int S = WPH * PW;
+  static constexpr int RING = 2 * S * STAGE;
+  static constexpr int SMEM = 1024 + RING + COMB + (2 * S + 2) * 8 + PREFIX;
+  static constexpr int MIN_BLOCKS = 2 * (SMEM + 1024) <= 228 * 1024 ? 2 : 1;  // CTAs per SM to plan registers for
+  static_assert(PW >= 2, "ring too shallow");
 };
 
 struct DecodeParams {
@@ -56,304 +89,571 @@ struct DecodeParams {
   const int32_t* context_lens;
   int32_t* status;
   int32_t* counters;
-  float* ws_m;
-  float* ws_l;
-  float* ws_o;
+  float* partials;  // [ctas][2][NH][RK][D + 4]: (m, l, pad, pad, O) per row
   int64_t out_sb, out_sh, q_sb, q_sh, kv_sb, kv_sh, table_stride;
   int32_t table_rows, table_cols;
-  int32_t batch, num_kv_heads, group, layer, nbt, max_chunks;
+  int32_t batch, group, layer, nbt, inputs_ready;
   float scale_log2;
 };
 
-// Rows of the M=16 tile that carry real query heads and are kept in the combine.
-template <int D> __host__ __device__ constexpr int kept_rows(int group) { return group <= 8 ? 8 : 16; }
+// Largest b in [0, n) with p[b] <= t (p non-decreasing, p[0] = 0 <= t).
+__device__ inline int seq_of(const int* p, int n, int t) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kNW * 32) decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
+__device__ inline void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ inline void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <typename T, int D, int NH, int RK, bool DEEP>
+__global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BLOCKS) decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                                           const __grid_constant__ CUtensorMap tmap_v,
                                                           const DecodeParams p) {
-  using S = DecodeShape<D>;
-  constexpr int CB = S::CB;
-  constexpr int TILE = S::TILE;
+  using S = DecodeShape<D, NH, RK, DEEP>;
+  constexpr int TILE = S::TILE, STAGE = S::STAGE, NS = S::S, WPH = S::WPH, PW = S::PW, DP = S::DP;
+  constexpr int WC = S::WARP_COMB;
+  constexpr int ROW = D + 4;          // partial row: m, l, 2 pad floats, O[D] (O 16-byte aligned)
+  constexpr int SLOT = RK * ROW;      // floats of one partial state of one head
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BARS);
-  __shared__ int s_last;
+  uint8_t* ring_k = smem;
+  uint8_t* ring_v = smem + NS * STAGE;
+  float* comb = reinterpret_cast<float*>(smem + S::RING);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::COMB);
+  uint64_t* empty = full + NS;
+  uint64_t* merge_bar = empty + NS;              // completion of the merge's bulk copies
+  int* sP = reinterpret_cast<int*>(merge_bar + 2);  // [batch + 1] block prefix sums
+  int* sCtx = sP + kMaxBatch + 1;                // [batch] clamped context lengths
+  int* sRow = sCtx + kMaxBatch + 1;              // [batch] block-table row of each sequence
+  __shared__ int s_combine[2];
+  __shared__ int s_bad;
 
-  const int chunk = blockIdx.x, head = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t4 = lane & 3;
-  const int G = p.group;
-  const int max_ctx = p.table_cols * kBS;
+  const int g_lane = lane >> 2, t4 = lane & 3;
+  const int B = p.batch, G = p.group;
+  const int cap = p.table_cols * kBS;
 
-  int ctx = p.context_lens[b];
-  if (ctx > max_ctx) {
-    if (chunk == 0 && tid == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
-    ctx = max_ctx;
+  // With programmatic dependent launch this CTA may start while the previous kernel in
+  // the stream drains; let the next kernel launch early too. Everything the previous
+  // kernel may have produced is read only after grid_dep_wait(). With inputs_ready the
+  // caller guarantees that context lengths, table rows and the cached K/V were complete
+  // before the previous kernel began, so the prologue, the block lookups and the first
+  // ring fill run before the wait, overlapping the previous kernel's tail; q, the new
+  // rows, the append, the output and the workspace still come after it.
+  grid_dep_launch_dependents();
+  if (!p.inputs_ready) grid_dep_wait();
+
+  // Every thread fetches some context lengths and table rows (independent loads, one
+  // round trip for the whole batch); warp 0 then scans them in shared memory.
+  for (int i = tid; i < B; i += blockDim.x) {
+    int ctx = p.context_lens[i];
+    int row = p.seq_rows ? p.seq_rows[i] : i;
+    if (ctx > cap) {
+      report(p.status, PKV_ERR_OUT_OF_RANGE);
+      ctx = cap;
+    }
+    if (row >= p.table_rows) {
+      report(p.status, PKV_ERR_OUT_OF_RANGE);
+      row = -1;
+    }
+    sCtx[i] = max(ctx, 0);
+    sRow[i] = row;
   }
-  const int nblk = (ctx + kBS - 1) / kBS;
-  const int nchunks = (nblk + CB - 1) / CB;
-  if (ctx <= 0) {  // nothing to attend to: zeros (the reference never asks for this)
-    if (chunk == 0) {
+  __syncthreads();
+  if (warp == 0) {  // prefix sums of the per-sequence block counts
+    int carry = 0;
+    for (int base = 0; base < B; base += 32) {
+      const int i = base + lane;
+      int v = i < B ? (sCtx[i] + kBS - 1) / kBS : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      if (i < B) sP[i + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) sP[0] = 0;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NH);  // one consumer warp per head releases each stage
+    }
+    mbar_init(merge_bar, 1);
+    fence_mbar_init();
+    s_bad = 0;
+    s_combine[0] = s_combine[1] = -1;
+  }
+  __syncthreads();
+
+  const int total = sP[B];
+  const int ctas = min((int)gridDim.x, max(total, 1));  // every working CTA gets at least one tile
+  const int g = blockIdx.x;
+  if (g == 0) {  // sequences with nothing to attend to get zeros (the reference never asks for this)
+    grid_dep_wait();
+    for (int b = warp; b < B; b += kNC + 1) {
+      if (sCtx[b] != 0) continue;
       T* o = reinterpret_cast<T*>(p.out) + b * p.out_sb;
-      for (int i = tid; i < G * D; i += blockDim.x) o[(head * G + i / D) * p.out_sh + i % D] = Dt<T>::from_f(0.f);
+      for (int e = lane; e < NH * G * D; e += 32) o[(e / D) * p.out_sh + e % D] = Dt<T>::from_f(0.f);
+    }
+  }
+  if (g >= ctas) return;
+  // Tile j of the run is consumed, for every head, by warp j % WPH of that head, whose
+  // private stages are w * PW .. w * PW + PW - 1. A warp therefore waits on every phase
+  // of its stages in order (an mbarrier parity wait is only unambiguous within one phase
+  // of the barrier), and the previous use of tile j's stage is tile j - NS.
+  auto stage_of = [](int j) { return (j % WPH) * PW + (j / WPH) % PW; };
+  auto use_of = [](int j) { return (j / WPH) / PW; };
+  const int t0 = (int)((int64_t)total * g / ctas);
+  const int t1 = (int)((int64_t)total * (g + 1) / ctas);
+  const int n = t1 - t0;
+  const uint64_t deadline = global_ns() + kWaitBudgetNs;
+
+  if (warp == kNC) {
+    // ---------------------------------------------------------------- producer
+    const uint64_t pol = policy_evict_first();
+    auto lookup = [&](int j) -> int {  // block id of local tile j
+      if (j >= n) return 0;
+      const int t = t0 + j;
+      const int b = seq_of(sP, B, t);
+      const int i = t - sP[b];
+      const int row = sRow[b];
+      int blk = row >= 0 ? p.tables[row * p.table_stride + i] : p.nbt - 1;  // padding rows: scratch block
+      if (blk < 0 || blk >= p.nbt) {
+        report(p.status, PKV_ERR_OUT_OF_RANGE);
+        blk = p.nbt - 1;
+      }
+      return blk;
+    };
+    int blk_next = lookup(lane);
+    bool ok = true;
+    for (int base = 0; base < n && ok; base += 32) {
+      const int blk_cur = blk_next;
+      blk_next = lookup(base + 32 + lane);  // in flight while this batch is issued
+      const int cnt = min(32, n - base);
+      for (int k = 0; k < cnt && ok; ++k) {
+        const int blk = __shfl_sync(0xffffffffu, blk_cur, k);
+        const int j = base + k;
+        const int st = stage_of(j);
+        if (j == NS) grid_dep_wait();  // before the consumers can release anything
+        if (lane == 0) {
+          if (j >= NS && !mbar_wait_until(&empty[st], (use_of(j) - 1) & 1, deadline)) {
+            report(p.status, PKV_ERR_TIMEOUT);
+            ok = false;
+          }
+          if (ok) {
+            const int c4 = p.layer * p.nbt + blk;
+            mbar_arrive_expect_tx(&full[st], 2 * STAGE);
+            tma_load_5d(ring_k + st * STAGE, &tmap_k, 0, 0, 0, 0, c4, &full[st], pol);
+            tma_load_5d(ring_v + st * STAGE, &tmap_v, 0, 0, 0, 0, c4, &full[st], pol);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      }
+    }
+    if (n <= NS) grid_dep_wait();
+    if (!ok) s_bad = 1;
+  } else {
+    // ---------------------------------------------------------------- consumers
+    grid_dep_wait();  // q, the new rows, the output and the pool writes depend on earlier kernels
+    // Every warp of a head walks the same pieces and meets the same named barriers, also
+    // after a timed-out wait (then it skips waits and math), so no barrier is left short.
+    const int h = warp / WPH, w = warp % WPH;
+    float* head_comb = comb + h * WPH * WC;
+    bool ok = true;
+    // Q fragments of this head's query group (A operand, rows = query heads). The next
+    // piece's are fetched while this piece runs, so a piece boundary does not wait on them.
+    auto load_q = [&](int bq, uint32_t (&dst)[D / 16][4]) {
+      const T* qb = reinterpret_cast<const T*>(p.q) + bq * p.q_sb + (int64_t)h * G * p.q_sh;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int c0 = kk * 16 + 2 * t4;
+        dst[kk][0] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0) : 0u;
+        dst[kk][1] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0) : 0u;
+        dst[kk][2] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0 + 8) : 0u;
+        dst[kk][3] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0 + 8) : 0u;
+      }
+    };
+    uint32_t qa[D / 16][4];
+    for (int b = seq_of(sP, B, t0); b < B && sP[b] < t1; ++b) {
+      const int ja = max(t0, sP[b]) - t0, jb = min(t1, sP[b + 1]) - t0;
+      if (ja >= jb) continue;  // an empty sequence
+      const int ctx = sCtx[b];
+      load_q(b, qa);
+      const int append_blk = p.k_new ? (ctx - 1) / kBS : -1;
+      float m_r[2] = {-INFINITY, -INFINITY};
+      float l_r[2] = {0.f, 0.f};
+      float o[D / 8][4];
+#pragma unroll
+      for (int jj = 0; jj < D / 8; ++jj) o[jj][0] = o[jj][1] = o[jj][2] = o[jj][3] = 0.f;
+
+      for (int j = ja + ((w - ja) % WPH + WPH) % WPH; j < jb; j += WPH) {
+        const int st = stage_of(j);
+        if (ok && !mbar_wait_until(&full[st], use_of(j) & 1, deadline)) {
+          report(p.status, PKV_ERR_TIMEOUT);
+          ok = false;
+        }
+        if (ok) {
+          uint8_t* kt = ring_k + st * STAGE + h * TILE;
+          uint8_t* vt = ring_v + st * STAGE + h * TILE;
+          const int i = t0 + j - sP[b];  // block index within the sequence
+          if (i == append_blk) {
+            // Put the new row into the staged tiles and write it to the pool at slot_mapping[b].
+            const int off = (ctx - 1) % kBS;
+            const int64_t slot = p.slot_mapping[b];
+            const bool write = slot >= 0 && slot < (int64_t)p.nbt * kBS;
+            if (slot >= (int64_t)p.nbt * kBS && lane == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
+            const T* kn = reinterpret_cast<const T*>(p.k_new) + b * p.kv_sb + h * p.kv_sh;
+            const T* vn = reinterpret_cast<const T*>(p.v_new) + b * p.kv_sb + h * p.kv_sh;
+            const int64_t dst =
+                (((int64_t)p.layer * p.nbt + (write ? slot / kBS : 0)) * NH + h) * kBS * D + (write ? slot % kBS : 0) * D;
+#pragma unroll
+            for (int wd = lane; wd < D / 2; wd += 32) {
+              const int d0 = 2 * wd;
+              const uint32_t kw = *reinterpret_cast<const uint32_t*>(kn + d0);
+              const uint32_t vw = *reinterpret_cast<const uint32_t*>(vn + d0);
+              const uint32_t r = (d0 / 64) * kBS + off;
+              *reinterpret_cast<uint32_t*>(kt + swz128(r, d0 % 64)) = kw;
+              *reinterpret_cast<uint32_t*>(vt + swz128(r, d0 % 64)) = vw;
+              if (write) {
+                *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.k_pool) + dst + d0) = kw;
+                *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.v_pool) + dst + d0) = vw;
+              }
+            }
+            __syncwarp();
+          }
+          attend_tile16<T, D>(qa, smem_u32(kt), smem_u32(vt), i * kBS, [ctx](int, int key) { return key < ctx; },
+                              p.scale_log2, m_r, l_r, o);
+        }
+        // This warp's generic accesses to the stage come before the producer's next
+        // async-proxy fill of it.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
+      finish_row_sums(l_r);
+      // Merge the head's warps through shared memory.
+      float* cm = head_comb + w * WC;
+      float* cl = cm + RK;
+      float* co = cl + RK;
+      if (t4 == 0) {
+        cm[g_lane] = m_r[0];
+        cl[g_lane] = l_r[0];
+        if (RK > 8) {
+          cm[g_lane + 8] = m_r[1];
+          cl[g_lane + 8] = l_r[1];
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < D / 8; ++jj) {
+        const int col = 8 * jj + 2 * t4;
+        *reinterpret_cast<float2*>(&co[g_lane * DP + col]) = make_float2(o[jj][0], o[jj][1]);
+        if (RK > 8) *reinterpret_cast<float2*>(&co[(g_lane + 8) * DP + col]) = make_float2(o[jj][2], o[jj][3]);
+      }
+      named_bar(1 + h, WPH * 32);
+      const bool whole = sP[b] >= t0 && sP[b + 1] <= t1;
+      const int slot_kind = sP[b] <= t0 ? 0 : 1;  // the run's first piece, else its last
+      float* part = p.partials + ((int64_t)(g * 2 + slot_kind) * NH + h) * SLOT;
+      T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)h * G * p.out_sh;
+      for (int it = w * 32 + lane; it < G * (D / 2); it += WPH * 32) {
+        const int r = it / (D / 2), col = 2 * (it % (D / 2));
+        float mm = -INFINITY;
+#pragma unroll
+        for (int ww = 0; ww < WPH; ++ww) mm = fmaxf(mm, head_comb[ww * WC + r]);
+        float ll = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < WPH; ++ww) {
+          const float* c = head_comb + ww * WC;
+          const float f = ex2(c[r] - mm);
+          ll += c[RK + r] * f;
+          const float2 v = *reinterpret_cast<const float2*>(&c[2 * RK + r * DP + col]);
+          o0 += v.x * f;
+          o1 += v.y * f;
+        }
+        if (whole) {
+          const float inv = 1.f / ll;
+          *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + col) = Dt<T>::pack(o0 * inv, o1 * inv);
+        } else {
+          __stcg(reinterpret_cast<float2*>(part + r * ROW + 4 + col), make_float2(o0, o1));
+          if (col == 0) __stcg(reinterpret_cast<float2*>(part + r * ROW), make_float2(mm, ll));
+        }
+      }
+      if (!whole && w == 0 && lane == 0) s_combine[slot_kind] = b;
+      named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next piece
+    }
+    if (!ok) s_bad = 1;
+  }
+  __syncthreads();
+  if (s_bad) return;
+
+  // Tickets for this run's split sequences; the last CTA of each merges its pieces.
+  // The barrier orders the CTA's partial writes before thread 0's release fence; the last
+  // ticket holder's acquire fence orders them before its CTA's reads (fence-fence
+  // synchronisation through the ticket atomics, cheaper than sequentially consistent fences).
+  auto cta_of = [&](int t) { return (int)(((int64_t)(t + 1) * ctas - 1) / total); };
+  if (tid == 0 && (s_combine[0] >= 0 || s_combine[1] >= 0)) {
+    fence_acq_rel_gpu();
+    int ticket[2] = {-1, -1};
+    for (int k = 0; k < 2; ++k)  // both in flight together
+      if (s_combine[k] >= 0) ticket[k] = atomicAdd(p.counters + s_combine[k], 1);
+    bool last_any = false;
+    for (int k = 0; k < 2; ++k) {
+      const int b = s_combine[k];
+      if (b < 0) continue;
+      const int pieces = cta_of(sP[b + 1] - 1) - cta_of(sP[b]) + 1;
+      if (ticket[k] == pieces - 1) {
+        p.counters[b] = 0;  // ready for the next call
+        last_any = true;
+      } else {
+        s_combine[k] = -1;
+      }
+    }
+    if (last_any) fence_acq_rel_gpu();
+  }
+  __syncthreads();
+  // Merge every sequence this CTA got the last ticket of. Piece pc of a sequence is CTA
+  // g_first + pc; every piece but the first starts its CTA's run (slot 0); the first is
+  // its CTA's last piece (slot 1) unless that run also starts with the sequence. The
+  // pieces' states of every pending merge are copied into the (now idle) ring with one
+  // round of independent 16-byte loads, then merged from shared memory; sequences split
+  // into more pieces than the ring holds go through it in several rounds.
+  const int nmerge = (s_combine[0] >= 0) + (s_combine[1] >= 0);
+  if (nmerge == 0) return;
+  int mb[2] = {0, 0}, mfirst[2] = {0, 0}, mnp[2] = {0, 0}, mkind0[2] = {0, 0};
+  for (int k = 0, m = 0; k < 2; ++k) {
+    if (s_combine[k] < 0) continue;
+    const int b = s_combine[k];
+    mb[m] = b;
+    mfirst[m] = cta_of(sP[b]);
+    mnp[m] = cta_of(sP[b + 1] - 1) - mfirst[m] + 1;
+    mkind0[m] = (int)((int64_t)total * mfirst[m] / ctas) >= sP[b] ? 0 : 1;
+    ++m;
+  }
+  constexpr int PIECE = NH * SLOT;             // floats of one piece (all heads)
+  constexpr int CAP = S::RING / (PIECE * 4);  // pieces the ring holds
+  static_assert(CAP >= 2, "ring too small to stage merge pieces");
+  float* stage = reinterpret_cast<float*>(smem);
+  const int per_seq = NH * G * (D / 2);
+  auto piece_src = [&](int m, int pc) {
+    const int kind = pc == 0 ? mkind0[m] : 0;
+    return p.partials + (int64_t)((mfirst[m] + pc) * 2 + kind) * PIECE;
+  };
+  // Pieces pc0.. of merge m -> stage slots q0..: one bulk copy per piece, issued by one
+  // thread, all completing on merge_bar (the other CTAs' partials were published with
+  // release fences and acquired above; the proxy fence orders that for the copy engine).
+  // stage_wait() waits for the round's bytes; every thread takes part, each round flips
+  // the barrier's phase.
+  int merge_phase = 0;
+  auto stage_pieces = [&](int m, int pc0, int cnt, int q0, uint32_t& bytes) {
+    if (tid == 0) {
+      for (int q = 0; q < cnt; ++q) {
+        bulk_load(stage + (q0 + q) * PIECE, piece_src(m, pc0 + q), PIECE * 4, merge_bar);
+      }
+    }
+    bytes += cnt * PIECE * 4;
+  };
+  auto stage_start = [&](uint32_t bytes) {
+    if (tid == 0) {
+      fence_proxy_async_global();
+      mbar_arrive_expect_tx(merge_bar, bytes);
+    }
+  };
+  auto stage_wait = [&]() {
+    if (!mbar_wait_until(merge_bar, merge_phase & 1, global_ns() + kWaitBudgetNs)) report(p.status, PKV_ERR_TIMEOUT);
+    ++merge_phase;
+  };
+  auto item_of = [&](int rest, int& h, int& r, int& col) {
+    h = rest / (G * (D / 2));
+    r = (rest / (D / 2)) % G;
+    col = 2 * (rest % (D / 2));
+  };
+  auto store = [&](int m, int h, int r, int col, float o0, float o1) {
+    T* outp = reinterpret_cast<T*>(p.out) + mb[m] * p.out_sb + (int64_t)h * G * p.out_sh;
+    *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + col) = Dt<T>::pack(o0, o1);
+  };
+
+  if (mnp[0] + mnp[1] <= CAP) {
+    // Common case: every piece of every pending merge fits; one round of loads.
+    stage_start((mnp[0] + mnp[1]) * PIECE * 4);
+    uint32_t bytes = 0;
+    stage_pieces(0, 0, mnp[0], 0, bytes);
+    if (nmerge > 1) stage_pieces(1, 0, mnp[1], mnp[0], bytes);
+    stage_wait();
+    for (int it = tid; it < nmerge * per_seq; it += blockDim.x) {
+      const int m = it / per_seq;
+      int h, r, col;
+      item_of(it % per_seq, h, r, col);
+      const float* base = stage + (m == 0 ? 0 : mnp[0]) * PIECE + h * SLOT + r * ROW;
+      float mm = -INFINITY;
+      for (int q = 0; q < mnp[m]; ++q) mm = fmaxf(mm, base[q * PIECE]);
+      float ll = 0.f, o0 = 0.f, o1 = 0.f;
+      for (int q = 0; q < mnp[m]; ++q) {
+        const float* row = base + q * PIECE;
+        const float f = row[0] == -INFINITY ? 0.f : ex2(row[0] - mm);
+        ll += row[1] * f;
+        o0 += row[4 + col] * f;
+        o1 += row[5 + col] * f;
+      }
+      const float inv = 1.f / ll;
+      store(m, h, r, col, o0 * inv, o1 * inv);
     }
     return;
   }
-  if (chunk >= nchunks) return;
-  const int blk0 = chunk * CB;
-  const int nb = min(CB, nblk - blk0);
-
-  int row = p.seq_rows ? p.seq_rows[b] : b;
-  if (row >= p.table_rows) {
-    if (tid == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
-    row = -1;
-  }
-  const int32_t* table = row >= 0 ? p.tables + row * p.table_stride : nullptr;
-
-  const uint64_t deadline = global_ns() + kWaitBudgetNs;
-  if (tid == 0) {
-    for (int i = 0; i < nb; ++i) mbar_init(&bars[i], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  if (warp == 0 && lane < nb) {
-    int blk = table ? table[blk0 + lane] : p.nbt - 1;  // padding rows read the scratch block
-    if (blk < 0 || blk >= p.nbt) {
-      report(p.status, PKV_ERR_OUT_OF_RANGE);
-      blk = p.nbt - 1;
-    }
-    const uint64_t pol = policy_evict_first();
-    const int c4 = p.layer * p.nbt + blk;
-    mbar_arrive_expect_tx(&bars[lane], 2 * TILE);
-    tma_load_5d(smem + lane * TILE, &tmap_k, 0, 0, 0, head, c4, &bars[lane], pol);
-    tma_load_5d(smem + (CB + lane) * TILE, &tmap_v, 0, 0, 0, head, c4, &bars[lane], pol);
-  }
-
-  // Q fragments (A operand, rows = the group's query heads), loaded while the tiles fly.
-  uint32_t qa[D / 16][4];
-  {
-    const T* qb = reinterpret_cast<const T*>(p.q) + b * p.q_sb + (int64_t)head * G * p.q_sh;
+  // A sequence split into more pieces than the ring holds: merge one sequence at a time,
+  // a few items per thread, the pieces in rounds of CAP with a running max / sum.
+  constexpr int kMaxItems = 4;
+  for (int m = 0; m < nmerge; ++m) {
+    for (int ibase = 0; ibase < per_seq; ibase += kMaxItems * blockDim.x) {
+      float run_m[kMaxItems], run_l[kMaxItems], acc0[kMaxItems], acc1[kMaxItems];
 #pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const int c0 = kk * 16 + 2 * t4;
-      qa[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * p.q_sh + c0) : 0u;
-      qa[kk][1] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * p.q_sh + c0) : 0u;
-      qa[kk][2] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * p.q_sh + c0 + 8) : 0u;
-      qa[kk][3] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * p.q_sh + c0 + 8) : 0u;
-    }
-  }
-
-  // The fused append: the new token sits at position ctx - 1, in the last chunk.
-  const bool append = p.k_new != nullptr && chunk == nchunks - 1;
-  const int new_pos = ctx - 1;
-  const int append_lb = append ? new_pos / kBS - blk0 : -1;
-
-  float m_r[2] = {-INFINITY, -INFINITY};
-  float l_r[2] = {0.f, 0.f};
-  float o[D / 8][4];
+      for (int u = 0; u < kMaxItems; ++u) run_m[u] = -INFINITY, run_l[u] = acc0[u] = acc1[u] = 0.f;
+      for (int done = 0; done < mnp[m]; done += CAP) {
+        const int cnt = min(CAP, mnp[m] - done);
+        stage_start(cnt * PIECE * 4);
+        uint32_t bytes = 0;
+        stage_pieces(m, done, cnt, 0, bytes);
+        stage_wait();
 #pragma unroll
-  for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  bool timed_out = false;
-
-  for (int lb = warp; lb < nb; lb += kNW) {
-    if (!mbar_wait_until(&bars[lb], 0, deadline)) {
-      timed_out = true;
-      break;
-    }
-    uint8_t* kt = smem + lb * TILE;
-    uint8_t* vt = smem + (CB + lb) * TILE;
-    if (lb == append_lb) {
-      // Put the new row into the staged tiles and write it to the pool at slot_mapping[b].
-      const int off = new_pos % kBS;
-      const int64_t slot = p.slot_mapping[b];
-      const bool write = slot >= 0 && slot < (int64_t)p.nbt * kBS;
-      if (slot >= (int64_t)p.nbt * kBS && lane == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
-      const T* kn = reinterpret_cast<const T*>(p.k_new) + b * p.kv_sb + head * p.kv_sh;
-      const T* vn = reinterpret_cast<const T*>(p.v_new) + b * p.kv_sb + head * p.kv_sh;
-      const int64_t dst = (((int64_t)p.layer * p.nbt + (write ? slot / kBS : 0)) * p.num_kv_heads + head) * kBS * D +
-                          (write ? slot % kBS : 0) * D;
-#pragma unroll
-      for (int w = lane; w < D / 2; w += 32) {
-        const int d0 = 2 * w;
-        const uint32_t kw = *reinterpret_cast<const uint32_t*>(kn + d0);
-        const uint32_t vw = *reinterpret_cast<const uint32_t*>(vn + d0);
-        const uint32_t r = (d0 / 64) * kBS + off;
-        *reinterpret_cast<uint32_t*>(kt + swz128(r, d0 % 64)) = kw;
-        *reinterpret_cast<uint32_t*>(vt + swz128(r, d0 % 64)) = vw;
-        if (write) {
-          *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.k_pool) + dst + d0) = kw;
-          *reinterpret_cast<uint32_t*>(reinterpret_cast<T*>(p.v_pool) + dst + d0) = vw;
+        for (int u = 0; u < kMaxItems; ++u) {
+          const int it = ibase + tid + u * blockDim.x;
+          if (it >= per_seq) break;
+          int h, r, col;
+          item_of(it, h, r, col);
+          const float* base = stage + h * SLOT + r * ROW;
+          float mm = run_m[u];
+          for (int q = 0; q < cnt; ++q) mm = fmaxf(mm, base[q * PIECE]);
+          const float f_old = run_m[u] == -INFINITY ? 0.f : ex2(run_m[u] - mm);
+          run_l[u] *= f_old;
+          acc0[u] *= f_old;
+          acc1[u] *= f_old;
+          for (int q = 0; q < cnt; ++q) {
+            const float* row = base + q * PIECE;
+            const float f = row[0] == -INFINITY ? 0.f : ex2(row[0] - mm);
+            run_l[u] += row[1] * f;
+            acc0[u] += row[4 + col] * f;
+            acc1[u] += row[5 + col] * f;
+          }
+          run_m[u] = mm;
         }
+        __syncthreads();  // the staging area is refilled by the next round
       }
-      __syncwarp();
-    }
-    const int key0 = (blk0 + lb) * kBS;
-    attend_tile16<T, D>(qa, smem_u32(kt), smem_u32(vt), key0, [ctx](int, int key) { return key < ctx; },
-                        p.scale_log2, m_r, l_r, o);
-  }
-  if (timed_out) report(p.status, PKV_ERR_TIMEOUT);
-  // No copy may still be landing when the tiles' memory is reused below. On the normal
-  // path every barrier has already completed and this is nb polls.
-  if (tid == 0) {
-    for (int i = 0; i < nb; ++i) {
-      if (!mbar_wait_until(&bars[i], 0, deadline)) {
-        report(p.status, PKV_ERR_TIMEOUT);
-        break;
+#pragma unroll
+      for (int u = 0; u < kMaxItems; ++u) {
+        const int it = ibase + tid + u * blockDim.x;
+        if (it >= per_seq) break;
+        int h, r, col;
+        item_of(it, h, r, col);
+        const float inv = 1.f / run_l[u];
+        store(m, h, r, col, acc0[u] * inv, acc1[u] * inv);
       }
     }
-  }
-
-  finish_row_sums(l_r);
-
-  // Combine the warps through shared memory (the tiles are no longer needed).
-  constexpr int MAXR = S::MAXR;
-  constexpr int DP = S::DP;
-  const int R = kept_rows<D>(G);
-  __syncthreads();
-  float* c_m = reinterpret_cast<float*>(smem);  // [kNW][MAXR]
-  float* c_l = c_m + kNW * MAXR;                // [kNW][MAXR]
-  float* c_o = c_l + kNW * MAXR;                // [kNW][R][DP]
-  if (t4 == 0) {
-    c_m[warp * MAXR + g] = m_r[0];
-    c_l[warp * MAXR + g] = l_r[0];
-    c_m[warp * MAXR + g + 8] = m_r[1];
-    c_l[warp * MAXR + g + 8] = l_r[1];
-  }
-#pragma unroll
-  for (int j = 0; j < D / 8; ++j) {
-    const int col = 8 * j + 2 * t4;
-    c_o[(warp * R + g) * DP + col] = o[j][0];
-    c_o[(warp * R + g) * DP + col + 1] = o[j][1];
-    if (R > 8) {
-      c_o[(warp * R + g + 8) * DP + col] = o[j][2];
-      c_o[(warp * R + g + 8) * DP + col + 1] = o[j][3];
-    }
-  }
-  __syncthreads();
-
-  const bool single = nchunks == 1;
-  const int unit_idx = (b * p.num_kv_heads + head) * p.max_chunks + chunk;
-  T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)head * G * p.out_sh;
-  // Each thread produces pairs of adjacent columns of the G x D result.
-  for (int i = tid; i < G * (D / 2); i += blockDim.x) {
-    const int r = i / (D / 2), col = 2 * (i % (D / 2));
-    float mm = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kNW; ++w) mm = fmaxf(mm, c_m[w * MAXR + r]);
-    float ll = 0.f, o0 = 0.f, o1 = 0.f;
-#pragma unroll
-    for (int w = 0; w < kNW; ++w) {
-      const float f = ex2(c_m[w * MAXR + r] - mm);
-      ll += c_l[w * MAXR + r] * f;
-      o0 += c_o[(w * R + r) * DP + col] * f;
-      o1 += c_o[(w * R + r) * DP + col + 1] * f;
-    }
-    if (single) {
-      const float inv = 1.f / ll;
-      *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + col) = Dt<T>::pack(o0 * inv, o1 * inv);
-    } else {
-      float* wo = p.ws_o + ((int64_t)unit_idx * R + r) * D;
-      __stcg(wo + col, o0);
-      __stcg(wo + col + 1, o1);
-      if (col == 0) {
-        __stcg(p.ws_m + (int64_t)unit_idx * R + r, mm);
-        __stcg(p.ws_l + (int64_t)unit_idx * R + r, ll);
-      }
-    }
-  }
-  if (single) return;
-
-  // Last CTA of this (sequence, head) combines every chunk, in chunk order.
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    int* ctr = p.counters + b * p.num_kv_heads + head;
-    const int ticket = atomicAdd(ctr, 1);
-    s_last = ticket == nchunks - 1;
-    if (s_last) *ctr = 0;  // ready for the next call
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const int first = (b * p.num_kv_heads + head) * p.max_chunks;
-  for (int i = tid; i < G * (D / 2); i += blockDim.x) {
-    const int r = i / (D / 2), col = 2 * (i % (D / 2));
-    float mm = -INFINITY;
-    for (int c = 0; c < nchunks; ++c) mm = fmaxf(mm, __ldcg(p.ws_m + (int64_t)(first + c) * R + r));
-    float ll = 0.f, o0 = 0.f, o1 = 0.f;
-    for (int c = 0; c < nchunks; ++c) {
-      const int64_t u = first + c;
-      const float f = ex2(__ldcg(p.ws_m + u * R + r) - mm);
-      ll += __ldcg(p.ws_l + u * R + r) * f;
-      const float* wo = p.ws_o + (u * R + r) * D;
-      o0 += __ldcg(wo + col) * f;
-      o1 += __ldcg(wo + col + 1) * f;
-    }
-    const float inv = 1.f / ll;
-    *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + col) = Dt<T>::pack(o0 * inv, o1 * inv);
   }
 }
 
-// Workspace layout: [counters: kMaxTickets int32][m][l][o], where m and l are float
-// [batch * Hkv * max_chunks * R] and o is float [batch * Hkv * max_chunks * R * D].
-// The counter region has a fixed size, so calls with different batch sizes or
-// table widths that share a workspace never see partial results where counters
-// live (each counter is back at zero when its call ends).
-constexpr int64_t kMaxTickets = 65536;
+// Workspace: [counters: kMaxTickets int32][partials: ctas * 2 * NH * RK * (D + 4) float].
+// Counters are indexed by sequence and are back at zero when a call ends.
+constexpr int64_t kPartialsOffset = kMaxTickets * 4;
+int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (int64_t)ctas * 2 * nh * rk * (d + 4) * 4; }
+constexpr int kMaxCtas = 4 * 256;  // workspace is sized for up to 4 CTAs on each of up to 256 SMs
 
-struct WsLayout {
-  int64_t counters, m, l, o, total;
+// Tuning knobs, read once from the environment (0 / unset = built-in choice):
+//   PKV_DECODE_CTAS_PER_SM  CTAs per SM (at most what the shared memory allows)
+//   PKV_DECODE_PDL          0 = launch without programmatic stream serialization
+//   PKV_DECODE_DEEP         1 = one CTA per SM with the deepest ring that fits
+struct DecodeKnobs {
+  int ctas_per_sm = 0, pdl = 1, deep = 0;
+  DecodeKnobs() {
+    auto env = [](const char* k, int dflt) {
+      const char* v = getenv(k);
+      return v && *v ? atoi(v) : dflt;
+    };
+    ctas_per_sm = env("PKV_DECODE_CTAS_PER_SM", 0);
+    pdl = env("PKV_DECODE_PDL", 1);
+    deep = env("PKV_DECODE_DEEP", 0);
+  }
 };
-
-inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
-
-WsLayout ws_layout(int batch, int hkv, int max_chunks, int rows, int d) {
-  WsLayout w;
-  const int64_t units = (int64_t)batch * hkv * max_chunks;
-  w.counters = 0;
-  w.m = kMaxTickets * 4;
-  w.l = w.m + align256(units * rows * 4);
-  w.o = w.l + align256(units * rows * 4);
-  w.total = w.o + align256(units * rows * d * 4);
-  return w;
+const DecodeKnobs& knobs() {
+  static const DecodeKnobs k;
+  return k;
 }
 
-int chunk_blocks(int d) { return d == 64 ? DecodeShape<64>::CB : DecodeShape<128>::CB; }
+template <typename T, int D, int NH, int RK, bool DEEP>
+int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace, int64_t workspace_bytes,
+                  cudaStream_t stream) {
+  using S = DecodeShape<D, NH, RK, DEEP>;
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, D, NH, RK, DEEP>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+    if (e != cudaSuccess) return cuda_status(e);
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK, DEEP>, kThreads, S::SMEM);
+    if (e != cudaSuccess) return cuda_status(e);
+    per_sm = std::max(1, occ);
+  }
+  const int want = knobs().ctas_per_sm > 0 ? std::min(knobs().ctas_per_sm, per_sm) : per_sm;
+  const int ctas = std::min(num_sms() * want, kMaxCtas);
+  if (!workspace || workspace_bytes < ws_bytes(ctas, NH, RK, D)) return PKV_ERR_WORKSPACE;
+  CUtensorMap tk, tv;
+  if (!get_pool_maps(pool, &tk, &tv, NH)) return PKV_ERR_CUDA;
+  DecodeParams p = p0;
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  p.counters = reinterpret_cast<int32_t*>(wsb);
+  p.partials = reinterpret_cast<float*>(wsb + kPartialsOffset);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = S::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = knobs().pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, DEEP>, tk, tv, p));
+}
+
+template <typename T, int D, int NH>
+int launch_rows(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
+  if (knobs().deep)
+    return p.group <= 8 ? launch_decode<T, D, NH, 8, true>(pool, p, ws, wsb, st)
+                        : launch_decode<T, D, NH, 16, true>(pool, p, ws, wsb, st);
+  return p.group <= 8 ? launch_decode<T, D, NH, 8, false>(pool, p, ws, wsb, st)
+                      : launch_decode<T, D, NH, 16, false>(pool, p, ws, wsb, st);
+}
 
 template <typename T, int D>
-int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeParams& p, int batch, int hkv,
-                  cudaStream_t stream) {
-  using S = DecodeShape<D>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
-    if (e != cudaSuccess) return cuda_status(e);
-    configured = true;
+int launch_heads(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
+  switch (pool.num_kv_heads) {
+    case 1: return launch_rows<T, D, 1>(pool, p, ws, wsb, st);
+    case 2: return launch_rows<T, D, 2>(pool, p, ws, wsb, st);
+    case 4: return launch_rows<T, D, 4>(pool, p, ws, wsb, st);
+    default: return PKV_ERR_UNSUPPORTED;
   }
-  dim3 grid(p.max_chunks, hkv, batch);
-  decode_kernel<T, D><<<grid, kNW * 32, S::SMEM, stream>>>(tk, tv, p);
-  return launch_status();
 }
 
 }  // namespace
-
-bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv);
-
 }  // namespace pkv
 
 using namespace pkv;
 
 extern "C" int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
                                               int32_t block_size, int32_t head_dim, int32_t num_q_heads) {
-  if (batch <= 0 || num_kv_heads <= 0 || max_blocks_per_seq <= 0 || block_size != kBS ||
-      (head_dim != 64 && head_dim != 128) || num_q_heads % num_kv_heads != 0)
+  if (batch <= 0 || batch > kMaxBatch || num_kv_heads <= 0 || max_blocks_per_seq <= 0 || block_size != kBS ||
+      (head_dim != 64 && head_dim != 128) || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0)
     return 0;
-  const int cb = chunk_blocks(head_dim);
-  const int max_chunks = (max_blocks_per_seq + cb - 1) / cb;
   const int group = num_q_heads / num_kv_heads;
-  return ws_layout(batch, num_kv_heads, max_chunks, group <= 8 ? 8 : 16, head_dim).total;
+  return ws_bytes(kMaxCtas, num_kv_heads, group <= 8 ? 8 : 16, head_dim);
 }
 
 extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
@@ -361,11 +661,12 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
                                     const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_new,
                                     const void* v_new, int64_t kv_stride_b, int64_t kv_stride_h,
                                     const int64_t* slot_mapping, const int32_t* context_lens, float scale,
-                                    void* workspace, int64_t workspace_bytes, int32_t* status_dev,
-                                    pkv_stream_t stream) {
+                                    int32_t flags, void* workspace, int64_t workspace_bytes,
+                                    int32_t* status_dev, pkv_stream_t stream) {
   if (!pool || !tables || !out || !q || !context_lens || !tables->block_tables) return PKV_ERR_INVALID_ARGUMENT;
-  if (batch < 0 || batch > 65535 || layer < 0 || layer >= pool->num_layers) return PKV_ERR_INVALID_ARGUMENT;
+  if (batch < 0 || layer < 0 || layer >= pool->num_layers) return PKV_ERR_INVALID_ARGUMENT;
   if (batch == 0) return PKV_OK;
+  if (batch > kMaxBatch) return PKV_ERR_UNSUPPORTED;
   const int d = pool->head_dim, hkv = pool->num_kv_heads;
   if (pool->block_size != kBS || (d != 64 && d != 128)) return PKV_ERR_UNSUPPORTED;
   if (hkv <= 0 || num_q_heads <= 0 || num_q_heads % hkv != 0) return PKV_ERR_INVALID_ARGUMENT;
@@ -380,18 +681,7 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   if (k_new && ((kv_stride_b | kv_stride_h) & 1)) return PKV_ERR_INVALID_ARGUMENT;
   if (tables->cols <= 0 || tables->rows <= 0) return PKV_ERR_INVALID_ARGUMENT;
   if (!tables->seq_rows && tables->rows < batch) return PKV_ERR_INVALID_ARGUMENT;
-  if ((int64_t)batch * hkv > kMaxTickets) return PKV_ERR_UNSUPPORTED;
-
-  const int cb = chunk_blocks(d);
-  const int max_chunks = (tables->cols + cb - 1) / cb;
-  const int rows = group <= 8 ? 8 : 16;
-  const WsLayout ws = ws_layout(batch, hkv, max_chunks, rows, d);
-  if (max_chunks > 1) {
-    if (!workspace || workspace_bytes < ws.total) return PKV_ERR_WORKSPACE;
-    if (reinterpret_cast<uintptr_t>(workspace) & 255) return PKV_ERR_INVALID_ARGUMENT;
-  }
-  CUtensorMap tk, tv;
-  if (!get_pool_maps(*pool, &tk, &tv)) return PKV_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return PKV_ERR_INVALID_ARGUMENT;
 
   DecodeParams p{};
   p.out = out;
@@ -405,11 +695,6 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   p.seq_rows = tables->seq_rows;
   p.context_lens = context_lens;
   p.status = status_dev;
-  uint8_t* wsb = static_cast<uint8_t*>(workspace);
-  p.counters = workspace ? reinterpret_cast<int32_t*>(wsb + ws.counters) : nullptr;
-  p.ws_m = workspace ? reinterpret_cast<float*>(wsb + ws.m) : nullptr;
-  p.ws_l = workspace ? reinterpret_cast<float*>(wsb + ws.l) : nullptr;
-  p.ws_o = workspace ? reinterpret_cast<float*>(wsb + ws.o) : nullptr;
   p.out_sb = out_stride_b;
   p.out_sh = out_stride_h;
   p.q_sb = q_stride_b;
@@ -420,21 +705,20 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   p.table_rows = tables->rows;
   p.table_cols = tables->cols;
   p.batch = batch;
-  p.num_kv_heads = hkv;
   p.group = group;
   p.layer = layer;
   p.nbt = pool->num_blocks_total;
-  p.max_chunks = max_chunks;
   p.scale_log2 = scale * kLog2e;
+  p.inputs_ready = (flags & PKV_DECODE_INPUTS_READY) ? 1 : 0;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (pool->dtype == PKV_F16) {
-    return d == 64 ? launch_decode<__half, 64>(tk, tv, p, batch, hkv, st)
-                   : launch_decode<__half, 128>(tk, tv, p, batch, hkv, st);
+    return d == 64 ? launch_heads<__half, 64>(*pool, p, workspace, workspace_bytes, st)
+                   : launch_heads<__half, 128>(*pool, p, workspace, workspace_bytes, st);
   }
   if (pool->dtype == PKV_BF16) {
-    return d == 64 ? launch_decode<__nv_bfloat16, 64>(tk, tv, p, batch, hkv, st)
-                   : launch_decode<__nv_bfloat16, 128>(tk, tv, p, batch, hkv, st);
+    return d == 64 ? launch_heads<__nv_bfloat16, 64>(*pool, p, workspace, workspace_bytes, st)
+                   : launch_heads<__nv_bfloat16, 128>(*pool, p, workspace, workspace_bytes, st);
   }
   return PKV_ERR_UNSUPPORTED;
 }

@@ -168,8 +168,6 @@ int launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillPa
 
 }  // namespace
 
-bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv);
-
 }  // namespace pkv
 
 using namespace pkv;

@@ -11,6 +11,18 @@
 
 namespace pkv {
 
+int num_sms() {
+  static int n = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+  });
+  return n;
+}
+
 namespace {
 thread_local std::string g_last_cuda_error;
 
@@ -30,6 +42,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct MapEntry {
   pkv_pool pool;
+  int heads_per_box;
   CUtensorMap k, v;
 };
 std::mutex g_map_mutex;
@@ -46,7 +59,7 @@ int cuda_status(cudaError_t e) {
   return PKV_ERR_CUDA;
 }
 
-int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool) {
+int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool, int heads_per_box) {
   auto fn = encode_fn();
   if (!fn) {
     g_last_cuda_error = "cuTensorMapEncodeTiled is not available from the driver";
@@ -58,7 +71,7 @@ int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& poo
                         (cuuint64_t)pool.num_layers * (cuuint64_t)pool.num_blocks_total};
   cuuint64_t strides[4] = {(cuuint64_t)d * esz, 64 * esz, (cuuint64_t)bs * d * esz,
                            (cuuint64_t)pool.num_kv_heads * bs * d * esz};
-  cuuint32_t box[5] = {64, (cuuint32_t)bs, (cuuint32_t)(d / 64), 1, 1};
+  cuuint32_t box[5] = {64, (cuuint32_t)bs, (cuuint32_t)(d / 64), (cuuint32_t)heads_per_box, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUtensorMapDataType dt =
       pool.dtype == PKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -71,10 +84,10 @@ int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& poo
   return PKV_OK;
 }
 
-bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv) {
+bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box) {
   std::lock_guard<std::mutex> lock(g_map_mutex);
   for (const MapEntry& e : g_maps) {
-    if (same_pool(e.pool, pool)) {
+    if (same_pool(e.pool, pool) && e.heads_per_box == heads_per_box) {
       *tk = e.k;
       *tv = e.v;
       return true;
@@ -83,8 +96,9 @@ bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv) {
   MapEntry e;
   std::memset(&e, 0, sizeof(e));
   e.pool = pool;
-  if (make_pool_tensor_map(&e.k, pool.k, pool) != PKV_OK) return false;
-  if (make_pool_tensor_map(&e.v, pool.v, pool) != PKV_OK) return false;
+  e.heads_per_box = heads_per_box;
+  if (make_pool_tensor_map(&e.k, pool.k, pool, heads_per_box) != PKV_OK) return false;
+  if (make_pool_tensor_map(&e.v, pool.v, pool, heads_per_box) != PKV_OK) return false;
   if (g_maps.size() >= 64) g_maps.erase(g_maps.begin());
   g_maps.push_back(e);
   *tk = e.k;

@@ -13,7 +13,7 @@ import math
 
 import torch
 
-from ._lib import PKV_BF16, PKV_F16, PkvPool, PkvTables, check, lib
+from ._lib import PKV_BF16, PKV_DECODE_INPUTS_READY, PKV_F16, PkvPool, PkvTables, check, lib
 
 _DTYPES = {torch.float16: PKV_F16, torch.bfloat16: PKV_BF16}
 
@@ -86,11 +86,13 @@ def decode_attention(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tens
                      workspace: torch.Tensor | None, k_new: torch.Tensor | None = None,
                      v_new: torch.Tensor | None = None, slot_mapping: torch.Tensor | None = None,
                      out: torch.Tensor | None = None, scale: float | None = None,
-                     status: torch.Tensor | None = None) -> torch.Tensor:
+                     status: torch.Tensor | None = None, inputs_ready: bool = False) -> torch.Tensor:
     """One decode step on one layer: q ``[B, Hq, d]`` (any row/head strides), optional fused append.
 
     Returns ``out`` of shape ``[B, Hq, d]``. ``context_lens`` (int32 [B]) counts the keys
-    each row attends to, its new token included.
+    each row attends to, its new token included. ``inputs_ready`` promises that the
+    lengths, tables and cached K/V were complete before the previous kernel in the
+    stream began (see PKV_DECODE_INPUTS_READY in include/pkv.h).
     """
     _require_cuda(q, context_lens, k_new, v_new, slot_mapping)
     batch, hq, d = q.shape
@@ -109,8 +111,8 @@ def decode_attention(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tens
         ctypes.byref(pool), layer, ctypes.byref(tables), batch, hq, out.data_ptr(), out.stride(0), out.stride(1),
         q.data_ptr(), q.stride(0), q.stride(1), _ptr(k_new), _ptr(v_new),
         k_new.stride(0) if k_new is not None else 0, k_new.stride(1) if k_new is not None else 0,
-        _ptr(slot_mapping), context_lens.data_ptr(), scale, ws_ptr, ws_bytes, _ptr(status), _stream()),
-        "decode_attention")
+        _ptr(slot_mapping), context_lens.data_ptr(), scale, PKV_DECODE_INPUTS_READY if inputs_ready else 0,
+        ws_ptr, ws_bytes, _ptr(status), _stream()), "decode_attention")
     return out
 
 

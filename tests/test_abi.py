@@ -55,7 +55,7 @@ def test_host_calls_work_without_a_gpu():
     pool = _lib.PkvPool(None, None, 1, 4, 2, 16, 96, _lib.PKV_F16)
     tables = _lib.PkvTables(None, 0, 0, 0, None)
     assert _lib.lib.pkv_decode_attention(ctypes.byref(pool), 0, ctypes.byref(tables), 1, 14, None, 0, 0, None, 0, 0,
-                                         None, None, 0, 0, None, None, 1.0, None, 0, None, None) \
+                                         None, None, 0, 0, None, None, 1.0, 0, None, 0, None, None) \
         == _lib.PKV_ERR_INVALID_ARGUMENT
 
 

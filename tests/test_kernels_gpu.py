@@ -347,3 +347,85 @@ def test_copy_blocks_is_exact(dev):
         ek[:, d_] = k0[:, s_]
         ev[:, d_] = v0[:, s_]
     assert torch.equal(k, ek) and torch.equal(v, ev)
+
+
+def test_decode_graph_replays_stay_exact(dev):
+    """Hundreds of back-to-back replays of a multi-layer decode graph: no device error, and
+    every replay returns the bits of the first eager call (split-K merge order is fixed).
+    Layers after the first start their block lookups before the previous kernel ends
+    (PKV_DECODE_INPUTS_READY), which must not change a bit.
+
+    Regression test for ring-stage phase tracking: a consumer that skips a stage's use can
+    mistake a phase two ahead for the one it waits on, which only shows under replay timing.
+    """
+    from mini_inference_b200 import ops
+
+    layers, bs, hq, hkv, d = 4, 16, 14, 2, 64
+    ctx, tables, k_pool, v_pool, q, k_new, v_new = micro_bench_case(dev, seed=7, layers=layers)
+    meta = decode_metadata(tables, ctx, bs, max(len(t) for t in tables), pad_block=0)
+    tab = torch.from_numpy(meta["block_tables"].astype(np.int32)).to(dev)
+    pool = ops.make_pool(k_pool, v_pool)
+    tabs = ops.make_tables(tab)
+    ctx_lens = torch.from_numpy(meta["context_lens"].astype(np.int32)).to(dev)
+    slots = torch.from_numpy(meta["slot_mapping"]).to(dev)
+    ws = torch.zeros(ops.decode_workspace_bytes(64, hkv, tab.shape[1], bs, d, hq), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    outs = torch.empty(layers, 64, hq, d, dtype=torch.float16, device=dev)
+
+    def step():
+        for layer in range(layers):
+            ops.decode_attention(pool, layer, tabs, q, ctx_lens, ws, k_new=k_new, v_new=v_new, slot_mapping=slots,
+                                 out=outs[layer], status=status, inputs_ready=layer > 0)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    ops.raise_device_errors(status)
+    first = outs.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(300):
+        graph.replay()
+    torch.cuda.synchronize()
+    ops.raise_device_errors(status)
+    assert torch.equal(outs, first)
+
+
+@pytest.mark.parametrize("dtype,hq,hkv,d,ctx", [(torch.float16, 14, 2, 64, [4000]), (torch.bfloat16, 28, 4, 128, [3000, 37])])
+def test_decode_few_long_sequences_split_over_many_ctas(dev, dtype, hq, hkv, d, ctx):
+    """A batch of one or two long sequences is spread over every CTA, so each is merged from
+    more pieces than the merging CTA can stage at once (the multi-round merge path)."""
+    from mini_inference_b200 import ops
+
+    bs = 16
+    g = torch.Generator().manual_seed(11)
+    nb = sum((c + 1 + bs - 1) // bs for c in ctx) + 1
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, at = [], 0
+    for c in ctx:
+        n = (c + 1 + bs - 1) // bs
+        tables.append(perm[at: at + n])
+        at += n
+    shape = (1, nb + 1, hkv, bs, d)
+    k_pool = torch.randn(shape, generator=g).to(dtype).to(dev)
+    v_pool = torch.randn(shape, generator=g).to(dtype).to(dev)
+    q = torch.randn(len(ctx), hq, d, generator=g).to(dtype).to(dev)
+    kn = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(dev)
+    vn = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(dev)
+    meta = decode_metadata(tables, ctx, bs, max(len(t) for t in tables), pad_block=0)
+    tab = torch.from_numpy(meta["block_tables"].astype(np.int32)).to(dev)
+    ws = torch.zeros(ops.decode_workspace_bytes(len(ctx), hkv, tab.shape[1], bs, d, hq), dtype=torch.uint8,
+                     device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    kp, vp = to_np(k_pool[0]), to_np(v_pool[0])
+    out = ops.decode_attention(ops.make_pool(k_pool, v_pool), 0, ops.make_tables(tab), q,
+                               torch.from_numpy(meta["context_lens"].astype(np.int32)).to(dev), ws, k_new=kn,
+                               v_new=vn, slot_mapping=torch.from_numpy(meta["slot_mapping"]).to(dev), status=status)
+    ops.raise_device_errors(status)
+    name = "float16" if dtype == torch.float16 else "bfloat16"
+    ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
+    assert excess(to_np(out), round_to(ref, name), name) <= 0
