@@ -142,6 +142,29 @@ enum {
 PKV_API int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
                                    int32_t block_size, int32_t head_dim, int32_t num_q_heads);
 
+/* Size of the device array that pkv_decode_attention_static uses as its workspace. */
+#define PKV_DECODE_STATIC_SCRATCH_BYTES (16 * 1024 * 1024)
+
+/*
+ * pkv_decode_attention without a workspace argument; it allocates nothing. No counterpart
+ * in the reference, which gathers each step into fresh tensors: this is for callers that
+ * reach the library over a plain C FFI from a process whose device memory another
+ * allocator owns, and so cannot get a workspace buffer mid-step.
+ * Arguments, results and status words are those of pkv_decode_attention. Its workspace is
+ * one file-scope device array of PKV_DECODE_STATIC_SCRATCH_BYTES per device:
+ *   - a call that would need more returns PKV_ERR_WORKSPACE and launches nothing;
+ *   - every call on a device shares it, so calls that overlap on the GPU (other streams,
+ *     other host threads) race and must be serialised by the caller;
+ *   - the first call on a device looks the array up and clears it on `stream` (the current
+ *     device must be the stream's); make that call before any stream capture.
+ */
+PKV_API int pkv_decode_attention_static(const pkv_pool* pool, int32_t layer, const pkv_tables* tables,
+                                int32_t batch, int32_t num_q_heads, void* out, int64_t out_stride_b,
+                                int64_t out_stride_h, const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                const void* k_new, const void* v_new, int64_t kv_stride_b,
+                                int64_t kv_stride_h, const int64_t* slot_mapping, const int32_t* context_lens,
+                                float scale, int32_t flags, int32_t* status_dev, pkv_stream_t stream);
+
 /*
  * Packed (varlen) prefill attention over the paged cache, prefix-cache hits included.
  * Replaces PackedPrefillContext.attend (engine/kv_cache.py:283-297) after its append:

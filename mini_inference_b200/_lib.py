@@ -28,6 +28,7 @@ PKV_F16 = 0
 PKV_BF16 = 1
 
 PKV_DECODE_INPUTS_READY = 1
+PKV_DECODE_STATIC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 
 class PkvPool(ctypes.Structure):
@@ -56,6 +57,9 @@ SIGNATURES: dict[str, tuple] = {
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                        c_void_p, c_float, c_int32, c_void_p, c_int64, c_void_p, c_void_p]),
     "pkv_decode_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "pkv_decode_attention_static": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64,
+                                              c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+                                              c_int64, c_void_p, c_void_p, c_float, c_int32, c_void_p, c_void_p]),
     "pkv_prefill_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_void_p, c_void_p, c_int32, c_int32,
                                         c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_float, c_void_p,
                                         c_void_p]),

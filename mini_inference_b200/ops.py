@@ -13,7 +13,8 @@ import math
 
 import torch
 
-from ._lib import PKV_BF16, PKV_DECODE_INPUTS_READY, PKV_F16, PkvPool, PkvTables, check, lib
+from ._lib import (PKV_BF16, PKV_DECODE_INPUTS_READY, PKV_DECODE_STATIC_SCRATCH_BYTES, PKV_ERR_WORKSPACE, PKV_F16,
+                   PkvError, PkvPool, PkvTables, check, lib)
 
 _DTYPES = {torch.float16: PKV_F16, torch.bfloat16: PKV_BF16}
 
@@ -113,6 +114,40 @@ def decode_attention(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tens
         k_new.stride(0) if k_new is not None else 0, k_new.stride(1) if k_new is not None else 0,
         _ptr(slot_mapping), context_lens.data_ptr(), scale, PKV_DECODE_INPUTS_READY if inputs_ready else 0,
         ws_ptr, ws_bytes, _ptr(status), _stream()), "decode_attention")
+    return out
+
+
+def decode_attention_static(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tensor,
+                            context_lens: torch.Tensor, out: torch.Tensor, k_new: torch.Tensor | None = None,
+                            v_new: torch.Tensor | None = None, slot_mapping: torch.Tensor | None = None,
+                            scale: float | None = None, status: torch.Tensor | None = None,
+                            inputs_ready: bool = False) -> torch.Tensor:
+    """:func:`decode_attention` through the entry point that allocates nothing.
+
+    The library's static per-device scratch replaces the workspace, and this
+    wrapper allocates nothing either: ``out`` is required, and tensors whose last
+    dimension is strided are refused rather than copied. Calls on one device must
+    not overlap on the GPU (they share the scratch).
+    """
+    _require_cuda(q, context_lens, out, k_new, v_new, slot_mapping)
+    batch, hq, d = q.shape
+    for t in (q, out, k_new, v_new):
+        if t is not None and t.stride(-1) != 1:
+            raise ValueError("decode_attention_static copies nothing: the last dimension must be contiguous")
+    if k_new is not None and k_new.stride() != v_new.stride():
+        raise ValueError("k_new and v_new must have the same strides")
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    status_code = lib.pkv_decode_attention_static(
+        ctypes.byref(pool), layer, ctypes.byref(tables), batch, hq, out.data_ptr(), out.stride(0), out.stride(1),
+        q.data_ptr(), q.stride(0), q.stride(1), _ptr(k_new), _ptr(v_new),
+        k_new.stride(0) if k_new is not None else 0, k_new.stride(1) if k_new is not None else 0,
+        _ptr(slot_mapping), context_lens.data_ptr(), scale, PKV_DECODE_INPUTS_READY if inputs_ready else 0,
+        _ptr(status), _stream())
+    if status_code == PKV_ERR_WORKSPACE:
+        raise PkvError(status_code, f"decode_attention_static: this launch needs more than the "
+                                    f"{PKV_DECODE_STATIC_SCRATCH_BYTES} bytes of static scratch; "
+                                    "use decode_attention with a workspace")
+    check(status_code, "decode_attention_static")
     return out
 
 
