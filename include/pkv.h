@@ -4,8 +4,7 @@
  * Every entry point takes plain pointers, sizes and strides (in elements),
  * returns an int status (PKV_OK == 0) and never allocates device memory:
  * the caller owns the KV pool, the inputs, the outputs and any workspace.
- * Kernels are enqueued on the given stream and never synchronise the host,
- * so every launch can be captured in a CUDA graph.
+ * Kernels are enqueued on the given stream and never synchronise the host.
  *
  * The reference (Ham12-3/mini-inference) is pure Python/PyTorch; each entry
  * point names the reference code it replaces. A Python binding (ctypes) is
@@ -114,10 +113,10 @@ PKV_API int pkv_kv_append(const pkv_pool* pool, int32_t layer, const void* k_new
  *   context_lens[b]: keys row b attends to (its position + 1), 1..tables->cols*block_size
  *   scale   : softmax scale (the reference uses 1/sqrt(head_dim))
  *   flags   : PKV_DECODE_INPUTS_READY or 0 (see below)
- *   workspace: >= pkv_decode_workspace_bytes(...) bytes, 256-byte aligned, zeroed once
- *             before first use; the kernel leaves it ready for the next call, whatever
- *             the next call's batch or table width. Calls that share a workspace must
- *             not overlap on the GPU. batch * num_kv_heads <= 65536.
+ *   workspace: >= pkv_decode_workspace_bytes(...) bytes, 256-byte aligned; needs no
+ *             initialisation (a call writes every word it reads). Calls that share a
+ *             workspace must not overlap on the GPU.
+ * Launches two kernels on `stream`: the attention and the merge of split sequences.
  * Query head h reads KV head h / (num_q_heads / num_kv_heads), as the reference's regrouping.
  */
 PKV_API int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,

@@ -31,9 +31,11 @@
 // of a head merge their softmax states through shared memory (a named barrier
 // per head). A piece that is a whole sequence is written out directly; only the
 // first and the last piece of a run can be partial, so a CTA keeps at most two
-// partial states per head in the workspace. The last CTA of a split sequence to
-// finish (an atomic ticket per sequence; no CTA ever waits for another) merges
-// its pieces in run order, so the result does not depend on which CTA came last.
+// partial states per head in the workspace. A second, small kernel launched right
+// behind (programmatic dependent launch: it is resident early and waits on the
+// decode grid) merges the pieces of each split sequence in run order; the CTA that
+// holds a sequence's first piece leaves it a descriptor. No CTA waits on another
+// and there are no atomics, so nothing in the workspace carries over between calls.
 #include <algorithm>
 #include <cstdlib>
 
@@ -48,7 +50,6 @@ constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
 constexpr int kMaxBatch = 1024;  // the prefix sums live in shared memory
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int64_t kMaxTickets = 65536;
 
 // D: head_dim, NH: KV heads (all in one tile), RK: rows kept per head (8 or 16 >= group),
 // DEEP: one CTA per SM with up to 6 ring stages per consumer warp.
@@ -71,7 +72,7 @@ template <int D, int NH, int RK, bool DEEP = false> struct DecodeShape {
                                  : (PW_HALF >= 2 ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > 3 ? 3 : PW_FULL));
   static constexpr int S = WPH * PW;
   static constexpr int RING = 2 * S * STAGE;
-  static constexpr int SMEM = 1024 + RING + COMB + (2 * S + 2) * 8 + PREFIX;
+  static constexpr int SMEM = 1024 + RING + COMB + 2 * S * 8 + PREFIX;
   static constexpr int MIN_BLOCKS = 2 * (SMEM + 1024) <= 228 * 1024 ? 2 : 1;  // CTAs per SM to plan registers for
   static_assert(PW >= 2, "ring too shallow");
 };
@@ -88,7 +89,7 @@ struct DecodeParams {
   const int32_t* seq_rows;
   const int32_t* context_lens;
   int32_t* status;
-  int32_t* counters;
+  int4* desc;        // [ctas] split sequence owned by each CTA: (sequence, pieces, first slot) or -1
   float* partials;  // [ctas][2][NH][RK][D + 4]: (m, l, pad, pad, O) per row
   int64_t out_sb, out_sh, q_sb, q_sh, kv_sb, kv_sh, table_stride;
   int32_t table_rows, table_cols;
@@ -130,11 +131,9 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
   float* comb = reinterpret_cast<float*>(smem + S::RING);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::COMB);
   uint64_t* empty = full + NS;
-  uint64_t* merge_bar = empty + NS;              // completion of the merge's bulk copies
-  int* sP = reinterpret_cast<int*>(merge_bar + 2);  // [batch + 1] block prefix sums
+  int* sP = reinterpret_cast<int*>(empty + NS);  // [batch + 1] block prefix sums
   int* sCtx = sP + kMaxBatch + 1;                // [batch] clamped context lengths
   int* sRow = sCtx + kMaxBatch + 1;              // [batch] block-table row of each sequence
-  __shared__ int s_combine[2];
   __shared__ int s_bad;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -189,10 +188,8 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], NH);  // one consumer warp per head releases each stage
     }
-    mbar_init(merge_bar, 1);
     fence_mbar_init();
     s_bad = 0;
-    s_combine[0] = s_combine[1] = -1;
   }
   __syncthreads();
 
@@ -207,7 +204,13 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
       for (int e = lane; e < NH * G * D; e += 32) o[(e / D) * p.out_sh + e % D] = Dt<T>::from_f(0.f);
     }
   }
-  if (g >= ctas) return;
+  if (g >= ctas) {  // no tiles: only say so to the merge kernel (after the previous one read its copy)
+    if (tid == 0) {
+      grid_dep_wait();
+      p.desc[g] = make_int4(-1, 0, 0, 0);
+    }
+    return;
+  }
   // Tile j of the run is consumed, for every head, by warp j % WPH of that head, whose
   // private stages are w * PW .. w * PW + PW - 1. A warp therefore waits on every phase
   // of its stages in order (an mbarrier parity wait is only unambiguous within one phase
@@ -388,183 +391,89 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
           if (col == 0) __stcg(reinterpret_cast<float2*>(part + r * ROW), make_float2(mm, ll));
         }
       }
-      if (!whole && w == 0 && lane == 0) s_combine[slot_kind] = b;
       named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next piece
     }
     if (!ok) s_bad = 1;
   }
   __syncthreads();
-  if (s_bad) return;
-
-  // Tickets for this run's split sequences; the last CTA of each merges its pieces.
-  // The barrier orders the CTA's partial writes before thread 0's release fence; the last
-  // ticket holder's acquire fence orders them before its CTA's reads (fence-fence
-  // synchronisation through the ticket atomics, cheaper than sequentially consistent fences).
-  auto cta_of = [&](int t) { return (int)(((int64_t)(t + 1) * ctas - 1) / total); };
-  if (tid == 0 && (s_combine[0] >= 0 || s_combine[1] >= 0)) {
-    fence_acq_rel_gpu();
-    int ticket[2] = {-1, -1};
-    for (int k = 0; k < 2; ++k)  // both in flight together
-      if (s_combine[k] >= 0) ticket[k] = atomicAdd(p.counters + s_combine[k], 1);
-    bool last_any = false;
-    for (int k = 0; k < 2; ++k) {
-      const int b = s_combine[k];
-      if (b < 0) continue;
-      const int pieces = cta_of(sP[b + 1] - 1) - cta_of(sP[b]) + 1;
-      if (ticket[k] == pieces - 1) {
-        p.counters[b] = 0;  // ready for the next call
-        last_any = true;
-      } else {
-        s_combine[k] = -1;
-      }
+  // Hand the split sequence whose first piece ends this run to the merge kernel: this CTA
+  // owns it when the run's last tile belongs to a sequence that started inside the run and
+  // continues past it. Every CTA rewrites its descriptor on every call.
+  if (tid == 0) {
+    int4 d = make_int4(-1, 0, 0, 0);
+    const int b = seq_of(sP, B, t1 - 1);
+    if (!s_bad && sP[b] >= t0 && sP[b + 1] > t1) {
+      const int last_cta = (int)(((int64_t)sP[b + 1] * ctas - 1) / total);  // CTA of tile sP[b + 1] - 1
+      d = make_int4(b, last_cta - g + 1, sP[b] == t0 ? 0 : 1, 0);
     }
-    if (last_any) fence_acq_rel_gpu();
-  }
-  __syncthreads();
-  // Merge every sequence this CTA got the last ticket of. Piece pc of a sequence is CTA
-  // g_first + pc; every piece but the first starts its CTA's run (slot 0); the first is
-  // its CTA's last piece (slot 1) unless that run also starts with the sequence. The
-  // pieces' states of every pending merge are copied into the (now idle) ring with one
-  // round of independent 16-byte loads, then merged from shared memory; sequences split
-  // into more pieces than the ring holds go through it in several rounds.
-  const int nmerge = (s_combine[0] >= 0) + (s_combine[1] >= 0);
-  if (nmerge == 0) return;
-  int mb[2] = {0, 0}, mfirst[2] = {0, 0}, mnp[2] = {0, 0}, mkind0[2] = {0, 0};
-  for (int k = 0, m = 0; k < 2; ++k) {
-    if (s_combine[k] < 0) continue;
-    const int b = s_combine[k];
-    mb[m] = b;
-    mfirst[m] = cta_of(sP[b]);
-    mnp[m] = cta_of(sP[b + 1] - 1) - mfirst[m] + 1;
-    mkind0[m] = (int)((int64_t)total * mfirst[m] / ctas) >= sP[b] ? 0 : 1;
-    ++m;
-  }
-  constexpr int PIECE = NH * SLOT;             // floats of one piece (all heads)
-  constexpr int CAP = S::RING / (PIECE * 4);  // pieces the ring holds
-  static_assert(CAP >= 2, "ring too small to stage merge pieces");
-  float* stage = reinterpret_cast<float*>(smem);
-  const int per_seq = NH * G * (D / 2);
-  auto piece_src = [&](int m, int pc) {
-    const int kind = pc == 0 ? mkind0[m] : 0;
-    return p.partials + (int64_t)((mfirst[m] + pc) * 2 + kind) * PIECE;
-  };
-  // Pieces pc0.. of merge m -> stage slots q0..: one bulk copy per piece, issued by one
-  // thread, all completing on merge_bar (the other CTAs' partials were published with
-  // release fences and acquired above; the proxy fence orders that for the copy engine).
-  // stage_wait() waits for the round's bytes; every thread takes part, each round flips
-  // the barrier's phase.
-  int merge_phase = 0;
-  auto stage_pieces = [&](int m, int pc0, int cnt, int q0, uint32_t& bytes) {
-    if (tid == 0) {
-      for (int q = 0; q < cnt; ++q) {
-        bulk_load(stage + (q0 + q) * PIECE, piece_src(m, pc0 + q), PIECE * 4, merge_bar);
-      }
-    }
-    bytes += cnt * PIECE * 4;
-  };
-  auto stage_start = [&](uint32_t bytes) {
-    if (tid == 0) {
-      fence_proxy_async_global();
-      mbar_arrive_expect_tx(merge_bar, bytes);
-    }
-  };
-  auto stage_wait = [&]() {
-    if (!mbar_wait_until(merge_bar, merge_phase & 1, global_ns() + kWaitBudgetNs)) report(p.status, PKV_ERR_TIMEOUT);
-    ++merge_phase;
-  };
-  auto item_of = [&](int rest, int& h, int& r, int& col) {
-    h = rest / (G * (D / 2));
-    r = (rest / (D / 2)) % G;
-    col = 2 * (rest % (D / 2));
-  };
-  auto store = [&](int m, int h, int r, int col, float o0, float o1) {
-    T* outp = reinterpret_cast<T*>(p.out) + mb[m] * p.out_sb + (int64_t)h * G * p.out_sh;
-    *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + col) = Dt<T>::pack(o0, o1);
-  };
-
-  if (mnp[0] + mnp[1] <= CAP) {
-    // Common case: every piece of every pending merge fits; one round of loads.
-    stage_start((mnp[0] + mnp[1]) * PIECE * 4);
-    uint32_t bytes = 0;
-    stage_pieces(0, 0, mnp[0], 0, bytes);
-    if (nmerge > 1) stage_pieces(1, 0, mnp[1], mnp[0], bytes);
-    stage_wait();
-    for (int it = tid; it < nmerge * per_seq; it += blockDim.x) {
-      const int m = it / per_seq;
-      int h, r, col;
-      item_of(it % per_seq, h, r, col);
-      const float* base = stage + (m == 0 ? 0 : mnp[0]) * PIECE + h * SLOT + r * ROW;
-      float mm = -INFINITY;
-      for (int q = 0; q < mnp[m]; ++q) mm = fmaxf(mm, base[q * PIECE]);
-      float ll = 0.f, o0 = 0.f, o1 = 0.f;
-      for (int q = 0; q < mnp[m]; ++q) {
-        const float* row = base + q * PIECE;
-        const float f = row[0] == -INFINITY ? 0.f : ex2(row[0] - mm);
-        ll += row[1] * f;
-        o0 += row[4 + col] * f;
-        o1 += row[5 + col] * f;
-      }
-      const float inv = 1.f / ll;
-      store(m, h, r, col, o0 * inv, o1 * inv);
-    }
-    return;
-  }
-  // A sequence split into more pieces than the ring holds: merge one sequence at a time,
-  // a few items per thread, the pieces in rounds of CAP with a running max / sum.
-  constexpr int kMaxItems = 4;
-  for (int m = 0; m < nmerge; ++m) {
-    for (int ibase = 0; ibase < per_seq; ibase += kMaxItems * blockDim.x) {
-      float run_m[kMaxItems], run_l[kMaxItems], acc0[kMaxItems], acc1[kMaxItems];
-#pragma unroll
-      for (int u = 0; u < kMaxItems; ++u) run_m[u] = -INFINITY, run_l[u] = acc0[u] = acc1[u] = 0.f;
-      for (int done = 0; done < mnp[m]; done += CAP) {
-        const int cnt = min(CAP, mnp[m] - done);
-        stage_start(cnt * PIECE * 4);
-        uint32_t bytes = 0;
-        stage_pieces(m, done, cnt, 0, bytes);
-        stage_wait();
-#pragma unroll
-        for (int u = 0; u < kMaxItems; ++u) {
-          const int it = ibase + tid + u * blockDim.x;
-          if (it >= per_seq) break;
-          int h, r, col;
-          item_of(it, h, r, col);
-          const float* base = stage + h * SLOT + r * ROW;
-          float mm = run_m[u];
-          for (int q = 0; q < cnt; ++q) mm = fmaxf(mm, base[q * PIECE]);
-          const float f_old = run_m[u] == -INFINITY ? 0.f : ex2(run_m[u] - mm);
-          run_l[u] *= f_old;
-          acc0[u] *= f_old;
-          acc1[u] *= f_old;
-          for (int q = 0; q < cnt; ++q) {
-            const float* row = base + q * PIECE;
-            const float f = row[0] == -INFINITY ? 0.f : ex2(row[0] - mm);
-            run_l[u] += row[1] * f;
-            acc0[u] += row[4 + col] * f;
-            acc1[u] += row[5 + col] * f;
-          }
-          run_m[u] = mm;
-        }
-        __syncthreads();  // the staging area is refilled by the next round
-      }
-#pragma unroll
-      for (int u = 0; u < kMaxItems; ++u) {
-        const int it = ibase + tid + u * blockDim.x;
-        if (it >= per_seq) break;
-        int h, r, col;
-        item_of(it, h, r, col);
-        const float inv = 1.f / run_l[u];
-        store(m, h, r, col, acc0[u] * inv, acc1[u] * inv);
-      }
-    }
+    p.desc[g] = d;
   }
 }
 
-// Workspace: [counters: kMaxTickets int32][partials: ctas * 2 * NH * RK * (D + 4) float].
-// Counters are indexed by sequence and are back at zero when a call ends.
-constexpr int64_t kPartialsOffset = kMaxTickets * 4;
-int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (int64_t)ctas * 2 * nh * rk * (d + 4) * 4; }
+// Merges the pieces of every split sequence, one CTA per possible owner (the decode
+// kernel's CTA g writes descriptor g). Pieces are combined in run order with the
+// running-max rescaling of the flash step, so the result does not depend on timing.
+// Each thread takes (head, row, 4 columns) items and loads up to 8 pieces' states at a
+// time, all independent, so a merge of up to 8 pieces costs one round trip to L2.
+constexpr int kMergeThreads = 512;
+
+template <typename T, int D, int NH, int RK>
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const DecodeParams p) {
+  constexpr int ROW = D + 4;
+  constexpr int SLOT = RK * ROW;
+  grid_dep_launch_dependents();
+  grid_dep_wait();  // the decode kernel's pieces and descriptors
+  const int4 d = __ldcg(&p.desc[blockIdx.x]);
+  if (d.x < 0) return;
+  const int b = d.x, np = d.y, kind0 = d.z, first = blockIdx.x;
+  const int G = p.group;
+  const int items = NH * G * (D / 4);
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int c = (it % (D / 4)) * 4;
+    const int r = (it / (D / 4)) % G;
+    const int h = it / (G * (D / 4));
+    float mx = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int q0 = 0; q0 < np; q0 += 8) {
+      const int cnt = min(8, np - q0);
+      float2 ml[8];
+      float4 o[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (u < cnt) {
+          const int q = q0 + u;
+          const float* row = p.partials + ((int64_t)((first + q) * 2 + (q == 0 ? kind0 : 0)) * NH + h) * SLOT + r * ROW;
+          ml[u] = __ldcg(reinterpret_cast<const float2*>(row));
+          o[u] = __ldcg(reinterpret_cast<const float4*>(row + 4 + c));
+        }
+      }
+      float mn = mx;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (u < cnt) mn = fmaxf(mn, ml[u].x);
+      const float fo = mx == -INFINITY ? 0.f : ex2(mx - mn);
+      l *= fo, a0 *= fo, a1 *= fo, a2 *= fo, a3 *= fo;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (u < cnt) {
+          const float f = ml[u].x == -INFINITY ? 0.f : ex2(ml[u].x - mn);
+          l += ml[u].y * f;
+          a0 += o[u].x * f, a1 += o[u].y * f, a2 += o[u].z * f, a3 += o[u].w * f;
+        }
+      }
+      mx = mn;
+    }
+    const float inv = 1.f / l;
+    T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)(h * G + r) * p.out_sh + c;
+    *reinterpret_cast<uint32_t*>(outp) = Dt<T>::pack(a0 * inv, a1 * inv);
+    *reinterpret_cast<uint32_t*>(outp + 2) = Dt<T>::pack(a2 * inv, a3 * inv);
+  }
+}
+
+// Workspace: [descriptors: kMaxCtas int4][partials: ctas * 2 * NH * RK * (D + 4) float].
+// Both are written before they are read within a call; nothing carries over between calls.
 constexpr int kMaxCtas = 4 * 256;  // workspace is sized for up to 4 CTAs on each of up to 256 SMs
+constexpr int64_t kPartialsOffset = (int64_t)kMaxCtas * 16;
+int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (int64_t)ctas * 2 * nh * rk * (d + 4) * 4; }
 
 // Tuning knobs, read once from the environment (0 / unset = built-in choice):
 //   PKV_DECODE_CTAS_PER_SM  CTAs per SM (at most what the shared memory allows)
@@ -608,7 +517,7 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   if (!get_pool_maps(pool, &tk, &tv, NH)) return PKV_ERR_CUDA;
   DecodeParams p = p0;
   uint8_t* wsb = static_cast<uint8_t*>(workspace);
-  p.counters = reinterpret_cast<int32_t*>(wsb);
+  p.desc = reinterpret_cast<int4*>(wsb);
   p.partials = reinterpret_cast<float*>(wsb + kPartialsOffset);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);
@@ -620,7 +529,13 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = knobs().pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, DEEP>, tk, tv, p));
+  const int st = cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, DEEP>, tk, tv, p));
+  if (st != PKV_OK) return st;
+  // The merge of split sequences: one small CTA per decode CTA, launched behind it (with
+  // programmatic serialization it is resident early and waits on the decode grid).
+  cfg.blockDim = dim3(kMergeThreads);
+  cfg.dynamicSmemBytes = 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, D, NH, RK>, p));
 }
 
 template <typename T, int D, int NH>
