@@ -54,7 +54,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode tok/s on 200-req mixed workload; paged-attn KV GB/s vs HBM peak"
 UNIT = "GB/s"
 LAYERS, BATCH, CTX_LO, CTX_HI = 24, 64, 128, 2048
-DECODE_KERNELS = 2  # kernels per pkv_decode_attention call: the attention and the split-sequence merge
+DECODE_KERNELS = 1  # kernels per pkv_decode_attention call
 HQ, HKV, D, BS, NUM_BLOCKS = 14, 2, 64, 16, 16384
 ELT = 2  # fp16 bytes
 
@@ -294,8 +294,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": f"{peak_kind} copy bandwidth",
                      "traffic": traffic, "algorithmic_bytes_per_launch": call_bytes,
-                     "kernel": "pkv decode_kernel<half,64> (fused append + split-K paged attention) "
-                               "+ decode_merge_kernel, per layer call",
+                     "kernel": "pkv decode_kernel<half,64> (fused append + paged attention, split items merged)",
                      "launch_us": round(per_launch_ms * 1e3, 3)},
         "e2e": {"value": round(world * step_bytes * args.e2e_steps / (ms_e2e_job * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -113,10 +113,10 @@ PKV_API int pkv_kv_append(const pkv_pool* pool, int32_t layer, const void* k_new
  *   context_lens[b]: keys row b attends to (its position + 1), 1..tables->cols*block_size
  *   scale   : softmax scale (the reference uses 1/sqrt(head_dim))
  *   flags   : PKV_DECODE_INPUTS_READY or 0 (see below)
- *   workspace: >= pkv_decode_workspace_bytes(...) bytes, 256-byte aligned; needs no
- *             initialisation (a call writes every word it reads). Calls that share a
- *             workspace must not overlap on the GPU.
- * Launches two kernels on `stream`: the attention and the merge of split sequences.
+ *   workspace: >= pkv_decode_workspace_bytes(...) bytes, 256-byte aligned, zeroed once
+ *             before first use; every call leaves it ready for the next, whatever the
+ *             next call's batch or table width. Calls that share a workspace must not
+ *             overlap on the GPU. num_kv_heads <= 16.
  * Query head h reads KV head h / (num_q_heads / num_kv_heads), as the reference's regrouping.
  */
 PKV_API int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,

@@ -150,6 +150,14 @@ __device__ inline void cp_async_wait_all() {
 
 // Acquire-release fence at GPU scope (cheaper than the sequentially consistent __threadfence).
 __device__ inline void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ inline int ld_acquire_gpu(const int32_t* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ inline void st_relaxed_gpu(int32_t* ptr, int v) {
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
 
 __device__ inline void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -6,36 +6,32 @@
 // (engine/model.py:126-147). Here nothing is gathered: K/V blocks are read in
 // place through the block table, each exactly once, straight into shared memory.
 //
-// Work split: one wave of CTAs that share the batch's blocks evenly. A "tile" is
-// one block of one sequence with all its KV heads (K and V of all heads of a
-// block are adjacent in the pool, so one 5-D TMA box per tensor fetches them).
-// The batch's tiles, sequence after sequence, are cut into equal runs, one per
-// CTA (every CTA computes the prefix sums of the per-sequence block counts from
-// context_lens), so every CTA streams the same number of bytes whatever the mix
-// of lengths.
+// Work split. An "item" is one KV head of one sequence: that head's K/V blocks and
+// the GQA group of query heads that reads them. A CTA takes one unit of work, an
+// item or a chunk of one, and streams its blocks once. Items longer than
+//   cap = max(kMinCap, ceil(T / max(C - I, C / 4)))
+// (T: the batch's (block, head) tiles, C: CTAs, I: items) are cut into
+// ceil(n / cap) balanced chunks of consecutive blocks, so that, when the items
+// allow it, all units fit one wave of CTAs and no unit is much longer than the
+// mean. Every CTA derives the same split from context_lens in its prologue; with
+// more units than CTAs, CTA g takes units g, g + C, ... The CTA that finishes the
+// last chunk of an item (an atomic ticket per item; no CTA waits for another)
+// merges the chunks' partial softmax states in chunk order, so the result does
+// not depend on which CTA came last.
 //
-// Inside a CTA one producer warp walks its run, resolves each tile's block id
-// through the block table (32 at a time, one lookup per lane, the next 32
-// already in flight) and keeps a ring of stages full with TMA copies (128B
-// swizzle, L2 evict-first). 8 consumer warps split the KV heads (8 / Hkv warps
-// per head) and take the run's tiles round-robin, each through stages of the
-// ring that only it consumes, so that it waits on every phase of those stages'
-// mbarriers in turn (a parity wait cannot tell a phase from the one two later).
-// Each consumer runs the 16-key flash
-// step on mma.sync m16n8k16 with the M = 16 rows being the GQA group's query
-// heads (the reference regroups head h to (h / group, h % group) the same
-// way), so a tile read from HBM serves the whole group (attn_tile.cuh), then
-// hands the stage back to the producer through an mbarrier.
-//
-// A run covers pieces of consecutive sequences. At the end of a piece the warps
-// of a head merge their softmax states through shared memory (a named barrier
-// per head). A piece that is a whole sequence is written out directly; only the
-// first and the last piece of a run can be partial, so a CTA keeps at most two
-// partial states per head in the workspace. A second, small kernel launched right
-// behind (programmatic dependent launch: it is resident early and waits on the
-// decode grid) merges the pieces of each split sequence in run order; the CTA that
-// holds a sequence's first piece leaves it a descriptor. No CTA waits on another
-// and there are no atomics, so nothing in the workspace carries over between calls.
+// Inside a CTA one producer warp resolves block ids through the block table (32
+// at a time, one lookup per lane, the next 32 already in flight) and keeps a ring
+// of stages full with TMA copies of one head's K and V tiles (128B swizzle, L2
+// evict-first). kIssueLanes lanes issue the copies of consecutive tiles with one
+// instruction: the issue rate of a single lane does not keep HBM busy with copies
+// of 2-4 KB. Tile j of the CTA's stream goes to consumer warp j % 8 through stage
+// j % S (S a multiple of 8), so every stage has one consumer, which waits on each
+// phase of it in turn (an mbarrier parity wait cannot tell a phase from the one two
+// later). Each consumer runs the 16-key flash step on mma.sync m16n8k16 with the
+// M = 16 rows being the GQA group's query heads (the reference regroups head h to
+// (h / group, h % group) the same way), so a tile read from HBM serves the whole
+// group (attn_tile.cuh). At the end of a unit the 8 warps merge their softmax
+// states through shared memory.
 #include <algorithm>
 #include <cstdlib>
 
@@ -48,33 +44,35 @@ namespace {
 constexpr int kBS = 16;  // tokens per block handled by this kernel
 constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
-constexpr int kMaxBatch = 1024;  // the prefix sums live in shared memory
+constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared memory
+constexpr int kMaxKvHeads = 16;    // ticket counters are indexed by (sequence, KV head)
+constexpr int kMinCap = 16;        // items of up to 16 blocks are never split
+constexpr int kIssueLanes = 4;     // producer lanes issuing copies together
+constexpr int kMergeBatch = 4;     // chunk states a merging thread loads at once
+constexpr int kMaxPending = 8;     // split units of one CTA whose tickets are taken at the end
 constexpr float kLog2e = 1.4426950408889634f;
 
-// D: head_dim, NH: KV heads (all in one tile), RK: rows kept per head (8 or 16 >= group),
-// DEEP: one CTA per SM with up to 6 ring stages per consumer warp.
-template <int D, int NH, int RK, bool DEEP = false> struct DecodeShape {
-  static constexpr int TILE = kBS * D * 2;  // one head's K (or V) for one block
-  static constexpr int STAGE = NH * TILE;   // K (or V) of all heads of one block
-  static constexpr int WPH = kNC / NH;      // consumer warps per KV head
-  static constexpr int DP = D + 4;          // padded combine row (no bank conflicts)
-  static constexpr int WARP_COMB = 2 * RK + RK * DP;        // floats: m[RK], l[RK], O[RK][DP]
-  static constexpr int COMB = NH * WPH * WARP_COMB * 4;     // bytes
-  static constexpr int PREFIX = 3 * (kMaxBatch + 1) * 4;    // block prefix sums, context lengths, table rows
-  // Each consumer warp owns PW stages of the ring (see decode_kernel): S = WPH * PW.
-  // Two CTAs per SM when every warp keeps at least 2 stages in half the shared memory,
-  // otherwise one CTA with up to 3 stages per warp.
-  static constexpr int HALF = 113 * 1024 - 1024 - COMB - PREFIX - 256;
-  static constexpr int FULL = 226 * 1024 - 1024 - COMB - PREFIX - 256;
-  static constexpr int PW_HALF = HALF / (2 * STAGE) / WPH;
-  static constexpr int PW_FULL = FULL / (2 * STAGE) / WPH;
-  static constexpr int PW = DEEP ? (PW_FULL > 6 ? 6 : PW_FULL)
-                                 : (PW_HALF >= 2 ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > 3 ? 3 : PW_FULL));
-  static constexpr int S = WPH * PW;
-  static constexpr int RING = 2 * S * STAGE;
-  static constexpr int SMEM = 1024 + RING + COMB + 2 * S * 8 + PREFIX;
-  static constexpr int MIN_BLOCKS = 2 * (SMEM + 1024) <= 228 * 1024 ? 2 : 1;  // CTAs per SM to plan registers for
-  static_assert(PW >= 2, "ring too shallow");
+// D: head_dim, RK: rows kept per item (8 or 16 >= group size), DEEP: one CTA per SM
+// with up to 6 stages per consumer warp.
+template <int D, int RK, bool DEEP = false> struct DecodeShape {
+  static constexpr int TILE = kBS * D * 2;             // one head's K (or V) of one block
+  static constexpr int DP = D + 4;                     // padded combine row (no bank conflicts)
+  static constexpr int WARP_STATE = 2 * RK + RK * DP;  // floats: m[RK], l[RK], O[RK][DP]
+  static constexpr int COMB = kNC * WARP_STATE * 4;
+  static constexpr int TABLES = 4 * (kMaxBatch + 1) * 4;  // context lengths, table rows, unit and split prefixes
+  static constexpr int FIXED = 1024 + COMB + TABLES + 256;
+  // Two CTAs per SM when each consumer warp keeps 2+ stages in half the shared
+  // memory, else one CTA with up to 4 stages per warp.
+  static constexpr int PW_HALF = (113 * 1024 - FIXED) / (2 * TILE * kNC);
+  static constexpr int PW_FULL = (226 * 1024 - FIXED) / (2 * TILE * kNC);
+  static constexpr bool TWO = !DEEP && PW_HALF >= 2;
+  static constexpr int PW_MAX_ONE = DEEP ? 6 : 4;
+  static constexpr int PW = TWO ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > PW_MAX_ONE ? PW_MAX_ONE : PW_FULL);
+  static constexpr int S = kNC * PW;
+  static constexpr int RING = 2 * S * TILE;
+  static constexpr int SMEM = 1024 + RING + COMB + 2 * S * 8 + TABLES;
+  static constexpr int MIN_BLOCKS = TWO ? 2 : 1;
+  static_assert(PW >= 1, "ring too shallow");
 };
 
 struct DecodeParams {
@@ -89,23 +87,13 @@ struct DecodeParams {
   const int32_t* seq_rows;
   const int32_t* context_lens;
   int32_t* status;
-  int4* desc;        // [ctas] split sequence owned by each CTA: (sequence, pieces, first slot) or -1
-  float* partials;  // [ctas][2][NH][RK][D + 4]: (m, l, pad, pad, O) per row
+  int32_t* counters;  // [kMaxBatch * kMaxKvHeads] chunks of each item finished so far
+  float* partials;    // [max_slots][RK][D + 4]: (m, l, pad, pad, O) per row of a chunk
   int64_t out_sb, out_sh, q_sb, q_sh, kv_sb, kv_sh, table_stride;
   int32_t table_rows, table_cols;
-  int32_t batch, group, layer, nbt, inputs_ready;
+  int32_t batch, group, kv_heads, layer, nbt, inputs_ready, max_slots, cap_override;
   float scale_log2;
 };
-
-// Largest b in [0, n) with p[b] <= t (p non-decreasing, p[0] = 0 <= t).
-__device__ inline int seq_of(const int* p, int n, int t) {
-  int lo = 0, hi = n - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (p[mid] <= t) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
 
 __device__ inline void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -115,31 +103,54 @@ __device__ inline void mbar_arrive(uint64_t* bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <typename T, int D, int NH, int RK, bool DEEP>
-__global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BLOCKS) decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
-                                                          const __grid_constant__ CUtensorMap tmap_v,
-                                                          const DecodeParams p) {
-  using S = DecodeShape<D, NH, RK, DEEP>;
-  constexpr int TILE = S::TILE, STAGE = S::STAGE, NS = S::S, WPH = S::WPH, PW = S::PW, DP = S::DP;
-  constexpr int WC = S::WARP_COMB;
-  constexpr int ROW = D + 4;          // partial row: m, l, 2 pad floats, O[D] (O 16-byte aligned)
-  constexpr int SLOT = RK * ROW;      // floats of one partial state of one head
+__device__ inline int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Inclusive scan over the warp.
+__device__ inline int warp_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  return v;
+}
+
+struct Unit {
+  int b, h, c, nch, i0, i1;
+};
+
+template <typename T, int D, int RK, bool DEEP>
+__global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS)
+    decode_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                  const DecodeParams p) {
+  using S = DecodeShape<D, RK, DEEP>;
+  constexpr int TILE = S::TILE, NS = S::S, DP = S::DP, WS = S::WARP_STATE;
+  constexpr int ROW = D + 4;      // partial row: m, l, 2 pad floats, O[D] (O 16-byte aligned)
+  constexpr int SLOT = RK * ROW;  // floats of one chunk's partial state
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring_k = smem;
-  uint8_t* ring_v = smem + NS * STAGE;
+  uint8_t* ring_v = smem + NS * TILE;
   float* comb = reinterpret_cast<float*>(smem + S::RING);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::COMB);
   uint64_t* empty = full + NS;
-  int* sP = reinterpret_cast<int*>(empty + NS);  // [batch + 1] block prefix sums
-  int* sCtx = sP + kMaxBatch + 1;                // [batch] clamped context lengths
-  int* sRow = sCtx + kMaxBatch + 1;              // [batch] block-table row of each sequence
-  __shared__ int s_bad;
+  int* sCtx = reinterpret_cast<int*>(empty + NS);  // [batch] clamped context lengths
+  int* sRow = sCtx + kMaxBatch + 1;                // [batch] block-table row of each sequence
+  int* sPU = sRow + kMaxBatch + 1;                 // [batch + 1] units (per KV head) before sequence b
+  int* sPS = sPU + kMaxBatch + 1;                  // [batch + 1] split units (per KV head) before b
+  __shared__ int s_bad, s_npend;
+  __shared__ int4 s_pend[kMaxPending];  // (sequence, KV head, chunks, first slot) of split units
+  __shared__ int s_last[kMaxPending];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g_lane = lane >> 2, t4 = lane & 3;
-  const int B = p.batch, G = p.group;
-  const int cap = p.table_cols * kBS;
+  const int B = p.batch, G = p.group, HKV = p.kv_heads;
+  const int C = gridDim.x, g = blockIdx.x;
+  const int cap_tokens = p.table_cols * kBS;
 
   // With programmatic dependent launch this CTA may start while the previous kernel in
   // the stream drains; let the next kernel launch early too. Everything the previous
@@ -151,14 +162,12 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
   grid_dep_launch_dependents();
   if (!p.inputs_ready) grid_dep_wait();
 
-  // Every thread fetches some context lengths and table rows (independent loads, one
-  // round trip for the whole batch); warp 0 then scans them in shared memory.
   for (int i = tid; i < B; i += blockDim.x) {
     int ctx = p.context_lens[i];
     int row = p.seq_rows ? p.seq_rows[i] : i;
-    if (ctx > cap) {
+    if (ctx > cap_tokens) {
       report(p.status, PKV_ERR_OUT_OF_RANGE);
-      ctx = cap;
+      ctx = cap_tokens;
     }
     if (row >= p.table_rows) {
       report(p.status, PKV_ERR_OUT_OF_RANGE);
@@ -167,132 +176,154 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
     sCtx[i] = max(ctx, 0);
     sRow[i] = row;
   }
-  __syncthreads();
-  if (warp == 0) {  // prefix sums of the per-sequence block counts
-    int carry = 0;
-    for (int base = 0; base < B; base += 32) {
-      const int i = base + lane;
-      int v = i < B ? (sCtx[i] + kBS - 1) / kBS : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += u;
-      }
-      if (i < B) sP[i + 1] = carry + v;
-      carry += __shfl_sync(0xffffffffu, v, 31);
-    }
-    if (lane == 0) sP[0] = 0;
-  }
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], NH);  // one consumer warp per head releases each stage
+      mbar_init(&empty[i], 1);
     }
     fence_mbar_init();
     s_bad = 0;
+    s_npend = 0;
   }
   __syncthreads();
-
-  const int total = sP[B];
-  const int ctas = min((int)gridDim.x, max(total, 1));  // every working CTA gets at least one tile
-  const int g = blockIdx.x;
-  if (g == 0) {  // sequences with nothing to attend to get zeros (the reference never asks for this)
-    grid_dep_wait();
-    for (int b = warp; b < B; b += kNC + 1) {
-      if (sCtx[b] != 0) continue;
-      T* o = reinterpret_cast<T*>(p.out) + b * p.out_sb;
-      for (int e = lane; e < NH * G * D; e += 32) o[(e / D) * p.out_sh + e % D] = Dt<T>::from_f(0.f);
+  if (warp == 0) {  // the split: cap, then per-sequence unit counts and their prefix sums
+    int tiles = 0, items = 0;
+    for (int i = lane; i < B; i += 32) {
+      const int n = (sCtx[i] + kBS - 1) / kBS;
+      tiles += n;
+      items += n > 0;
     }
+    tiles = warp_sum(tiles) * HKV;
+    items = warp_sum(items) * HKV;
+    const int free_ctas = max(C - items, max(C / 4, 1));
+    const int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
+    int carry_u = 0, carry_s = 0;
+    for (int base = 0; base < B; base += 32) {
+      const int i = base + lane;
+      const int n = i < B ? (sCtx[i] + kBS - 1) / kBS : 0;
+      const int nch = n == 0 ? 0 : (n <= cap ? 1 : (n + cap - 1) / cap);
+      const int pu = warp_scan(nch, lane), ps = warp_scan(nch > 1 ? nch : 0, lane);
+      if (i < B) {
+        sPU[i + 1] = carry_u + pu;
+        sPS[i + 1] = carry_s + ps;
+      }
+      carry_u += __shfl_sync(0xffffffffu, pu, 31);
+      carry_s += __shfl_sync(0xffffffffu, ps, 31);
+    }
+    if (lane == 0) sPU[0] = sPS[0] = 0;
   }
-  if (g >= ctas) {  // no tiles: only say so to the merge kernel (after the previous one read its copy)
-    if (tid == 0) {
-      grid_dep_wait();
-      p.desc[g] = make_int4(-1, 0, 0, 0);
-    }
+  __syncthreads();
+  const int U = HKV * sPU[B];
+  // Split units never exceed 2 * max(C - I, C / 4) <= 2 * C, the slots the host provides
+  // (with the built-in cap; an overriding cap may ask for more).
+  if (HKV * sPS[B] > p.max_slots) {
+    if (tid == 0) report(p.status, PKV_ERR_WORKSPACE);
     return;
   }
-  // Tile j of the run is consumed, for every head, by warp j % WPH of that head, whose
-  // private stages are w * PW .. w * PW + PW - 1. A warp therefore waits on every phase
-  // of its stages in order (an mbarrier parity wait is only unambiguous within one phase
-  // of the barrier), and the previous use of tile j's stage is tile j - NS.
-  auto stage_of = [](int j) { return (j % WPH) * PW + (j / WPH) % PW; };
-  auto use_of = [](int j) { return (j / WPH) / PW; };
-  const int t0 = (int)((int64_t)total * g / ctas);
-  const int t1 = (int)((int64_t)total * (g + 1) / ctas);
-  const int n = t1 - t0;
-  const uint64_t deadline = global_ns() + kWaitBudgetNs;
+  auto unit_of = [&](int u) {
+    Unit r;
+    int lo = 0, hi = B - 1;  // largest b with HKV * sPU[b] <= u (a sequence with units)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (HKV * sPU[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    r.b = lo;
+    r.nch = sPU[lo + 1] - sPU[lo];
+    const int k = u - HKV * sPU[lo];
+    r.h = k / r.nch;
+    r.c = k % r.nch;
+    const int n = (sCtx[lo] + kBS - 1) / kBS;
+    const int cs = (n + r.nch - 1) / r.nch;
+    r.i0 = r.c * cs;
+    r.i1 = min(n, r.i0 + cs);
+    return r;
+  };
 
   if (warp == kNC) {
     // ---------------------------------------------------------------- producer
     const uint64_t pol = policy_evict_first();
-    auto lookup = [&](int j) -> int {  // block id of local tile j
-      if (j >= n) return 0;
-      const int t = t0 + j;
-      const int b = seq_of(sP, B, t);
-      const int i = t - sP[b];
-      const int row = sRow[b];
-      int blk = row >= 0 ? p.tables[row * p.table_stride + i] : p.nbt - 1;  // padding rows: scratch block
-      if (blk < 0 || blk >= p.nbt) {
-        report(p.status, PKV_ERR_OUT_OF_RANGE);
-        blk = p.nbt - 1;
-      }
-      return blk;
-    };
-    int blk_next = lookup(lane);
-    bool ok = true;
-    for (int base = 0; base < n && ok; base += 32) {
-      const int blk_cur = blk_next;
-      blk_next = lookup(base + 32 + lane);  // in flight while this batch is issued
-      const int cnt = min(32, n - base);
-      for (int k = 0; k < cnt && ok; ++k) {
-        const int blk = __shfl_sync(0xffffffffu, blk_cur, k);
-        const int j = base + k;
-        const int st = stage_of(j);
-        if (j == NS) grid_dep_wait();  // before the consumers can release anything
-        if (lane == 0) {
-          if (j >= NS && !mbar_wait_until(&empty[st], (use_of(j) - 1) & 1, deadline)) {
-            report(p.status, PKV_ERR_TIMEOUT);
-            ok = false;
-          }
-          if (ok) {
-            const int c4 = p.layer * p.nbt + blk;
-            mbar_arrive_expect_tx(&full[st], 2 * STAGE);
-            tma_load_5d(ring_k + st * STAGE, &tmap_k, 0, 0, 0, 0, c4, &full[st], pol);
-            tma_load_5d(ring_v + st * STAGE, &tmap_v, 0, 0, 0, 0, c4, &full[st], pol);
-          }
+    bool ok = true, waited = false;
+    uint64_t deadline = 0;
+    int j = 0;  // tiles of this CTA issued so far
+    for (int u = g; u < U && ok; u += C) {
+      const Unit un = unit_of(u);
+      const int row = sRow[un.b];
+      auto lookup = [&](int i) -> int {  // block id of block i of the unit's sequence
+        if (i >= un.i1) return 0;
+        int blk = row >= 0 ? p.tables[row * p.table_stride + i] : p.nbt - 1;  // padding rows: scratch block
+        if (blk < 0 || blk >= p.nbt) {
+          report(p.status, PKV_ERR_OUT_OF_RANGE);
+          blk = p.nbt - 1;
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+        return blk;
+      };
+      int blk_next = lookup(un.i0 + lane);
+      for (int base = un.i0; base < un.i1 && ok; base += 32) {
+        const int blk_cur = blk_next;
+        blk_next = lookup(base + 32 + lane);  // in flight while this batch is issued
+        const int cnt = min(32, un.i1 - base);
+        for (int k0 = 0; k0 < cnt && ok; k0 += kIssueLanes) {
+          const int blk = __shfl_sync(0xffffffffu, blk_cur, (k0 + lane) & 31);
+          if (!waited && j + k0 + kIssueLanes > NS) {
+            // Stages are reused from here on; their consumers start after the previous
+            // kernel, and the wait budget starts with them.
+            grid_dep_wait();
+            waited = true;
+            deadline = global_ns() + kWaitBudgetNs;
+          }
+          bool lok = true;
+          if (lane < kIssueLanes && k0 + lane < cnt) {
+            const int jj = j + k0 + lane, st = jj % NS;
+            if (jj >= NS && !mbar_wait_until(&empty[st], ((jj / NS) - 1) & 1, deadline)) {
+              report(p.status, PKV_ERR_TIMEOUT);
+              lok = false;
+            }
+            if (lok) {
+              const int c4 = p.layer * p.nbt + blk;
+              mbar_arrive_expect_tx(&full[st], 2 * TILE);
+              tma_load_5d(ring_k + st * TILE, &tmap_k, 0, 0, 0, un.h, c4, &full[st], pol);
+              tma_load_5d(ring_v + st * TILE, &tmap_v, 0, 0, 0, un.h, c4, &full[st], pol);
+            }
+          }
+          ok = __all_sync(0xffffffffu, lok);
+        }
+        j += cnt;
       }
     }
-    if (n <= NS) grid_dep_wait();
+    if (!waited) grid_dep_wait();
     if (!ok) s_bad = 1;
   } else {
     // ---------------------------------------------------------------- consumers
     grid_dep_wait();  // q, the new rows, the output and the pool writes depend on earlier kernels
-    // Every warp of a head walks the same pieces and meets the same named barriers, also
-    // after a timed-out wait (then it skips waits and math), so no barrier is left short.
-    const int h = warp / WPH, w = warp % WPH;
-    float* head_comb = comb + h * WPH * WC;
-    bool ok = true;
-    // Q fragments of this head's query group (A operand, rows = query heads). The next
-    // piece's are fetched while this piece runs, so a piece boundary does not wait on them.
-    auto load_q = [&](int bq, uint32_t (&dst)[D / 16][4]) {
-      const T* qb = reinterpret_cast<const T*>(p.q) + bq * p.q_sb + (int64_t)h * G * p.q_sh;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const int c0 = kk * 16 + 2 * t4;
-        dst[kk][0] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0) : 0u;
-        dst[kk][1] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0) : 0u;
-        dst[kk][2] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0 + 8) : 0u;
-        dst[kk][3] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0 + 8) : 0u;
+    const uint64_t deadline = global_ns() + kWaitBudgetNs;
+    if (g == C - 1) {  // sequences with nothing to attend to get zeros (the reference never asks for this)
+      for (int b = warp; b < B; b += kNC) {
+        if (sCtx[b] != 0) continue;
+        T* o = reinterpret_cast<T*>(p.out) + b * p.out_sb;
+        for (int e = lane; e < HKV * G * D; e += 32) o[(e / D) * p.out_sh + e % D] = Dt<T>::from_f(0.f);
       }
-    };
-    uint32_t qa[D / 16][4];
-    for (int b = seq_of(sP, B, t0); b < B && sP[b] < t1; ++b) {
-      const int ja = max(t0, sP[b]) - t0, jb = min(t1, sP[b + 1]) - t0;
-      if (ja >= jb) continue;  // an empty sequence
+    }
+    const int w = warp;
+    float* cw_state = comb + w * WS;
+    bool ok = true;
+    int j = 0;  // tiles of this CTA consumed so far (by all warps)
+    for (int u = g; u < U; u += C) {
+      const Unit un = unit_of(u);
+      const int b = un.b, h = un.h;
       const int ctx = sCtx[b];
-      load_q(b, qa);
+      // Q fragments of this head's query group (A operand, rows = query heads).
+      uint32_t qa[D / 16][4];
+      {
+        const T* qb = reinterpret_cast<const T*>(p.q) + b * p.q_sb + (int64_t)h * G * p.q_sh;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c0 = kk * 16 + 2 * t4;
+          qa[kk][0] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0) : 0u;
+          qa[kk][1] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0) : 0u;
+          qa[kk][2] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0 + 8) : 0u;
+          qa[kk][3] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0 + 8) : 0u;
+        }
+      }
       const int append_blk = p.k_new ? (ctx - 1) / kBS : -1;
       float m_r[2] = {-INFINITY, -INFINITY};
       float l_r[2] = {0.f, 0.f};
@@ -300,16 +331,17 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
 #pragma unroll
       for (int jj = 0; jj < D / 8; ++jj) o[jj][0] = o[jj][1] = o[jj][2] = o[jj][3] = 0.f;
 
-      for (int j = ja + ((w - ja) % WPH + WPH) % WPH; j < jb; j += WPH) {
-        const int st = stage_of(j);
-        if (ok && !mbar_wait_until(&full[st], use_of(j) & 1, deadline)) {
+      const int n_i = un.i1 - un.i0;
+      for (int k = ((w - j) % kNC + kNC) % kNC; k < n_i; k += kNC) {
+        const int jj = j + k, st = jj % NS;
+        if (ok && !mbar_wait_until(&full[st], (jj / NS) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
           ok = false;
         }
         if (ok) {
-          uint8_t* kt = ring_k + st * STAGE + h * TILE;
-          uint8_t* vt = ring_v + st * STAGE + h * TILE;
-          const int i = t0 + j - sP[b];  // block index within the sequence
+          uint8_t* kt = ring_k + st * TILE;
+          uint8_t* vt = ring_v + st * TILE;
+          const int i = un.i0 + k;  // block index within the sequence
           if (i == append_blk) {
             // Put the new row into the staged tiles and write it to the pool at slot_mapping[b].
             const int off = (ctx - 1) % kBS;
@@ -319,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
             const T* kn = reinterpret_cast<const T*>(p.k_new) + b * p.kv_sb + h * p.kv_sh;
             const T* vn = reinterpret_cast<const T*>(p.v_new) + b * p.kv_sb + h * p.kv_sh;
             const int64_t dst =
-                (((int64_t)p.layer * p.nbt + (write ? slot / kBS : 0)) * NH + h) * kBS * D + (write ? slot % kBS : 0) * D;
+                (((int64_t)p.layer * p.nbt + (write ? slot / kBS : 0)) * HKV + h) * kBS * D + (write ? slot % kBS : 0) * D;
 #pragma unroll
             for (int wd = lane; wd < D / 2; wd += 32) {
               const int d0 = 2 * wd;
@@ -345,8 +377,8 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
         if (lane == 0) mbar_arrive(&empty[st]);
       }
       finish_row_sums(l_r);
-      // Merge the head's warps through shared memory.
-      float* cm = head_comb + w * WC;
+      // Merge the 8 warps' states through shared memory.
+      float* cm = cw_state;
       float* cl = cm + RK;
       float* co = cl + RK;
       if (t4 == 0) {
@@ -363,21 +395,21 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
         *reinterpret_cast<float2*>(&co[g_lane * DP + col]) = make_float2(o[jj][0], o[jj][1]);
         if (RK > 8) *reinterpret_cast<float2*>(&co[(g_lane + 8) * DP + col]) = make_float2(o[jj][2], o[jj][3]);
       }
-      named_bar(1 + h, WPH * 32);
-      const bool whole = sP[b] >= t0 && sP[b + 1] <= t1;
-      const int slot_kind = sP[b] <= t0 ? 0 : 1;  // the run's first piece, else its last
-      float* part = p.partials + ((int64_t)(g * 2 + slot_kind) * NH + h) * SLOT;
+      named_bar(1, kNC * 32);
+      const bool whole = un.nch == 1;
+      const int slot = HKV * sPS[b] + h * un.nch + un.c;  // of a chunk of a split item
+      float* part = p.partials + (int64_t)slot * SLOT;
       T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)h * G * p.out_sh;
-      for (int it = w * 32 + lane; it < G * (D / 2); it += WPH * 32) {
+      for (int it = tid; it < G * (D / 2); it += kNC * 32) {
         const int r = it / (D / 2), col = 2 * (it % (D / 2));
         float mm = -INFINITY;
 #pragma unroll
-        for (int ww = 0; ww < WPH; ++ww) mm = fmaxf(mm, head_comb[ww * WC + r]);
+        for (int ww = 0; ww < kNC; ++ww) mm = fmaxf(mm, comb[ww * WS + r]);
         float ll = 0.f, o0 = 0.f, o1 = 0.f;
 #pragma unroll
-        for (int ww = 0; ww < WPH; ++ww) {
-          const float* c = head_comb + ww * WC;
-          const float f = ex2(c[r] - mm);
+        for (int ww = 0; ww < kNC; ++ww) {
+          const float* c = comb + ww * WS;
+          const float f = ex2(c[r] - mm);  // a warp without tiles has m = -inf: f = 0
           ll += c[RK + r] * f;
           const float2 v = *reinterpret_cast<const float2*>(&c[2 * RK + r * DP + col]);
           o0 += v.x * f;
@@ -391,96 +423,101 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, DEEP>::MIN_BL
           if (col == 0) __stcg(reinterpret_cast<float2*>(part + r * ROW), make_float2(mm, ll));
         }
       }
-      named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next piece
+      if (!whole && tid == 0) {
+        if (s_npend < kMaxPending) {
+          s_pend[s_npend++] = make_int4(b, h, un.nch, HKV * sPS[b] + h * un.nch);
+        } else {
+          report(p.status, PKV_ERR_WORKSPACE);  // cannot happen: see kMaxPending
+        }
+      }
+      named_bar(1, kNC * 32);  // the combine buffer is reused by the next unit
+      j += n_i;
     }
     if (!ok) s_bad = 1;
   }
   __syncthreads();
-  // Hand the split sequence whose first piece ends this run to the merge kernel: this CTA
-  // owns it when the run's last tile belongs to a sequence that started inside the run and
-  // continues past it. Every CTA rewrites its descriptor on every call.
+  const int npend = s_npend;
+  if (npend == 0) return;
+
+  // Tickets for this CTA's chunks; the CTA holding the last ticket of an item merges it.
+  // The barrier orders every consumer's partial writes before thread 0's release fence;
+  // the last holder's acquire fence orders them before its CTA's reads.
   if (tid == 0) {
-    int4 d = make_int4(-1, 0, 0, 0);
-    const int b = seq_of(sP, B, t1 - 1);
-    if (!s_bad && sP[b] >= t0 && sP[b + 1] > t1) {
-      const int last_cta = (int)(((int64_t)sP[b + 1] * ctas - 1) / total);  // CTA of tile sP[b + 1] - 1
-      d = make_int4(b, last_cta - g + 1, sP[b] == t0 ? 0 : 1, 0);
+    fence_acq_rel_gpu();
+    int ticket[kMaxPending];
+#pragma unroll
+    for (int k = 0; k < kMaxPending; ++k)  // all in flight together
+      if (k < npend) ticket[k] = atomicAdd(p.counters + s_pend[k].x * kMaxKvHeads + s_pend[k].y, 1);
+    bool any = false;
+#pragma unroll
+    for (int k = 0; k < kMaxPending; ++k) {
+      if (k >= npend) break;
+      const bool last = ticket[k] == s_pend[k].z - 1;
+      if (last) p.counters[s_pend[k].x * kMaxKvHeads + s_pend[k].y] = 0;  // ready for the next call
+      s_last[k] = last;
+      any |= last;
     }
-    p.desc[g] = d;
+    if (any) fence_acq_rel_gpu();
+  }
+  __syncthreads();
+  if (warp == kNC || s_bad) return;
+  for (int k = 0; k < npend; ++k) {
+    if (!s_last[k]) continue;
+    const int4 pe = s_pend[k];
+    const int b = pe.x, h = pe.y, nch = pe.z, slot0 = pe.w;
+    for (int it = tid; it < G * (D / 4); it += kNC * 32) {
+      const int c = (it % (D / 4)) * 4;
+      const int r = it / (D / 4);
+      float mx = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      for (int q0 = 0; q0 < nch; q0 += kMergeBatch) {
+        const int cnt = min(kMergeBatch, nch - q0);
+        float2 ml[kMergeBatch];
+        float4 ov[kMergeBatch];
+#pragma unroll
+        for (int q = 0; q < kMergeBatch; ++q) {
+          if (q < cnt) {
+            const float* row = p.partials + (int64_t)(slot0 + q0 + q) * SLOT + r * ROW;
+            ml[q] = __ldcg(reinterpret_cast<const float2*>(row));
+            ov[q] = __ldcg(reinterpret_cast<const float4*>(row + 4 + c));
+          }
+        }
+        float mn = mx;
+#pragma unroll
+        for (int q = 0; q < kMergeBatch; ++q)
+          if (q < cnt) mn = fmaxf(mn, ml[q].x);
+        const float fo = mx == -INFINITY ? 0.f : ex2(mx - mn);
+        l *= fo, a0 *= fo, a1 *= fo, a2 *= fo, a3 *= fo;
+#pragma unroll
+        for (int q = 0; q < kMergeBatch; ++q) {
+          if (q < cnt) {
+            const float f = ex2(ml[q].x - mn);
+            l += ml[q].y * f;
+            a0 += ov[q].x * f, a1 += ov[q].y * f, a2 += ov[q].z * f, a3 += ov[q].w * f;
+          }
+        }
+        mx = mn;
+      }
+      const float inv = 1.f / l;
+      T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)(h * G + r) * p.out_sh + c;
+      *reinterpret_cast<uint32_t*>(outp) = Dt<T>::pack(a0 * inv, a1 * inv);
+      *reinterpret_cast<uint32_t*>(outp + 2) = Dt<T>::pack(a2 * inv, a3 * inv);
+    }
   }
 }
 
-// Merges the pieces of every split sequence, one CTA per possible owner (the decode
-// kernel's CTA g writes descriptor g). Pieces are combined in run order with the
-// running-max rescaling of the flash step, so the result does not depend on timing.
-// Each thread takes (head, row, 4 columns) items and loads up to 8 pieces' states at a
-// time, all independent, so a merge of up to 8 pieces costs one round trip to L2.
-constexpr int kMergeThreads = 512;
-
-template <typename T, int D, int NH, int RK>
-__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const DecodeParams p) {
-  constexpr int ROW = D + 4;
-  constexpr int SLOT = RK * ROW;
-  grid_dep_launch_dependents();
-  grid_dep_wait();  // the decode kernel's pieces and descriptors
-  const int4 d = __ldcg(&p.desc[blockIdx.x]);
-  if (d.x < 0) return;
-  const int b = d.x, np = d.y, kind0 = d.z, first = blockIdx.x;
-  const int G = p.group;
-  const int items = NH * G * (D / 4);
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int c = (it % (D / 4)) * 4;
-    const int r = (it / (D / 4)) % G;
-    const int h = it / (G * (D / 4));
-    float mx = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int q0 = 0; q0 < np; q0 += 8) {
-      const int cnt = min(8, np - q0);
-      float2 ml[8];
-      float4 o[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (u < cnt) {
-          const int q = q0 + u;
-          const float* row = p.partials + ((int64_t)((first + q) * 2 + (q == 0 ? kind0 : 0)) * NH + h) * SLOT + r * ROW;
-          ml[u] = __ldcg(reinterpret_cast<const float2*>(row));
-          o[u] = __ldcg(reinterpret_cast<const float4*>(row + 4 + c));
-        }
-      }
-      float mn = mx;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (u < cnt) mn = fmaxf(mn, ml[u].x);
-      const float fo = mx == -INFINITY ? 0.f : ex2(mx - mn);
-      l *= fo, a0 *= fo, a1 *= fo, a2 *= fo, a3 *= fo;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (u < cnt) {
-          const float f = ml[u].x == -INFINITY ? 0.f : ex2(ml[u].x - mn);
-          l += ml[u].y * f;
-          a0 += o[u].x * f, a1 += o[u].y * f, a2 += o[u].z * f, a3 += o[u].w * f;
-        }
-      }
-      mx = mn;
-    }
-    const float inv = 1.f / l;
-    T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)(h * G + r) * p.out_sh + c;
-    *reinterpret_cast<uint32_t*>(outp) = Dt<T>::pack(a0 * inv, a1 * inv);
-    *reinterpret_cast<uint32_t*>(outp + 2) = Dt<T>::pack(a2 * inv, a3 * inv);
-  }
-}
-
-// Workspace: [descriptors: kMaxCtas int4][partials: ctas * 2 * NH * RK * (D + 4) float].
-// Both are written before they are read within a call; nothing carries over between calls.
+// Workspace: [ticket counters: kMaxBatch * kMaxKvHeads int32][partials: 2 * ctas slots of
+// RK * (D + 4) floats]. The counters start at zero and every call leaves them at zero.
 constexpr int kMaxCtas = 4 * 256;  // workspace is sized for up to 4 CTAs on each of up to 256 SMs
-constexpr int64_t kPartialsOffset = (int64_t)kMaxCtas * 16;
-int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (int64_t)ctas * 2 * nh * rk * (d + 4) * 4; }
+constexpr int64_t kPartialsOffset = (int64_t)kMaxBatch * kMaxKvHeads * 4;
+int64_t ws_bytes(int ctas, int rk, int d) { return kPartialsOffset + (int64_t)2 * ctas * rk * (d + 4) * 4; }
 
 // Tuning knobs, read once from the environment (0 / unset = built-in choice):
 //   PKV_DECODE_CTAS_PER_SM  CTAs per SM (at most what the shared memory allows)
 //   PKV_DECODE_PDL          0 = launch without programmatic stream serialization
+//   PKV_DECODE_CAP          blocks per unit above which an item is split
 //   PKV_DECODE_DEEP         1 = one CTA per SM with the deepest ring that fits
 struct DecodeKnobs {
-  int ctas_per_sm = 0, pdl = 1, deep = 0;
+  int ctas_per_sm = 0, pdl = 1, cap = 0, deep = 0;
   DecodeKnobs() {
     auto env = [](const char* k, int dflt) {
       const char* v = getenv(k);
@@ -488,6 +525,7 @@ struct DecodeKnobs {
     };
     ctas_per_sm = env("PKV_DECODE_CTAS_PER_SM", 0);
     pdl = env("PKV_DECODE_PDL", 1);
+    cap = env("PKV_DECODE_CAP", 0);
     deep = env("PKV_DECODE_DEEP", 0);
   }
 };
@@ -496,29 +534,31 @@ const DecodeKnobs& knobs() {
   return k;
 }
 
-template <typename T, int D, int NH, int RK, bool DEEP>
+template <typename T, int D, int RK, bool DEEP>
 int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace, int64_t workspace_bytes,
                   cudaStream_t stream) {
-  using S = DecodeShape<D, NH, RK, DEEP>;
+  using S = DecodeShape<D, RK, DEEP>;
   static int per_sm = 0;
   if (per_sm == 0) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel<T, D, NH, RK, DEEP>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+    cudaError_t e =
+        cudaFuncSetAttribute(decode_kernel<T, D, RK, DEEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK, DEEP>, kThreads, S::SMEM);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, RK, DEEP>, kThreads, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     per_sm = std::max(1, occ);
   }
   const int want = knobs().ctas_per_sm > 0 ? std::min(knobs().ctas_per_sm, per_sm) : per_sm;
   const int ctas = std::min(num_sms() * want, kMaxCtas);
-  if (!workspace || workspace_bytes < ws_bytes(ctas, NH, RK, D)) return PKV_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < ws_bytes(ctas, RK, D)) return PKV_ERR_WORKSPACE;
   CUtensorMap tk, tv;
-  if (!get_pool_maps(pool, &tk, &tv, NH)) return PKV_ERR_CUDA;
+  if (!get_pool_maps(pool, &tk, &tv, 1)) return PKV_ERR_CUDA;
   DecodeParams p = p0;
   uint8_t* wsb = static_cast<uint8_t*>(workspace);
-  p.desc = reinterpret_cast<int4*>(wsb);
+  p.counters = reinterpret_cast<int32_t*>(wsb);
   p.partials = reinterpret_cast<float*>(wsb + kPartialsOffset);
+  p.max_slots = 2 * ctas;
+  p.cap_override = knobs().cap;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(kThreads);
@@ -529,32 +569,16 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = knobs().pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const int st = cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, DEEP>, tk, tv, p));
-  if (st != PKV_OK) return st;
-  // The merge of split sequences: one small CTA per decode CTA, launched behind it (with
-  // programmatic serialization it is resident early and waits on the decode grid).
-  cfg.blockDim = dim3(kMergeThreads);
-  cfg.dynamicSmemBytes = 0;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, D, NH, RK>, p));
-}
-
-template <typename T, int D, int NH>
-int launch_rows(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
-  if (knobs().deep)
-    return p.group <= 8 ? launch_decode<T, D, NH, 8, true>(pool, p, ws, wsb, st)
-                        : launch_decode<T, D, NH, 16, true>(pool, p, ws, wsb, st);
-  return p.group <= 8 ? launch_decode<T, D, NH, 8, false>(pool, p, ws, wsb, st)
-                      : launch_decode<T, D, NH, 16, false>(pool, p, ws, wsb, st);
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, RK, DEEP>, tk, tv, p));
 }
 
 template <typename T, int D>
-int launch_heads(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
-  switch (pool.num_kv_heads) {
-    case 1: return launch_rows<T, D, 1>(pool, p, ws, wsb, st);
-    case 2: return launch_rows<T, D, 2>(pool, p, ws, wsb, st);
-    case 4: return launch_rows<T, D, 4>(pool, p, ws, wsb, st);
-    default: return PKV_ERR_UNSUPPORTED;
-  }
+int launch_rows(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
+  if (knobs().deep)
+    return p.group <= 8 ? launch_decode<T, D, 8, true>(pool, p, ws, wsb, st)
+                        : launch_decode<T, D, 16, true>(pool, p, ws, wsb, st);
+  return p.group <= 8 ? launch_decode<T, D, 8, false>(pool, p, ws, wsb, st)
+                      : launch_decode<T, D, 16, false>(pool, p, ws, wsb, st);
 }
 
 }  // namespace
@@ -564,11 +588,11 @@ using namespace pkv;
 
 extern "C" int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
                                               int32_t block_size, int32_t head_dim, int32_t num_q_heads) {
-  if (batch <= 0 || batch > kMaxBatch || num_kv_heads <= 0 || max_blocks_per_seq <= 0 || block_size != kBS ||
-      (head_dim != 64 && head_dim != 128) || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0)
+  if (batch <= 0 || batch > kMaxBatch || num_kv_heads <= 0 || num_kv_heads > kMaxKvHeads || max_blocks_per_seq <= 0 ||
+      block_size != kBS || (head_dim != 64 && head_dim != 128) || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0)
     return 0;
   const int group = num_q_heads / num_kv_heads;
-  return ws_bytes(kMaxCtas, num_kv_heads, group <= 8 ? 8 : 16, head_dim);
+  return ws_bytes(kMaxCtas, group <= 8 ? 8 : 16, head_dim);
 }
 
 extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
@@ -585,6 +609,7 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   const int d = pool->head_dim, hkv = pool->num_kv_heads;
   if (pool->block_size != kBS || (d != 64 && d != 128)) return PKV_ERR_UNSUPPORTED;
   if (hkv <= 0 || num_q_heads <= 0 || num_q_heads % hkv != 0) return PKV_ERR_INVALID_ARGUMENT;
+  if (hkv > kMaxKvHeads) return PKV_ERR_UNSUPPORTED;
   const int group = num_q_heads / hkv;
   if (group > 16) return PKV_ERR_UNSUPPORTED;
   if ((k_new == nullptr) != (v_new == nullptr)) return PKV_ERR_INVALID_ARGUMENT;
@@ -621,6 +646,7 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   p.table_cols = tables->cols;
   p.batch = batch;
   p.group = group;
+  p.kv_heads = hkv;
   p.layer = layer;
   p.nbt = pool->num_blocks_total;
   p.scale_log2 = scale * kLog2e;
@@ -628,12 +654,12 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (pool->dtype == PKV_F16) {
-    return d == 64 ? launch_heads<__half, 64>(*pool, p, workspace, workspace_bytes, st)
-                   : launch_heads<__half, 128>(*pool, p, workspace, workspace_bytes, st);
+    return d == 64 ? launch_rows<__half, 64>(*pool, p, workspace, workspace_bytes, st)
+                   : launch_rows<__half, 128>(*pool, p, workspace, workspace_bytes, st);
   }
   if (pool->dtype == PKV_BF16) {
-    return d == 64 ? launch_heads<__nv_bfloat16, 64>(*pool, p, workspace, workspace_bytes, st)
-                   : launch_heads<__nv_bfloat16, 128>(*pool, p, workspace, workspace_bytes, st);
+    return d == 64 ? launch_rows<__nv_bfloat16, 64>(*pool, p, workspace, workspace_bytes, st)
+                   : launch_rows<__nv_bfloat16, 128>(*pool, p, workspace, workspace_bytes, st);
   }
   return PKV_ERR_UNSUPPORTED;
 }

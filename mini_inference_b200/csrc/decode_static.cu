@@ -26,7 +26,7 @@ namespace {
 constexpr int64_t kScratchBytes = PKV_DECODE_STATIC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
 
-// Split-sequence descriptors first, then the partial softmax states (the layout
+// Ticket counters first, then the partial softmax states of split items (the layout
 // pkv_decode_attention gives a caller workspace).
 static __device__ __align__(256) uint8_t g_decode_scratch[kScratchBytes];
 
@@ -34,8 +34,8 @@ std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
 
 // Address of the current device's scratch. The first call for a device looks it
-// up and clears it on `stream`, ahead of the kernels that follow on that stream, so
-// its contents are defined from the start (a call writes every word it reads).
+// up and clears it on `stream`, ahead of the kernel that follows on that stream:
+// the ticket counters must start at zero (every call leaves them at zero again).
 int device_scratch(void** out, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
