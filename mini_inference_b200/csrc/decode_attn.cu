@@ -6,32 +6,33 @@
 // (engine/model.py:126-147). Here nothing is gathered: K/V blocks are read in
 // place through the block table, each exactly once, straight into shared memory.
 //
-// Work split. An "item" is one KV head of one sequence: that head's K/V blocks and
-// the GQA group of query heads that reads them. A CTA takes one unit of work, an
-// item or a chunk of one, and streams its blocks once. Items longer than
+// Work split. An "item" is one sequence: its K/V blocks (all KV heads) and its
+// query heads. A CTA takes one unit of work, an item or a chunk of one, and
+// streams its blocks once. Items longer than
 //   cap = max(kMinCap, ceil(T / max(C - I, C / 4)))
-// (T: the batch's (block, head) tiles, C: CTAs, I: items) are cut into
-// ceil(n / cap) balanced chunks of consecutive blocks, so that, when the items
-// allow it, all units fit one wave of CTAs and no unit is much longer than the
-// mean. Every CTA derives the same split from context_lens in its prologue; with
-// more units than CTAs, CTA g takes units g, g + C, ... The CTA that finishes the
-// last chunk of an item (an atomic ticket per item; no CTA waits for another)
-// merges the chunks' partial softmax states in chunk order, so the result does
-// not depend on which CTA came last.
+// blocks (T: the batch's blocks, C: CTAs, I: items) are cut into ceil(n / cap)
+// balanced chunks of consecutive blocks, so that, when the items allow it, all units
+// fit one wave of CTAs and no unit is much longer than the mean. Every CTA derives
+// the same split from context_lens in its prologue; with more units than CTAs, CTA
+// g takes units g, g + C, ... The CTA that finishes the last chunk of an item (an
+// atomic ticket per item; no CTA waits for another) merges the chunks' partial
+// softmax states in chunk order, so the result does not depend on which CTA came
+// last.
 //
 // Inside a CTA one producer warp resolves block ids through the block table (32
 // at a time, one lookup per lane, the next 32 already in flight) and keeps a ring
-// of stages full with TMA copies of one head's K and V tiles (128B swizzle, L2
-// evict-first). kIssueLanes lanes issue the copies of consecutive tiles with one
-// instruction: the issue rate of a single lane does not keep HBM busy with copies
-// of 2-4 KB. Tile j of the CTA's stream goes to consumer warp j % 8 through stage
-// j % S (S a multiple of 8), so every stage has one consumer, which waits on each
-// phase of it in turn (an mbarrier parity wait cannot tell a phase from the one two
-// later). Each consumer runs the 16-key flash step on mma.sync m16n8k16 with the
-// M = 16 rows being the GQA group's query heads (the reference regroups head h to
+// of stages full with TMA copies of a block's K and V for all KV heads at once
+// (adjacent in the pool: 4 KB per tensor at 2 heads x d 64; 128B swizzle, L2
+// evict-first). kIssueLanes lanes issue the copies of consecutive blocks with one
+// instruction. The 8 consumer warps split the KV heads (8 / Hkv warps per head);
+// block j goes, for every head, to warp j % (8 / Hkv) of that head through stage
+// j % S (S a multiple of 8 / Hkv), so each warp waits on every phase of its stages
+// in turn (an mbarrier parity wait cannot tell a phase from the one two later).
+// Each consumer runs the 16-key flash step on mma.sync m16n8k16 with the M = 16
+// rows being its head's GQA group of query heads (the reference regroups head h to
 // (h / group, h % group) the same way), so a tile read from HBM serves the whole
-// group (attn_tile.cuh). At the end of a unit the 8 warps merge their softmax
-// states through shared memory.
+// group (attn_tile.cuh). At the end of a unit the warps of a head merge their
+// softmax states through shared memory.
 #include <algorithm>
 #include <cstdlib>
 
@@ -45,31 +46,30 @@ constexpr int kBS = 16;  // tokens per block handled by this kernel
 constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
 constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared memory
-constexpr int kMaxKvHeads = 16;    // ticket counters are indexed by (sequence, KV head)
 constexpr int kMinCap = 16;        // items of up to 16 blocks are never split
 constexpr int kIssueLanes = 4;     // producer lanes issuing copies together
 constexpr int kMergeBatch = 4;     // chunk states a merging thread loads at once
 constexpr int kMaxPending = 8;     // split units of one CTA whose tickets are taken at the end
 constexpr float kLog2e = 1.4426950408889634f;
 
-// D: head_dim, RK: rows kept per item (8 or 16 >= group size), DEEP: one CTA per SM
-// with up to 6 stages per consumer warp.
-template <int D, int RK, bool DEEP = false> struct DecodeShape {
+// D: head_dim, NH: KV heads (all in one tile), RK: rows kept per head (8 or 16 >= group).
+template <int D, int NH, int RK> struct DecodeShape {
   static constexpr int TILE = kBS * D * 2;             // one head's K (or V) of one block
+  static constexpr int STAGE = NH * TILE;              // K (or V) of all heads of one block
+  static constexpr int WPH = kNC / NH;                 // consumer warps per KV head
   static constexpr int DP = D + 4;                     // padded combine row (no bank conflicts)
   static constexpr int WARP_STATE = 2 * RK + RK * DP;  // floats: m[RK], l[RK], O[RK][DP]
   static constexpr int COMB = kNC * WARP_STATE * 4;
   static constexpr int TABLES = 4 * (kMaxBatch + 1) * 4;  // context lengths, table rows, unit and split prefixes
   static constexpr int FIXED = 1024 + COMB + TABLES + 256;
-  // Two CTAs per SM when each consumer warp keeps 2+ stages in half the shared
-  // memory, else one CTA with up to 4 stages per warp.
-  static constexpr int PW_HALF = (113 * 1024 - FIXED) / (2 * TILE * kNC);
-  static constexpr int PW_FULL = (226 * 1024 - FIXED) / (2 * TILE * kNC);
-  static constexpr bool TWO = !DEEP && PW_HALF >= 2;
-  static constexpr int PW_MAX_ONE = DEEP ? 6 : 4;
-  static constexpr int PW = TWO ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > PW_MAX_ONE ? PW_MAX_ONE : PW_FULL);
-  static constexpr int S = kNC * PW;
-  static constexpr int RING = 2 * S * TILE;
+  // Two CTAs per SM when each consumer warp keeps 2+ stages in half the shared memory,
+  // else one CTA with up to 4 stages per warp.
+  static constexpr int PW_HALF = (113 * 1024 - FIXED) / (2 * STAGE * WPH);
+  static constexpr int PW_FULL = (226 * 1024 - FIXED) / (2 * STAGE * WPH);
+  static constexpr bool TWO = PW_HALF >= 2;
+  static constexpr int PW = TWO ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > 4 ? 4 : PW_FULL);
+  static constexpr int S = WPH * PW;
+  static constexpr int RING = 2 * S * STAGE;
   static constexpr int SMEM = 1024 + RING + COMB + 2 * S * 8 + TABLES;
   static constexpr int MIN_BLOCKS = TWO ? 2 : 1;
   static_assert(PW >= 1, "ring too shallow");
@@ -87,8 +87,8 @@ struct DecodeParams {
   const int32_t* seq_rows;
   const int32_t* context_lens;
   int32_t* status;
-  int32_t* counters;  // [kMaxBatch * kMaxKvHeads] chunks of each item finished so far
-  float* partials;    // [max_slots][RK][D + 4]: (m, l, pad, pad, O) per row of a chunk
+  int32_t* counters;  // [kMaxBatch] chunks of each item finished so far
+  float* partials;    // [max_slots][NH][RK][D + 4]: (m, l, pad, pad, O) per row of a chunk
   int64_t out_sb, out_sh, q_sb, q_sh, kv_sb, kv_sh, table_stride;
   int32_t table_rows, table_cols;
   int32_t batch, group, kv_heads, layer, nbt, inputs_ready, max_slots, cap_override;
@@ -120,21 +120,22 @@ __device__ inline int warp_scan(int v, int lane) {
 }
 
 struct Unit {
-  int b, h, c, nch, i0, i1;
+  int b, c, nch, i0, i1;
 };
 
-template <typename T, int D, int RK, bool DEEP>
-__global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS)
+template <typename T, int D, int NH, int RK>
+__global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                   const DecodeParams p) {
-  using S = DecodeShape<D, RK, DEEP>;
-  constexpr int TILE = S::TILE, NS = S::S, DP = S::DP, WS = S::WARP_STATE;
-  constexpr int ROW = D + 4;      // partial row: m, l, 2 pad floats, O[D] (O 16-byte aligned)
-  constexpr int SLOT = RK * ROW;  // floats of one chunk's partial state
+  using S = DecodeShape<D, NH, RK>;
+  constexpr int TILE = S::TILE, STAGE = S::STAGE, NS = S::S, WPH = S::WPH, DP = S::DP, WS = S::WARP_STATE;
+  constexpr int LANES = kIssueLanes < NS ? kIssueLanes : NS;  // the copies of one issue use distinct stages
+  constexpr int ROW = D + 4;            // partial row: m, l, 2 pad floats, O[D] (O 16-byte aligned)
+  constexpr int SLOT = NH * RK * ROW;   // floats of one chunk's partial state (all heads)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring_k = smem;
-  uint8_t* ring_v = smem + NS * TILE;
+  uint8_t* ring_v = smem + NS * STAGE;
   float* comb = reinterpret_cast<float*>(smem + S::RING);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::COMB);
   uint64_t* empty = full + NS;
@@ -143,12 +144,12 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
   int* sPU = sRow + kMaxBatch + 1;                 // [batch + 1] units (per KV head) before sequence b
   int* sPS = sPU + kMaxBatch + 1;                  // [batch + 1] split units (per KV head) before b
   __shared__ int s_bad, s_npend;
-  __shared__ int4 s_pend[kMaxPending];  // (sequence, KV head, chunks, first slot) of split units
+  __shared__ int4 s_pend[kMaxPending];  // (sequence, chunks, first slot, -) of split units
   __shared__ int s_last[kMaxPending];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g_lane = lane >> 2, t4 = lane & 3;
-  const int B = p.batch, G = p.group, HKV = p.kv_heads;
+  const int B = p.batch, G = p.group;
   const int C = gridDim.x, g = blockIdx.x;
   const int cap_tokens = p.table_cols * kBS;
 
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], NH);  // one consumer warp per head releases each stage
     }
     fence_mbar_init();
     s_bad = 0;
@@ -193,8 +194,8 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
       tiles += n;
       items += n > 0;
     }
-    tiles = warp_sum(tiles) * HKV;
-    items = warp_sum(items) * HKV;
+    tiles = warp_sum(tiles);
+    items = warp_sum(items);
     const int free_ctas = max(C - items, max(C / 4, 1));
     const int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
     int carry_u = 0, carry_s = 0;
@@ -213,25 +214,23 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
     if (lane == 0) sPU[0] = sPS[0] = 0;
   }
   __syncthreads();
-  const int U = HKV * sPU[B];
+  const int U = sPU[B];
   // Split units never exceed 2 * max(C - I, C / 4) <= 2 * C, the slots the host provides
   // (with the built-in cap; an overriding cap may ask for more).
-  if (HKV * sPS[B] > p.max_slots) {
+  if (sPS[B] > p.max_slots) {
     if (tid == 0) report(p.status, PKV_ERR_WORKSPACE);
     return;
   }
   auto unit_of = [&](int u) {
     Unit r;
-    int lo = 0, hi = B - 1;  // largest b with HKV * sPU[b] <= u (a sequence with units)
+    int lo = 0, hi = B - 1;  // largest b with sPU[b] <= u (a sequence with units)
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (HKV * sPU[mid] <= u) lo = mid; else hi = mid - 1;
+      if (sPU[mid] <= u) lo = mid; else hi = mid - 1;
     }
     r.b = lo;
     r.nch = sPU[lo + 1] - sPU[lo];
-    const int k = u - HKV * sPU[lo];
-    r.h = k / r.nch;
-    r.c = k % r.nch;
+    r.c = u - sPU[lo];
     const int n = (sCtx[lo] + kBS - 1) / kBS;
     const int cs = (n + r.nch - 1) / r.nch;
     r.i0 = r.c * cs;
@@ -262,9 +261,9 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
         const int blk_cur = blk_next;
         blk_next = lookup(base + 32 + lane);  // in flight while this batch is issued
         const int cnt = min(32, un.i1 - base);
-        for (int k0 = 0; k0 < cnt && ok; k0 += kIssueLanes) {
+        for (int k0 = 0; k0 < cnt && ok; k0 += LANES) {
           const int blk = __shfl_sync(0xffffffffu, blk_cur, (k0 + lane) & 31);
-          if (!waited && j + k0 + kIssueLanes > NS) {
+          if (!waited && j + k0 + LANES > NS) {
             // Stages are reused from here on; their consumers start after the previous
             // kernel, and the wait budget starts with them.
             grid_dep_wait();
@@ -272,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
             deadline = global_ns() + kWaitBudgetNs;
           }
           bool lok = true;
-          if (lane < kIssueLanes && k0 + lane < cnt) {
+          if (lane < LANES && k0 + lane < cnt) {
             const int jj = j + k0 + lane, st = jj % NS;
             if (jj >= NS && !mbar_wait_until(&empty[st], ((jj / NS) - 1) & 1, deadline)) {
               report(p.status, PKV_ERR_TIMEOUT);
@@ -280,9 +279,9 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
             }
             if (lok) {
               const int c4 = p.layer * p.nbt + blk;
-              mbar_arrive_expect_tx(&full[st], 2 * TILE);
-              tma_load_5d(ring_k + st * TILE, &tmap_k, 0, 0, 0, un.h, c4, &full[st], pol);
-              tma_load_5d(ring_v + st * TILE, &tmap_v, 0, 0, 0, un.h, c4, &full[st], pol);
+              mbar_arrive_expect_tx(&full[st], 2 * STAGE);
+              tma_load_5d(ring_k + st * STAGE, &tmap_k, 0, 0, 0, 0, c4, &full[st], pol);
+              tma_load_5d(ring_v + st * STAGE, &tmap_v, 0, 0, 0, 0, c4, &full[st], pol);
             }
           }
           ok = __all_sync(0xffffffffu, lok);
@@ -300,16 +299,17 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
       for (int b = warp; b < B; b += kNC) {
         if (sCtx[b] != 0) continue;
         T* o = reinterpret_cast<T*>(p.out) + b * p.out_sb;
-        for (int e = lane; e < HKV * G * D; e += 32) o[(e / D) * p.out_sh + e % D] = Dt<T>::from_f(0.f);
+        for (int e = lane; e < NH * G * D; e += 32) o[(e / D) * p.out_sh + e % D] = Dt<T>::from_f(0.f);
       }
     }
-    const int w = warp;
-    float* cw_state = comb + w * WS;
+    const int h = warp / WPH, w = warp % WPH;  // this warp's KV head and its rank among the head's warps
+    float* head_comb = comb + h * WPH * WS;
+    float* cw_state = head_comb + w * WS;
     bool ok = true;
     int j = 0;  // tiles of this CTA consumed so far (by all warps)
     for (int u = g; u < U; u += C) {
       const Unit un = unit_of(u);
-      const int b = un.b, h = un.h;
+      const int b = un.b;
       const int ctx = sCtx[b];
       // Q fragments of this head's query group (A operand, rows = query heads).
       uint32_t qa[D / 16][4];
@@ -332,15 +332,15 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
       for (int jj = 0; jj < D / 8; ++jj) o[jj][0] = o[jj][1] = o[jj][2] = o[jj][3] = 0.f;
 
       const int n_i = un.i1 - un.i0;
-      for (int k = ((w - j) % kNC + kNC) % kNC; k < n_i; k += kNC) {
+      for (int k = ((w - j) % WPH + WPH) % WPH; k < n_i; k += WPH) {
         const int jj = j + k, st = jj % NS;
         if (ok && !mbar_wait_until(&full[st], (jj / NS) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
           ok = false;
         }
         if (ok) {
-          uint8_t* kt = ring_k + st * TILE;
-          uint8_t* vt = ring_v + st * TILE;
+          uint8_t* kt = ring_k + st * STAGE + h * TILE;
+          uint8_t* vt = ring_v + st * STAGE + h * TILE;
           const int i = un.i0 + k;  // block index within the sequence
           if (i == append_blk) {
             // Put the new row into the staged tiles and write it to the pool at slot_mapping[b].
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
             const T* kn = reinterpret_cast<const T*>(p.k_new) + b * p.kv_sb + h * p.kv_sh;
             const T* vn = reinterpret_cast<const T*>(p.v_new) + b * p.kv_sb + h * p.kv_sh;
             const int64_t dst =
-                (((int64_t)p.layer * p.nbt + (write ? slot / kBS : 0)) * HKV + h) * kBS * D + (write ? slot % kBS : 0) * D;
+                (((int64_t)p.layer * p.nbt + (write ? slot / kBS : 0)) * NH + h) * kBS * D + (write ? slot % kBS : 0) * D;
 #pragma unroll
             for (int wd = lane; wd < D / 2; wd += 32) {
               const int d0 = 2 * wd;
@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
         if (lane == 0) mbar_arrive(&empty[st]);
       }
       finish_row_sums(l_r);
-      // Merge the 8 warps' states through shared memory.
+      // Merge the head's warps through shared memory.
       float* cm = cw_state;
       float* cl = cm + RK;
       float* co = cl + RK;
@@ -395,20 +395,20 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
         *reinterpret_cast<float2*>(&co[g_lane * DP + col]) = make_float2(o[jj][0], o[jj][1]);
         if (RK > 8) *reinterpret_cast<float2*>(&co[(g_lane + 8) * DP + col]) = make_float2(o[jj][2], o[jj][3]);
       }
-      named_bar(1, kNC * 32);
+      named_bar(1 + h, WPH * 32);
       const bool whole = un.nch == 1;
-      const int slot = HKV * sPS[b] + h * un.nch + un.c;  // of a chunk of a split item
-      float* part = p.partials + (int64_t)slot * SLOT;
+      const int slot = sPS[b] + un.c;  // of a chunk of a split item
+      float* part = p.partials + (int64_t)slot * SLOT + h * RK * ROW;
       T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)h * G * p.out_sh;
-      for (int it = tid; it < G * (D / 2); it += kNC * 32) {
+      for (int it = w * 32 + lane; it < G * (D / 2); it += WPH * 32) {
         const int r = it / (D / 2), col = 2 * (it % (D / 2));
         float mm = -INFINITY;
 #pragma unroll
-        for (int ww = 0; ww < kNC; ++ww) mm = fmaxf(mm, comb[ww * WS + r]);
+        for (int ww = 0; ww < WPH; ++ww) mm = fmaxf(mm, head_comb[ww * WS + r]);
         float ll = 0.f, o0 = 0.f, o1 = 0.f;
 #pragma unroll
-        for (int ww = 0; ww < kNC; ++ww) {
-          const float* c = comb + ww * WS;
+        for (int ww = 0; ww < WPH; ++ww) {
+          const float* c = head_comb + ww * WS;
           const float f = ex2(c[r] - mm);  // a warp without tiles has m = -inf: f = 0
           ll += c[RK + r] * f;
           const float2 v = *reinterpret_cast<const float2*>(&c[2 * RK + r * DP + col]);
@@ -423,14 +423,14 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
           if (col == 0) __stcg(reinterpret_cast<float2*>(part + r * ROW), make_float2(mm, ll));
         }
       }
-      if (!whole && tid == 0) {
+      if (!whole && warp == 0 && lane == 0) {
         if (s_npend < kMaxPending) {
-          s_pend[s_npend++] = make_int4(b, h, un.nch, HKV * sPS[b] + h * un.nch);
+          s_pend[s_npend++] = make_int4(b, un.nch, sPS[b], 0);
         } else {
           report(p.status, PKV_ERR_WORKSPACE);  // cannot happen: see kMaxPending
         }
       }
-      named_bar(1, kNC * 32);  // the combine buffer is reused by the next unit
+      named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next unit
       j += n_i;
     }
     if (!ok) s_bad = 1;
@@ -447,13 +447,13 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
     int ticket[kMaxPending];
 #pragma unroll
     for (int k = 0; k < kMaxPending; ++k)  // all in flight together
-      if (k < npend) ticket[k] = atomicAdd(p.counters + s_pend[k].x * kMaxKvHeads + s_pend[k].y, 1);
+      if (k < npend) ticket[k] = atomicAdd(p.counters + s_pend[k].x, 1);
     bool any = false;
 #pragma unroll
     for (int k = 0; k < kMaxPending; ++k) {
       if (k >= npend) break;
-      const bool last = ticket[k] == s_pend[k].z - 1;
-      if (last) p.counters[s_pend[k].x * kMaxKvHeads + s_pend[k].y] = 0;  // ready for the next call
+      const bool last = ticket[k] == s_pend[k].y - 1;
+      if (last) p.counters[s_pend[k].x] = 0;  // ready for the next call
       s_last[k] = last;
       any |= last;
     }
@@ -464,10 +464,10 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
   for (int k = 0; k < npend; ++k) {
     if (!s_last[k]) continue;
     const int4 pe = s_pend[k];
-    const int b = pe.x, h = pe.y, nch = pe.z, slot0 = pe.w;
-    for (int it = tid; it < G * (D / 4); it += kNC * 32) {
+    const int b = pe.x, nch = pe.y, slot0 = pe.z;
+    for (int it = tid; it < NH * G * (D / 4); it += kNC * 32) {
       const int c = (it % (D / 4)) * 4;
-      const int r = it / (D / 4);
+      const int hr = it / (D / 4), h = hr / G, r = hr - h * G;
       float mx = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
       for (int q0 = 0; q0 < nch; q0 += kMergeBatch) {
         const int cnt = min(kMergeBatch, nch - q0);
@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
 #pragma unroll
         for (int q = 0; q < kMergeBatch; ++q) {
           if (q < cnt) {
-            const float* row = p.partials + (int64_t)(slot0 + q0 + q) * SLOT + r * ROW;
+            const float* row = p.partials + (int64_t)(slot0 + q0 + q) * SLOT + (h * RK + r) * ROW;
             ml[q] = __ldcg(reinterpret_cast<const float2*>(row));
             ov[q] = __ldcg(reinterpret_cast<const float4*>(row + 4 + c));
           }
@@ -505,19 +505,18 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, RK, DEEP>::MIN_BLOCKS
   }
 }
 
-// Workspace: [ticket counters: kMaxBatch * kMaxKvHeads int32][partials: 2 * ctas slots of
-// RK * (D + 4) floats]. The counters start at zero and every call leaves them at zero.
+// Workspace: [ticket counters: kMaxBatch int32][partials: 2 * ctas slots of
+// NH * RK * (D + 4) floats]. The counters start at zero and every call leaves them at zero.
 constexpr int kMaxCtas = 4 * 256;  // workspace is sized for up to 4 CTAs on each of up to 256 SMs
-constexpr int64_t kPartialsOffset = (int64_t)kMaxBatch * kMaxKvHeads * 4;
-int64_t ws_bytes(int ctas, int rk, int d) { return kPartialsOffset + (int64_t)2 * ctas * rk * (d + 4) * 4; }
+constexpr int64_t kPartialsOffset = (int64_t)kMaxBatch * 4;
+int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (int64_t)2 * ctas * nh * rk * (d + 4) * 4; }
 
 // Tuning knobs, read once from the environment (0 / unset = built-in choice):
 //   PKV_DECODE_CTAS_PER_SM  CTAs per SM (at most what the shared memory allows)
 //   PKV_DECODE_PDL          0 = launch without programmatic stream serialization
 //   PKV_DECODE_CAP          blocks per unit above which an item is split
-//   PKV_DECODE_DEEP         1 = one CTA per SM with the deepest ring that fits
 struct DecodeKnobs {
-  int ctas_per_sm = 0, pdl = 1, cap = 0, deep = 0;
+  int ctas_per_sm = 0, pdl = 1, cap = 0;
   DecodeKnobs() {
     auto env = [](const char* k, int dflt) {
       const char* v = getenv(k);
@@ -526,7 +525,6 @@ struct DecodeKnobs {
     ctas_per_sm = env("PKV_DECODE_CTAS_PER_SM", 0);
     pdl = env("PKV_DECODE_PDL", 1);
     cap = env("PKV_DECODE_CAP", 0);
-    deep = env("PKV_DECODE_DEEP", 0);
   }
 };
 const DecodeKnobs& knobs() {
@@ -534,25 +532,25 @@ const DecodeKnobs& knobs() {
   return k;
 }
 
-template <typename T, int D, int RK, bool DEEP>
+template <typename T, int D, int NH, int RK>
 int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace, int64_t workspace_bytes,
                   cudaStream_t stream) {
-  using S = DecodeShape<D, RK, DEEP>;
+  using S = DecodeShape<D, NH, RK>;
   static int per_sm = 0;
   if (per_sm == 0) {
     cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<T, D, RK, DEEP>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        cudaFuncSetAttribute(decode_kernel<T, D, NH, RK>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, RK, DEEP>, kThreads, S::SMEM);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK>, kThreads, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     per_sm = std::max(1, occ);
   }
   const int want = knobs().ctas_per_sm > 0 ? std::min(knobs().ctas_per_sm, per_sm) : per_sm;
   const int ctas = std::min(num_sms() * want, kMaxCtas);
-  if (!workspace || workspace_bytes < ws_bytes(ctas, RK, D)) return PKV_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < ws_bytes(ctas, NH, RK, D)) return PKV_ERR_WORKSPACE;
   CUtensorMap tk, tv;
-  if (!get_pool_maps(pool, &tk, &tv, 1)) return PKV_ERR_CUDA;
+  if (!get_pool_maps(pool, &tk, &tv, NH)) return PKV_ERR_CUDA;
   DecodeParams p = p0;
   uint8_t* wsb = static_cast<uint8_t*>(workspace);
   p.counters = reinterpret_cast<int32_t*>(wsb);
@@ -569,16 +567,24 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = knobs().pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, RK, DEEP>, tk, tv, p));
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK>, tk, tv, p));
+}
+
+template <typename T, int D, int NH>
+int launch_rows(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
+  return p.group <= 8 ? launch_decode<T, D, NH, 8>(pool, p, ws, wsb, st)
+                      : launch_decode<T, D, NH, 16>(pool, p, ws, wsb, st);
 }
 
 template <typename T, int D>
-int launch_rows(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
-  if (knobs().deep)
-    return p.group <= 8 ? launch_decode<T, D, 8, true>(pool, p, ws, wsb, st)
-                        : launch_decode<T, D, 16, true>(pool, p, ws, wsb, st);
-  return p.group <= 8 ? launch_decode<T, D, 8, false>(pool, p, ws, wsb, st)
-                      : launch_decode<T, D, 16, false>(pool, p, ws, wsb, st);
+int launch_heads(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
+  switch (pool.num_kv_heads) {
+    case 1: return launch_rows<T, D, 1>(pool, p, ws, wsb, st);
+    case 2: return launch_rows<T, D, 2>(pool, p, ws, wsb, st);
+    case 4: return launch_rows<T, D, 4>(pool, p, ws, wsb, st);
+    case 8: return launch_rows<T, D, 8>(pool, p, ws, wsb, st);
+    default: return PKV_ERR_UNSUPPORTED;
+  }
 }
 
 }  // namespace
@@ -588,11 +594,13 @@ using namespace pkv;
 
 extern "C" int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
                                               int32_t block_size, int32_t head_dim, int32_t num_q_heads) {
-  if (batch <= 0 || batch > kMaxBatch || num_kv_heads <= 0 || num_kv_heads > kMaxKvHeads || max_blocks_per_seq <= 0 ||
-      block_size != kBS || (head_dim != 64 && head_dim != 128) || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0)
+  if (batch <= 0 || batch > kMaxBatch || max_blocks_per_seq <= 0 || block_size != kBS ||
+      (head_dim != 64 && head_dim != 128) || num_q_heads <= 0)
     return 0;
+  if (num_kv_heads != 1 && num_kv_heads != 2 && num_kv_heads != 4 && num_kv_heads != 8) return 0;
+  if (num_q_heads % num_kv_heads != 0) return 0;
   const int group = num_q_heads / num_kv_heads;
-  return ws_bytes(kMaxCtas, group <= 8 ? 8 : 16, head_dim);
+  return ws_bytes(kMaxCtas, num_kv_heads, group <= 8 ? 8 : 16, head_dim);
 }
 
 extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
@@ -609,7 +617,7 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   const int d = pool->head_dim, hkv = pool->num_kv_heads;
   if (pool->block_size != kBS || (d != 64 && d != 128)) return PKV_ERR_UNSUPPORTED;
   if (hkv <= 0 || num_q_heads <= 0 || num_q_heads % hkv != 0) return PKV_ERR_INVALID_ARGUMENT;
-  if (hkv > kMaxKvHeads) return PKV_ERR_UNSUPPORTED;
+  if (hkv != 1 && hkv != 2 && hkv != 4 && hkv != 8) return PKV_ERR_UNSUPPORTED;
   const int group = num_q_heads / hkv;
   if (group > 16) return PKV_ERR_UNSUPPORTED;
   if ((k_new == nullptr) != (v_new == nullptr)) return PKV_ERR_INVALID_ARGUMENT;
@@ -654,12 +662,12 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (pool->dtype == PKV_F16) {
-    return d == 64 ? launch_rows<__half, 64>(*pool, p, workspace, workspace_bytes, st)
-                   : launch_rows<__half, 128>(*pool, p, workspace, workspace_bytes, st);
+    return d == 64 ? launch_heads<__half, 64>(*pool, p, workspace, workspace_bytes, st)
+                   : launch_heads<__half, 128>(*pool, p, workspace, workspace_bytes, st);
   }
   if (pool->dtype == PKV_BF16) {
-    return d == 64 ? launch_rows<__nv_bfloat16, 64>(*pool, p, workspace, workspace_bytes, st)
-                   : launch_rows<__nv_bfloat16, 128>(*pool, p, workspace, workspace_bytes, st);
+    return d == 64 ? launch_heads<__nv_bfloat16, 64>(*pool, p, workspace, workspace_bytes, st)
+                   : launch_heads<__nv_bfloat16, 128>(*pool, p, workspace, workspace_bytes, st);
   }
   return PKV_ERR_UNSUPPORTED;
 }
