@@ -76,6 +76,11 @@ __device__ inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
       : "memory");
 }
 
+// One arrival (no transaction bytes).
+__device__ inline void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -235,9 +240,13 @@ __device__ inline uint32_t swz128(uint32_t row, uint32_t col) {
 // an ldmatrix reads are 8 distinct swizzle rows (no bank conflicts for D = 64 or 128).
 // heads_per_box > 1 widens the box over that many consecutive KV heads of the block:
 // shared-memory layout [heads][D/64][bs][64], head h's tile at h * bs * D * 2 bytes.
-int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool, int heads_per_box);
+// Box: 64 elements x block_size tokens x chunks_per_box 64-wide head_dim chunks (0 = all)
+// x heads_per_box KV heads of one (layer, block).
+int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool, int heads_per_box,
+                         int chunks_per_box = 0);
 // Cached K and V maps of a pool (one encode per pool and box shape).
-bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box = 1);
+bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box = 1,
+                   int chunks_per_box = 0);
 // Streaming multiprocessors of the current device (queried once).
 int num_sms();
 

@@ -9,23 +9,41 @@
 // its blocks (the new tokens were appended first, so one path serves both
 // cases), and only the causal part of each sequence is visited.
 //
-// One CTA per (16-token query tile of one sequence, kv head) with one warp per
-// query head of the GQA group: all warps share each K/V tile, which arrives by
-// TMA into a 4-stage ring of swizzled shared memory. Each warp runs the same
-// 16-key flash-attention step as the decode kernel (attn_tile.cuh).
-#include "attn_tile.cuh"
+// The contraction runs on the fifth-generation tensor cores (tcgen05) with the
+// accumulators in tensor memory. One CTA takes one KV head of one sequence and TQ of
+// its new tokens; the M = 128 rows of the MMA tile are those tokens x the GQA group's
+// query heads (16 x 7 = 112 rows for Qwen2's group of 7), so every K/V block read
+// serves the whole group. Keys stream in stages of NK = 64 (four blocks) through a
+// two-stage TMA ring: S = Q K^T (M 128 x N 64, fp32 in TMEM), an online softmax by
+// four warps that each own 32 TMEM lanes (one row per thread, no shuffles), P written
+// to shared memory as fp16/bf16, then O_stage = P V (M 128 x N head_dim, in TMEM),
+// which the softmax warps fold into their fp32 row accumulators with the running
+// rescale. One warp issues the TMA copies, one thread the MMAs; mbarriers (MMA
+// completion through tcgen05.commit) order the three roles. Only the causal part of
+// each sequence is visited; keys past a tile's last position are masked to -inf.
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace pkv {
 namespace {
 
 constexpr int kBS = 16;
-constexpr int kStages = 4;
+constexpr int kNK = 64;           // keys per stage
+constexpr int kKST = 2;           // ring stages
+constexpr int kPrefillThreads = 192;  // 4 softmax warps, 1 copy warp, 1 MMA warp
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int D> struct PrefillShape {
-  static constexpr int TILE = kBS * D * 2;
-  static constexpr int SMEM = 2 * kStages * TILE + kStages * 8 + 1024;
+// SPLIT: P goes to the tensor cores as hi + lo halves (bf16 keeps 8 bits of a weight;
+// the two halves together ~16, as the fp16 path has in one).
+template <int D, bool SPLIT> struct PrefillShape {
+  static constexpr int DC = D / 64;                  // 64-wide head_dim chunks
+  static constexpr int QB = DC * 128 * 128;          // Q tile: [DC][128 rows][64]
+  static constexpr int KSB = DC * kNK * 128;         // one stage of K (or V): [DC][NK keys][64]
+  static constexpr int PB = (kNK / 64) * 128 * 128;  // P tile: [NK/64][128 rows][64]
+  static constexpr int NP = SPLIT ? 2 : 1;           // P tiles (hi, lo)
+  static constexpr int SMEM = 1024 + QB + 2 * kKST * KSB + NP * PB + 16 * 8 + 16;
+  static constexpr int NCOLS = kNK + D <= 128 ? 128 : 256;  // TMEM columns: S then O
+  static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
 };
 
 struct PrefillParams {
@@ -38,132 +56,296 @@ struct PrefillParams {
   int32_t* status;
   int64_t out_st, out_sh, q_st, q_sh, table_stride;
   int32_t table_rows, table_cols;
-  int32_t group, layer, nbt;
+  int32_t group, layer, nbt, q_vec16;
   float scale_log2;
 };
 
-template <typename T, int D>
-__global__ void __launch_bounds__(512) prefill_kernel(const __grid_constant__ CUtensorMap tmap_k,
-                                                      const __grid_constant__ CUtensorMap tmap_v,
-                                                      const PrefillParams p) {
-  using S = PrefillShape<D>;
-  constexpr int TILE = S::TILE;
+template <typename T, int D, int TQ>
+__global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_BLOCKS)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                   const PrefillParams p) {
+  constexpr bool kSplit = !Dt<T>::kExactP;
+  using S = PrefillShape<D, kSplit>;
+  constexpr int DC = S::DC;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * kStages * TILE);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + S::QB;                 // [kKST][KSB]
+  uint8_t* sV = sK + kKST * S::KSB;         // [kKST][KSB]
+  uint8_t* sP = sV + kKST * S::KSB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + S::NP * S::PB);
+  uint64_t* kv_full = bars;       // [2] TMA bytes landed
+  uint64_t* kv_empty = bars + 2;  // [2] the stage's MMAs are done with it
+  uint64_t* q_ready = bars + 4;   // the softmax warps stored Q
+  uint64_t* s_full = bars + 5;    // S = Q K^T done
+  uint64_t* s_free = bars + 6;    // S read out
+  uint64_t* p_full = bars + 7;    // P stored
+  uint64_t* o_full = bars + 8;    // O_stage = P V done
+  uint64_t* o_free = bars + 9;    // O_stage read out
+  uint64_t* mma_done = bars + 10; // every MMA of the CTA has completed (before TMEM is freed)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int tile = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t4 = lane & 3;
   const int tok0 = p.cu[s];
   const int n_new = p.cu[s + 1] - tok0;
-  if (tile * 16 >= n_new) return;
+  if (tile * TQ >= n_new) return;
   const int start = p.starts[s];
-  const int rows_here = min(16, n_new - tile * 16);
-  const int q_first = start + tile * 16;             // position of the tile's first query
-  int kend = q_first + rows_here;                     // keys 0 .. kend-1 are visible to the tile
+  const int rows_here = min(TQ, n_new - tile * TQ);
+  const int q_first = start + tile * TQ;  // position of the tile's first query
+  int kend = q_first + rows_here;         // keys 0 .. kend-1 are visible to the tile
   if (kend > p.table_cols * kBS) {
     if (tid == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
     kend = p.table_cols * kBS;
   }
   const int nkb = (kend + kBS - 1) / kBS;
+  const int nst = (kend + kNK - 1) / kNK;
   int row = p.seq_rows ? p.seq_rows[s] : s;
   if (row < 0 || row >= p.table_rows) {
     if (tid == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
     row = -1;
   }
   const int32_t* table = row >= 0 ? p.tables + row * p.table_stride : nullptr;
+  const int G = p.group;
 
-  auto issue = [&](int i) {
-    const int st = i % kStages;
-    int blk = table ? table[i] : p.nbt - 1;
-    if (blk < 0 || blk >= p.nbt) {
-      report(p.status, PKV_ERR_OUT_OF_RANGE);
-      blk = p.nbt - 1;
-    }
-    const int c4 = p.layer * p.nbt + blk;
-    mbar_arrive_expect_tx(&full[st], 2 * TILE);
-    // Default L2 policy: the tiles of a sequence are re-read by its other query tiles.
-    tma_load_5d(smem + st * TILE, &tmap_k, 0, 0, 0, head, c4, &full[st]);
-    tma_load_5d(smem + (kStages + st) * TILE, &tmap_v, 0, 0, 0, head, c4, &full[st]);
-  };
-
-  const uint64_t deadline = global_ns() + kWaitBudgetNs;
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) mbar_init(&full[i], 1);
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(&kv_empty[0], 1);
+    mbar_init(&kv_empty[1], 1);
+    mbar_init(q_ready, 4);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 4);
+    mbar_init(mma_done, 1);
     fence_mbar_init();
   }
+  if (warp == 0) {
+    tmem_alloc(tslot, S::NCOLS);
+    tc_fence_before_sync();
+  }
   __syncthreads();
-  if (tid == 0) {
-    for (int i = 0; i < min(kStages, nkb); ++i) issue(i);
-  }
+  tc_fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint64_t deadline = global_ns() + kWaitBudgetNs;
 
-  // Q fragments of this warp's query head for the tile's 16 tokens (rows past the sequence are zero).
-  const int hq = head * p.group + warp;
-  uint32_t qa[D / 16][4];
-  {
-    const T* qb = reinterpret_cast<const T*>(p.q) + (int64_t)(tok0 + tile * 16) * p.q_st + (int64_t)hq * p.q_sh;
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA copies
+    if (lane == 0) {
+      for (int i = 0; i < nst; ++i) {
+        const int st = i % kKST;
+        if (i >= kKST && !mbar_wait_until(&kv_empty[st], ((i / kKST) - 1) & 1, deadline)) {
+          report(p.status, PKV_ERR_TIMEOUT);
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[st], 2 * S::KSB);
+        for (int b = 0; b < kNK / kBS; ++b) {
+          const int kb = i * (kNK / kBS) + b;
+          // Blocks past the visible keys are masked; the scratch block keeps their rows finite.
+          int blk = (kb < nkb && table) ? table[kb] : p.nbt - 1;
+          if (blk < 0 || blk >= p.nbt) {
+            report(p.status, PKV_ERR_OUT_OF_RANGE);
+            blk = p.nbt - 1;
+          }
+          const int c4 = p.layer * p.nbt + blk;
 #pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const int c0 = kk * 16 + 2 * t4;
-      qa[kk][0] = g < rows_here ? *reinterpret_cast<const uint32_t*>(qb + g * p.q_st + c0) : 0u;
-      qa[kk][1] = g + 8 < rows_here ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * p.q_st + c0) : 0u;
-      qa[kk][2] = g < rows_here ? *reinterpret_cast<const uint32_t*>(qb + g * p.q_st + c0 + 8) : 0u;
-      qa[kk][3] = g + 8 < rows_here ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * p.q_st + c0 + 8) : 0u;
+          for (int c = 0; c < DC; ++c) {
+            tma_load_5d(sK + st * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_k, 0, 0, c, head, c4, &kv_full[st]);
+            tma_load_5d(sV + st * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_v, 0, 0, c, head, c4, &kv_full[st]);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr bool kBf16 = Dt<T>::code == PKV_BF16;
+      constexpr uint32_t idesc_s = umma_idesc_f16(kBf16, false, 128, kNK);
+      constexpr uint32_t idesc_o = umma_idesc_f16(kBf16, true, 128, D);
+      bool ok = mbar_wait_until(q_ready, 0, deadline);
+      for (int i = 0; i < nst && ok; ++i) {
+        const int st = i % kKST;
+        ok = mbar_wait_until(&kv_full[st], (i / kKST) & 1, deadline) &&
+             (i == 0 || mbar_wait_until(s_free, (i - 1) & 1, deadline));
+        if (!ok) break;
+        tc_fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c = kk / 4, k16 = kk % 4;
+          const uint64_t a = umma_desc_sw128(smem_u32(sQ + c * 128 * 128 + k16 * 32), 16, 1024);
+          const uint64_t b = umma_desc_sw128(smem_u32(sK + st * S::KSB + c * kNK * 128 + k16 * 32), 16, 1024);
+          umma_f16_ss(tmem, a, b, idesc_s, kk > 0);
+        }
+        umma_commit(s_full);
+        ok = mbar_wait_until(p_full, i & 1, deadline) && (i == 0 || mbar_wait_until(o_free, (i - 1) & 1, deadline));
+        if (!ok) break;
+        tc_fence_after_sync();
+#pragma unroll
+        for (int h = 0; h < S::NP; ++h) {
+#pragma unroll
+          for (int kb = 0; kb < kNK / 16; ++kb) {
+            const uint64_t a =
+                umma_desc_sw128(smem_u32(sP + h * S::PB + (kb / 4) * 128 * 128 + (kb % 4) * 32), 16, 1024);
+            const uint64_t b = umma_desc_sw128(smem_u32(sV + st * S::KSB + kb * kBS * 128), kNK * 128, 1024);
+            umma_f16_ss(tmem + kNK, a, b, idesc_o, h > 0 || kb > 0);
+          }
+        }
+        umma_commit(o_full);
+        umma_commit(&kv_empty[st]);
+      }
+      if (!ok) report(p.status, PKV_ERR_TIMEOUT);
+      umma_commit(mma_done);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax warps: one row per thread
+    const int r = tid;  // TMEM lane = tile row
+    const int t = r / G, gq = r - t * G;
+    const bool valid = r < TQ * G && t < rows_here;
+    const int qpos = q_first + t;
+    // Q row r into the swizzled tile (zeros for rows without a query).
+    {
+      const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)(tok0 + tile * TQ + t) * p.q_st +
+                      (int64_t)(head * G + gq) * p.q_sh;
+#pragma unroll
+      for (int c16 = 0; c16 < D / 8; ++c16) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (valid) {
+          if (p.q_vec16) {
+            v = *reinterpret_cast<const uint4*>(qrow + 8 * c16);
+          } else {
+            const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qrow + 8 * c16);
+            v = make_uint4(q32[0], q32[1], q32[2], q32[3]);
+          }
+        }
+        const int c = c16 / 8, gr = c16 % 8;
+        *reinterpret_cast<uint4*>(sQ + c * 128 * 128 + r * 128 + ((gr ^ (r & 7)) * 16)) = v;
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_ready);
+
+    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    float acc[D];
+#pragma unroll
+    for (int e = 0; e < D; ++e) acc[e] = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nst; ++i) {
+      if (ok && !mbar_wait_until(s_full, i & 1, deadline)) ok = false;
+      tc_fence_after_sync();
+      const int key0 = i * kNK;
+      uint32_t sr[32];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < kNK / 32; ++cc) {
+        tmem_ld32(tl + cc * 32, sr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int key = key0 + cc * 32 + e;
+          if (valid && key <= qpos && key < kend) mx = fmaxf(mx, __uint_as_float(sr[e]) * p.scale_log2);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      const float mref = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet keeps p = 0
+      const float alpha = ex2(m - mref);
+      float lsum = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < kNK / 32; ++cc) {
+        tmem_ld32(tl + cc * 32, sr);
+        tmem_wait_ld();
+        uint32_t pk[16], pl[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int key = key0 + cc * 32 + e;
+          const bool v0 = valid && key <= qpos && key < kend;
+          const bool v1 = valid && key + 1 <= qpos && key + 1 < kend;
+          const float p0 = v0 ? ex2(__uint_as_float(sr[e]) * p.scale_log2 - mref) : 0.f;
+          const float p1 = v1 ? ex2(__uint_as_float(sr[e + 1]) * p.scale_log2 - mref) : 0.f;
+          pk[e / 2] = Dt<T>::pack(p0, p1);
+          const float2 hi = Dt<T>::unpack(pk[e / 2]);  // the sum uses the weights the MMA sees
+          if (kSplit) {
+            pl[e / 2] = Dt<T>::pack(p0 - hi.x, p1 - hi.y);
+            const float2 lo = Dt<T>::unpack(pl[e / 2]);
+            lsum += (hi.x + lo.x) + (hi.y + lo.y);
+          } else {
+            lsum += hi.x + hi.y;
+          }
+        }
+        // keys cc*32 .. cc*32+31 of row r: 16-byte granules 4*cc .. 4*cc+3 of the row
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int gr = cc * 4 + u;
+          const int off = r * 128 + ((gr ^ (r & 7)) * 16);
+          *reinterpret_cast<uint4*>(sP + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          if (kSplit)
+            *reinterpret_cast<uint4*>(sP + S::PB + off) =
+                make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
+        }
+      }
+      tc_fence_before_sync();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_free);
+        mbar_arrive(p_full);
+      }
+      l = l * alpha + lsum;
+      if (ok && !mbar_wait_until(o_full, i & 1, deadline)) ok = false;
+      tc_fence_after_sync();
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        tmem_ld32(tl + kNK + cc * 32, sr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[cc * 32 + e] = acc[cc * 32 + e] * alpha + __uint_as_float(sr[e]);
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);
+      m = m_new;
+    }
+    if (!ok) report(p.status, PKV_ERR_TIMEOUT);
+    if (valid && ok) {
+      const float inv = 1.f / l;
+      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(tok0 + tile * TQ + t) * p.out_st + (int64_t)(head * G + gq) * p.out_sh;
+#pragma unroll
+      for (int e = 0; e < D; e += 2) *reinterpret_cast<uint32_t*>(orow + e) = Dt<T>::pack(acc[e] * inv, acc[e + 1] * inv);
     }
   }
-
-  float m_r[2] = {-INFINITY, -INFINITY};
-  float l_r[2] = {0.f, 0.f};
-  float o[D / 8][4];
-#pragma unroll
-  for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  bool ok = true;
-  for (int i = 0; i < nkb; ++i) {
-    const int st = i % kStages;
-    if (ok && !mbar_wait_until(&full[st], (i / kStages) & 1, deadline)) {
-      report(p.status, PKV_ERR_TIMEOUT);
-      ok = false;
-    }
-    if (ok) {
-      attend_tile16<T, D>(qa, smem_u32(smem + st * TILE), smem_u32(smem + (kStages + st) * TILE), i * kBS,
-                          [q_first, rows_here](int r, int key) { return r < rows_here && key <= q_first + r; },
-                          p.scale_log2, m_r, l_r, o);
-    }
-    __syncthreads();  // every warp is done with stage st
-    if (tid == 0 && ok && i + kStages < nkb) issue(i + kStages);
-  }
-  finish_row_sums(l_r);
-  if (!ok) return;
-
-  T* ob = reinterpret_cast<T*>(p.out) + (int64_t)(tok0 + tile * 16) * p.out_st + (int64_t)hq * p.out_sh;
-#pragma unroll
-  for (int j = 0; j < D / 8; ++j) {
-    const int col = 8 * j + 2 * t4;
-    if (g < rows_here) {
-      const float inv = 1.f / l_r[0];
-      *reinterpret_cast<uint32_t*>(ob + g * p.out_st + col) = Dt<T>::pack(o[j][0] * inv, o[j][1] * inv);
-    }
-    if (g + 8 < rows_here) {
-      const float inv = 1.f / l_r[1];
-      *reinterpret_cast<uint32_t*>(ob + (g + 8) * p.out_st + col) = Dt<T>::pack(o[j][2] * inv, o[j][3] * inv);
-    }
+  __syncthreads();
+  if (warp == 0) {
+    if (!mbar_wait_until(mma_done, 0, global_ns() + kWaitBudgetNs) && lane == 0) report(p.status, PKV_ERR_TIMEOUT);
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, S::NCOLS);
   }
 }
 
-template <typename T, int D>
-int launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& p, int tiles, int hkv,
+template <typename T, int D, int TQ>
+int launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& p, int max_new, int hkv,
                    int seqs, cudaStream_t st) {
-  using S = PrefillShape<D>;
+  using S = PrefillShape<D, !Dt<T>::kExactP>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+    cudaError_t e =
+        cudaFuncSetAttribute(prefill_kernel<T, D, TQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     configured = true;
   }
-  dim3 grid(tiles, hkv, seqs);
-  prefill_kernel<T, D><<<grid, 32 * p.group, S::SMEM, st>>>(tk, tv, p);
+  dim3 grid((max_new + TQ - 1) / TQ, hkv, seqs);
+  prefill_kernel<T, D, TQ><<<grid, kPrefillThreads, S::SMEM, st>>>(tk, tv, p);
   return launch_status();
+}
+
+// Query tokens per CTA: the tile's rows are tokens x group <= 128.
+template <typename T, int D>
+int launch_group(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& p, int max_new, int hkv,
+                 int seqs, cudaStream_t st) {
+  return p.group <= 8 ? launch_prefill<T, D, 16>(tk, tv, p, max_new, hkv, seqs, st)
+                      : launch_prefill<T, D, 8>(tk, tv, p, max_new, hkv, seqs, st);
 }
 
 }  // namespace
@@ -193,7 +375,7 @@ extern "C" int pkv_prefill_attention(const pkv_pool* pool, int32_t layer, const 
   if (!aligned4(q) || !aligned4(out) || ((q_stride_t | q_stride_h | out_stride_t | out_stride_h) & 1))
     return PKV_ERR_INVALID_ARGUMENT;
   CUtensorMap tk, tv;
-  if (!get_pool_maps(*pool, &tk, &tv)) return PKV_ERR_CUDA;
+  if (!get_pool_maps(*pool, &tk, &tv, 1, 1)) return PKV_ERR_CUDA;  // one head, one 64-wide chunk per copy
   PrefillParams p{};
   p.out = out;
   p.q = q;
@@ -213,13 +395,13 @@ extern "C" int pkv_prefill_attention(const pkv_pool* pool, int32_t layer, const 
   p.layer = layer;
   p.nbt = pool->num_blocks_total;
   p.scale_log2 = scale * kLog2e;
-  const int tiles = (max_new_tokens + 15) / 16;
+  p.q_vec16 = (reinterpret_cast<uintptr_t>(q) & 15) == 0 && ((q_stride_t | q_stride_h) & 7) == 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (pool->dtype == PKV_F16)
-    return d == 64 ? launch_prefill<__half, 64>(tk, tv, p, tiles, hkv, num_seqs, st)
-                   : launch_prefill<__half, 128>(tk, tv, p, tiles, hkv, num_seqs, st);
+    return d == 64 ? launch_group<__half, 64>(tk, tv, p, max_new_tokens, hkv, num_seqs, st)
+                   : launch_group<__half, 128>(tk, tv, p, max_new_tokens, hkv, num_seqs, st);
   if (pool->dtype == PKV_BF16)
-    return d == 64 ? launch_prefill<__nv_bfloat16, 64>(tk, tv, p, tiles, hkv, num_seqs, st)
-                   : launch_prefill<__nv_bfloat16, 128>(tk, tv, p, tiles, hkv, num_seqs, st);
+    return d == 64 ? launch_group<__nv_bfloat16, 64>(tk, tv, p, max_new_tokens, hkv, num_seqs, st)
+                   : launch_group<__nv_bfloat16, 128>(tk, tv, p, max_new_tokens, hkv, num_seqs, st);
   return PKV_ERR_UNSUPPORTED;
 }

@@ -42,7 +42,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct MapEntry {
   pkv_pool pool;
-  int heads_per_box;
+  int heads_per_box, chunks_per_box;
   CUtensorMap k, v;
 };
 std::mutex g_map_mutex;
@@ -59,7 +59,8 @@ int cuda_status(cudaError_t e) {
   return PKV_ERR_CUDA;
 }
 
-int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool, int heads_per_box) {
+int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& pool, int heads_per_box,
+                         int chunks_per_box) {
   auto fn = encode_fn();
   if (!fn) {
     g_last_cuda_error = "cuTensorMapEncodeTiled is not available from the driver";
@@ -71,7 +72,8 @@ int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& poo
                         (cuuint64_t)pool.num_layers * (cuuint64_t)pool.num_blocks_total};
   cuuint64_t strides[4] = {(cuuint64_t)d * esz, 64 * esz, (cuuint64_t)bs * d * esz,
                            (cuuint64_t)pool.num_kv_heads * bs * d * esz};
-  cuuint32_t box[5] = {64, (cuuint32_t)bs, (cuuint32_t)(d / 64), (cuuint32_t)heads_per_box, 1};
+  const cuuint32_t chunks = chunks_per_box > 0 ? (cuuint32_t)chunks_per_box : (cuuint32_t)(d / 64);
+  cuuint32_t box[5] = {64, (cuuint32_t)bs, chunks, (cuuint32_t)heads_per_box, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUtensorMapDataType dt =
       pool.dtype == PKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -84,10 +86,10 @@ int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& poo
   return PKV_OK;
 }
 
-bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box) {
+bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box, int chunks_per_box) {
   std::lock_guard<std::mutex> lock(g_map_mutex);
   for (const MapEntry& e : g_maps) {
-    if (same_pool(e.pool, pool) && e.heads_per_box == heads_per_box) {
+    if (same_pool(e.pool, pool) && e.heads_per_box == heads_per_box && e.chunks_per_box == chunks_per_box) {
       *tk = e.k;
       *tv = e.v;
       return true;
@@ -97,8 +99,9 @@ bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int h
   std::memset(&e, 0, sizeof(e));
   e.pool = pool;
   e.heads_per_box = heads_per_box;
-  if (make_pool_tensor_map(&e.k, pool.k, pool, heads_per_box) != PKV_OK) return false;
-  if (make_pool_tensor_map(&e.v, pool.v, pool, heads_per_box) != PKV_OK) return false;
+  e.chunks_per_box = chunks_per_box;
+  if (make_pool_tensor_map(&e.k, pool.k, pool, heads_per_box, chunks_per_box) != PKV_OK) return false;
+  if (make_pool_tensor_map(&e.v, pool.v, pool, heads_per_box, chunks_per_box) != PKV_OK) return false;
   if (g_maps.size() >= 64) g_maps.erase(g_maps.begin());
   g_maps.push_back(e);
   *tk = e.k;

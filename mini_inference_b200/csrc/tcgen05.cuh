@@ -1,0 +1,88 @@
+// Fifth-generation tensor core (tcgen05) and tensor memory (TMEM) wrappers for sm_100a,
+// written from the PTX ISA's description of these instructions.
+//
+// Conventions used by the kernels here:
+//  * Operands A and B live in shared memory in the 128-byte-swizzled layout that TMA
+//    writes with CU_TENSOR_MAP_SWIZZLE_128B: 128-byte rows, 8-row atoms of 1024 bytes,
+//    16-byte granule g of row r stored at granule g ^ (r % 8). A tile's base is
+//    1024-byte aligned.
+//  * The accumulator D lives in TMEM: lane = row of the 128-row tile, column = 32-bit
+//    element. A warp can read only its own quarter of the lanes (32 * (warp % 4) ...).
+//  * One thread issues the MMAs of a CTA; tcgen05.commit makes an mbarrier track their
+//    completion.
+#pragma once
+
+#include "common.cuh"
+
+namespace pkv {
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), descriptor version 1.
+//   K-major operand: rows (M or N) at 128 B, 8-row groups `sbo` bytes apart; a K step of
+//   16 16-bit elements is a +32 B start offset inside the 128 B row. `lbo` is unused (1).
+//   MN-major operand: 64-element MN chunks `lbo` bytes apart, 8-row K groups `sbo` apart.
+__device__ inline uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)2 << 61;  // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation: A, B both fp16 (bf16 = false)
+// or both bf16, K-major A, B K-major (b_mn = false) or MN-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, bool b_mn, int m, int n) {
+  return (1u << 4)                             // D format: f32
+         | ((bf16 ? 1u : 0u) << 7)             // A format
+         | ((bf16 ? 1u : 0u) << 10)            // B format
+         | ((b_mn ? 1u : 0u) << 16)            // B major
+         | ((uint32_t)(n >> 3) << 17)          // N / 8
+         | ((uint32_t)(m >> 4) << 24);         // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T (per the descriptors); accumulate = false overwrites D.
+__device__ inline void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                   bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// The mbarrier gets one arrival when every tcgen05 operation this thread issued before
+// has completed.
+__device__ inline void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// TMEM allocation by one full warp: the base address is written to *slot (shared memory).
+__device__ inline void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ inline void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ inline void tc_fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ inline void tc_fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane (lane = 32 * (warp % 4) + lane id).
+__device__ inline void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ inline void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+}  // namespace pkv
