@@ -28,8 +28,8 @@ namespace pkv {
 namespace {
 
 constexpr int kBS = 16;
-constexpr int kNK = 64;           // keys per stage
-constexpr int kKST = 2;           // ring stages
+constexpr int kNK = 64;               // keys per stage
+constexpr int kKST = 3;               // K/V ring stages
 constexpr int kPrefillThreads = 192;  // 4 softmax warps, 1 copy warp, 1 MMA warp
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -40,9 +40,11 @@ template <int D, bool SPLIT> struct PrefillShape {
   static constexpr int QB = DC * 128 * 128;          // Q tile: [DC][128 rows][64]
   static constexpr int KSB = DC * kNK * 128;         // one stage of K (or V): [DC][NK keys][64]
   static constexpr int PB = (kNK / 64) * 128 * 128;  // P tile: [NK/64][128 rows][64]
-  static constexpr int NP = SPLIT ? 2 : 1;           // P tiles (hi, lo)
-  static constexpr int SMEM = 1024 + QB + 2 * kKST * KSB + NP * PB + 16 * 8 + 16;
-  static constexpr int NCOLS = kNK + D <= 128 ? 128 : 256;  // TMEM columns: S then O
+  static constexpr int NP = SPLIT ? 2 : 1;           // P tiles per buffer (hi, lo)
+  static constexpr int SMEM = 1024 + QB + 2 * kKST * KSB + 2 * NP * PB + 24 * 8 + 16;
+  // TMEM: S double-buffered at columns 0 and NK, O double-buffered at 2 NK and 2 NK + D.
+  static constexpr int COLS = 2 * kNK + 2 * D;
+  static constexpr int NCOLS = COLS <= 128 ? 128 : (COLS <= 256 ? 256 : 512);
   static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
 };
 
@@ -60,6 +62,10 @@ struct PrefillParams {
   float scale_log2;
 };
 
+// Pipeline (stage i = keys 64 i .. 64 i + 63): the MMA thread issues S(0), then for each
+// i: S(i+1) into the other S buffer, then O(i) = P(i) V(i) into O buffer i % 2 once the
+// softmax warps stored P(i). The softmax warps turn S(i) into P(i) while the tensor cores
+// compute S(i+1) and O(i-1), and fold O(i-1) into their accumulators one stage late.
 template <typename T, int D, int TQ>
 __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_BLOCKS)
     prefill_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -72,18 +78,18 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + S::QB;                 // [kKST][KSB]
   uint8_t* sV = sK + kKST * S::KSB;         // [kKST][KSB]
-  uint8_t* sP = sV + kKST * S::KSB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + S::NP * S::PB);
-  uint64_t* kv_full = bars;       // [2] TMA bytes landed
-  uint64_t* kv_empty = bars + 2;  // [2] the stage's MMAs are done with it
-  uint64_t* q_ready = bars + 4;   // the softmax warps stored Q
-  uint64_t* s_full = bars + 5;    // S = Q K^T done
-  uint64_t* s_free = bars + 6;    // S read out
-  uint64_t* p_full = bars + 7;    // P stored
-  uint64_t* o_full = bars + 8;    // O_stage = P V done
-  uint64_t* o_free = bars + 9;    // O_stage read out
-  uint64_t* mma_done = bars + 10; // every MMA of the CTA has completed (before TMEM is freed)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint8_t* sP = sV + kKST * S::KSB;         // [2][NP][PB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * S::NP * S::PB);
+  uint64_t* kv_full = bars;        // [kKST] TMA bytes landed
+  uint64_t* kv_empty = bars + 3;   // [kKST] the stage's MMAs are done with it
+  uint64_t* s_full = bars + 6;     // [2] S = Q K^T done
+  uint64_t* s_free = bars + 8;     // [2] S read out
+  uint64_t* p_full = bars + 10;    // [2] P stored
+  uint64_t* o_full = bars + 12;    // [2] O(i) = P V done
+  uint64_t* o_free = bars + 14;    // [2] O(i) read out
+  uint64_t* q_ready = bars + 16;   // the softmax warps stored Q
+  uint64_t* mma_done = bars + 17;  // every MMA of the CTA has completed (before TMEM is freed)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 24);
 
   const int tile = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -109,16 +115,18 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   const int G = p.group;
 
   if (tid == 0) {
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(&kv_empty[0], 1);
-    mbar_init(&kv_empty[1], 1);
+    for (int i = 0; i < kKST; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
     mbar_init(q_ready, 4);
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, 4);
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
@@ -130,6 +138,8 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   tc_fence_after_sync();
   const uint32_t tmem = *tslot;
   const uint64_t deadline = global_ns() + kWaitBudgetNs;
+  auto s_col = [](int b) { return (uint32_t)(b * kNK); };
+  auto o_col = [](int b) { return (uint32_t)(2 * kNK + b * D); };
 
   if (warp == 4) {
     // ---------------------------------------------------------------- TMA copies
@@ -164,36 +174,43 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
       constexpr bool kBf16 = Dt<T>::code == PKV_BF16;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBf16, false, 128, kNK);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBf16, true, 128, D);
-      bool ok = mbar_wait_until(q_ready, 0, deadline);
-      for (int i = 0; i < nst && ok; ++i) {
-        const int st = i % kKST;
-        ok = mbar_wait_until(&kv_full[st], (i / kKST) & 1, deadline) &&
-             (i == 0 || mbar_wait_until(s_free, (i - 1) & 1, deadline));
-        if (!ok) break;
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % kKST, b = j % 2;
+        if (!mbar_wait_until(&kv_full[st], (j / kKST) & 1, deadline)) return false;
+        if (j >= 2 && !mbar_wait_until(&s_free[b], ((j / 2) - 1) & 1, deadline)) return false;
         tc_fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int c = kk / 4, k16 = kk % 4;
           const uint64_t a = umma_desc_sw128(smem_u32(sQ + c * 128 * 128 + k16 * 32), 16, 1024);
-          const uint64_t b = umma_desc_sw128(smem_u32(sK + st * S::KSB + c * kNK * 128 + k16 * 32), 16, 1024);
-          umma_f16_ss(tmem, a, b, idesc_s, kk > 0);
+          const uint64_t bd = umma_desc_sw128(smem_u32(sK + st * S::KSB + c * kNK * 128 + k16 * 32), 16, 1024);
+          umma_f16_ss(tmem + s_col(b), a, bd, idesc_s, kk > 0);
         }
-        umma_commit(s_full);
-        ok = mbar_wait_until(p_full, i & 1, deadline) && (i == 0 || mbar_wait_until(o_free, (i - 1) & 1, deadline));
-        if (!ok) break;
+        umma_commit(&s_full[b]);
+        return true;
+      };
+      auto issue_o = [&](int j) -> bool {
+        const int st = j % kKST, b = j % 2;
+        if (!mbar_wait_until(&p_full[b], (j / 2) & 1, deadline)) return false;
+        if (j >= 2 && !mbar_wait_until(&o_free[b], ((j / 2) - 1) & 1, deadline)) return false;
         tc_fence_after_sync();
+        uint8_t* pb = sP + b * S::NP * S::PB;
 #pragma unroll
         for (int h = 0; h < S::NP; ++h) {
 #pragma unroll
           for (int kb = 0; kb < kNK / 16; ++kb) {
-            const uint64_t a =
-                umma_desc_sw128(smem_u32(sP + h * S::PB + (kb / 4) * 128 * 128 + (kb % 4) * 32), 16, 1024);
-            const uint64_t b = umma_desc_sw128(smem_u32(sV + st * S::KSB + kb * kBS * 128), kNK * 128, 1024);
-            umma_f16_ss(tmem + kNK, a, b, idesc_o, h > 0 || kb > 0);
+            const uint64_t a = umma_desc_sw128(smem_u32(pb + h * S::PB + (kb / 4) * 128 * 128 + (kb % 4) * 32), 16, 1024);
+            const uint64_t bd = umma_desc_sw128(smem_u32(sV + st * S::KSB + kb * kBS * 128), kNK * 128, 1024);
+            umma_f16_ss(tmem + o_col(b), a, bd, idesc_o, h > 0 || kb > 0);
           }
         }
-        umma_commit(o_full);
+        umma_commit(&o_full[b]);
         umma_commit(&kv_empty[st]);
+        return true;
+      };
+      bool ok = mbar_wait_until(q_ready, 0, deadline) && (nst == 0 || issue_s(0));
+      for (int i = 0; i < nst && ok; ++i) {
+        ok = (i + 1 >= nst || issue_s(i + 1)) && issue_o(i);
       }
       if (!ok) report(p.status, PKV_ERR_TIMEOUT);
       umma_commit(mma_done);
@@ -228,43 +245,62 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
     if (lane == 0) mbar_arrive(q_ready);
 
     const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
     float acc[D];
 #pragma unroll
     for (int e = 0; e < D; ++e) acc[e] = 0.f;
     bool ok = true;
-    for (int i = 0; i < nst; ++i) {
-      if (ok && !mbar_wait_until(s_full, i & 1, deadline)) ok = false;
+    // acc = acc * alpha + O(j): the stage's P V, read from its TMEM buffer.
+    auto fold = [&](int j, float alpha) {
+      const int b = j % 2;
+      if (ok && !mbar_wait_until(&o_full[b], (j / 2) & 1, deadline)) ok = false;
       tc_fence_after_sync();
-      const int key0 = i * kNK;
-      uint32_t sr[32];
-      float mx = -INFINITY;
 #pragma unroll
-      for (int cc = 0; cc < kNK / 32; ++cc) {
-        tmem_ld32(tl + cc * 32, sr);
+      for (int c2 = 0; c2 < D / 64; ++c2) {
+        uint32_t ob[64];
+        tmem_ld32(tl + o_col(b) + c2 * 64, *reinterpret_cast<uint32_t(*)[32]>(ob));
+        tmem_ld32(tl + o_col(b) + c2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(ob + 32));
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = key0 + cc * 32 + e;
-          if (valid && key <= qpos && key < kend) mx = fmaxf(mx, __uint_as_float(sr[e]) * p.scale_log2);
-        }
+        for (int e = 0; e < 64; ++e) acc[c2 * 64 + e] = acc[c2 * 64 + e] * alpha + __uint_as_float(ob[e]);
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[b]);
+    };
+    for (int i = 0; i < nst; ++i) {
+      const int b = i % 2;
+      if (ok && !mbar_wait_until(&s_full[b], (i / 2) & 1, deadline)) ok = false;
+      tc_fence_after_sync();
+      const int key0 = i * kNK;
+      // All NK scores of the row in registers with one wait: scaled, masked to -inf.
+      uint32_t sa[kNK];
+#pragma unroll
+      for (int cc = 0; cc < kNK / 32; ++cc) tmem_ld32(tl + s_col(b) + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(sa + cc * 32));
+      tmem_wait_ld();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < kNK; ++e) {
+        const int key = key0 + e;
+        const float v = (valid && key <= qpos && key < kend) ? __uint_as_float(sa[e]) * p.scale_log2 : -INFINITY;
+        sa[e] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
       }
       const float m_new = fmaxf(m, mx);
       const float mref = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet keeps p = 0
       const float alpha = ex2(m - mref);
       float lsum = 0.f;
+      uint8_t* pb = sP + b * S::NP * S::PB;
+      tc_fence_before_sync();  // S is in registers: its buffer may take S(i + 2)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
 #pragma unroll
       for (int cc = 0; cc < kNK / 32; ++cc) {
-        tmem_ld32(tl + cc * 32, sr);
-        tmem_wait_ld();
         uint32_t pk[16], pl[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          const int key = key0 + cc * 32 + e;
-          const bool v0 = valid && key <= qpos && key < kend;
-          const bool v1 = valid && key + 1 <= qpos && key + 1 < kend;
-          const float p0 = v0 ? ex2(__uint_as_float(sr[e]) * p.scale_log2 - mref) : 0.f;
-          const float p1 = v1 ? ex2(__uint_as_float(sr[e + 1]) * p.scale_log2 - mref) : 0.f;
+          const float p0 = ex2(__uint_as_float(sa[cc * 32 + e]) - mref);  // ex2(-inf) = 0 for masked keys
+          const float p1 = ex2(__uint_as_float(sa[cc * 32 + e + 1]) - mref);
           pk[e / 2] = Dt<T>::pack(p0, p1);
           const float2 hi = Dt<T>::unpack(pk[e / 2]);  // the sum uses the weights the MMA sees
           if (kSplit) {
@@ -279,35 +315,22 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int gr = cc * 4 + u;
-          const int off = r * 128 + ((gr ^ (r & 7)) * 16);
-          *reinterpret_cast<uint4*>(sP + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          const int off = (gr / 8) * 128 * 128 + r * 128 + (((gr % 8) ^ (r & 7)) * 16);
+          *reinterpret_cast<uint4*>(pb + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
           if (kSplit)
-            *reinterpret_cast<uint4*>(sP + S::PB + off) =
+            *reinterpret_cast<uint4*>(pb + S::PB + off) =
                 make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
         }
       }
-      tc_fence_before_sync();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free);
-        mbar_arrive(p_full);
-      }
+      if (lane == 0) mbar_arrive(&p_full[b]);
       l = l * alpha + lsum;
-      if (ok && !mbar_wait_until(o_full, i & 1, deadline)) ok = false;
-      tc_fence_after_sync();
-#pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
-        tmem_ld32(tl + kNK + cc * 32, sr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) acc[cc * 32 + e] = acc[cc * 32 + e] * alpha + __uint_as_float(sr[e]);
-      }
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_free);
+      if (i > 0) fold(i - 1, alpha_prev);
+      alpha_prev = alpha;
       m = m_new;
     }
+    if (nst > 0) fold(nst - 1, alpha_prev);
     if (!ok) report(p.status, PKV_ERR_TIMEOUT);
     if (valid && ok) {
       const float inv = 1.f / l;
