@@ -76,6 +76,11 @@ __device__ inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
       : "memory");
 }
 
+// Named barrier `id` (1..15; 0 is __syncthreads) over `threads` threads (a multiple of 32).
+__device__ inline void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // One arrival (no transaction bytes).
 __device__ inline void mbar_arrive(uint64_t* bar) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");

@@ -30,7 +30,8 @@ namespace {
 constexpr int kBS = 16;
 constexpr int kNK = 64;               // keys per stage
 constexpr int kKST = 3;               // K/V ring stages
-constexpr int kPrefillThreads = 192;  // 4 softmax warps, 1 copy warp, 1 MMA warp
+constexpr int kSoftWarps = 8;          // softmax warps: two per TMEM lane quarter (half a row each)
+constexpr int kPrefillThreads = (kSoftWarps + 2) * 32;  // + 1 copy warp, 1 MMA warp
 constexpr float kLog2e = 1.4426950408889634f;
 
 // SPLIT: P goes to the tensor cores as hi + lo halves (bf16 keeps 8 bits of a weight;
@@ -41,7 +42,7 @@ template <int D, bool SPLIT> struct PrefillShape {
   static constexpr int KSB = DC * kNK * 128;         // one stage of K (or V): [DC][NK keys][64]
   static constexpr int PB = (kNK / 64) * 128 * 128;  // P tile: [NK/64][128 rows][64]
   static constexpr int NP = SPLIT ? 2 : 1;           // P tiles per buffer (hi, lo)
-  static constexpr int SMEM = 1024 + QB + 2 * kKST * KSB + 2 * NP * PB + 24 * 8 + 16;
+  static constexpr int SMEM = 1024 + QB + 2 * kKST * KSB + 2 * NP * PB + 24 * 8 + 16 + 3 * 2 * 128 * 4;
   // TMEM: S double-buffered at columns 0 and NK, O double-buffered at 2 NK and 2 NK + D.
   static constexpr int COLS = 2 * kNK + 2 * D;
   static constexpr int NCOLS = COLS <= 128 ? 128 : (COLS <= 256 ? 256 : 512);
@@ -90,6 +91,8 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   uint64_t* q_ready = bars + 16;   // the softmax warps stored Q
   uint64_t* mma_done = bars + 17;  // every MMA of the CTA has completed (before TMEM is freed)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 24);
+  float* s_mx = reinterpret_cast<float*>(bars + 26);  // [2 stage parities][2 halves][128 rows] partial row maxima
+  float* s_l = s_mx + 2 * 2 * 128;                    // [2 halves][128 rows] final partial row sums
 
   const int tile = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -121,12 +124,12 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&s_free[i], kSoftWarps);
+      mbar_init(&p_full[i], kSoftWarps);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 4);
+      mbar_init(&o_free[i], kSoftWarps);
     }
-    mbar_init(q_ready, 4);
+    mbar_init(q_ready, kSoftWarps);
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
@@ -141,34 +144,37 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   auto s_col = [](int b) { return (uint32_t)(b * kNK); };
   auto o_col = [](int b) { return (uint32_t)(2 * kNK + b * D); };
 
-  if (warp == 4) {
+  if (warp == kSoftWarps) {
     // ---------------------------------------------------------------- TMA copies
-    if (lane == 0) {
-      for (int i = 0; i < nst; ++i) {
-        const int st = i % kKST;
+    // One copy per lane (a lane issues one (block, tensor, head_dim chunk) of the stage):
+    // a single issuing lane cannot keep up with 2 KB copies.
+    constexpr int kCopies = (kNK / kBS) * 2 * DC;
+    bool ok = true;
+    for (int i = 0; i < nst && ok; ++i) {
+      const int st = i % kKST;
+      if (lane == 0) {
         if (i >= kKST && !mbar_wait_until(&kv_empty[st], ((i / kKST) - 1) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
-          break;
+          ok = false;
         }
-        mbar_arrive_expect_tx(&kv_full[st], 2 * S::KSB);
-        for (int b = 0; b < kNK / kBS; ++b) {
-          const int kb = i * (kNK / kBS) + b;
-          // Blocks past the visible keys are masked; the scratch block keeps their rows finite.
-          int blk = (kb < nkb && table) ? table[kb] : p.nbt - 1;
-          if (blk < 0 || blk >= p.nbt) {
-            report(p.status, PKV_ERR_OUT_OF_RANGE);
-            blk = p.nbt - 1;
-          }
-          const int c4 = p.layer * p.nbt + blk;
-#pragma unroll
-          for (int c = 0; c < DC; ++c) {
-            tma_load_5d(sK + st * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_k, 0, 0, c, head, c4, &kv_full[st]);
-            tma_load_5d(sV + st * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_v, 0, 0, c, head, c4, &kv_full[st]);
-          }
+        if (ok) mbar_arrive_expect_tx(&kv_full[st], 2 * S::KSB);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok && lane < kCopies) {
+        const int b = lane / (2 * DC), tensor = (lane / DC) % 2, c = lane % DC;
+        const int kb = i * (kNK / kBS) + b;
+        // Blocks past the visible keys are masked; the scratch block keeps their rows finite.
+        int blk = (kb < nkb && table) ? table[kb] : p.nbt - 1;
+        if (blk < 0 || blk >= p.nbt) {
+          report(p.status, PKV_ERR_OUT_OF_RANGE);
+          blk = p.nbt - 1;
         }
+        const int c4 = p.layer * p.nbt + blk;
+        uint8_t* dst = (tensor ? sV : sK) + st * S::KSB + c * kNK * 128 + b * kBS * 128;
+        tma_load_5d(dst, tensor ? &tmap_v : &tmap_k, 0, 0, c, head, c4, &kv_full[st]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kSoftWarps + 1) {
     // ---------------------------------------------------------------- MMA issue
     if (lane == 0) {
       constexpr bool kBf16 = Dt<T>::code == PKV_BF16;
@@ -216,17 +222,23 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
       umma_commit(mma_done);
     }
   } else {
-    // ---------------------------------------------------------------- softmax warps: one row per thread
-    const int r = tid;  // TMEM lane = tile row
+    // ---------------------------------------------------------------- softmax warps: half a row per thread
+    // Warps w and w + 4 read TMEM lanes 32 (w % 4) .. + 31: the same rows. Half hf of a row
+    // owns keys 32 hf .. 32 hf + 31 of every stage and output columns hf D/2 .. + D/2; the
+    // two halves trade their partial maxima through shared memory once per stage.
+    constexpr int KH = kNK / 2, DH = D / 2;
+    const int hf = warp / 4;
+    const int r = (warp % 4) * 32 + lane;  // TMEM lane = tile row
     const int t = r / G, gq = r - t * G;
     const bool valid = r < TQ * G && t < rows_here;
     const int qpos = q_first + t;
-    // Q row r into the swizzled tile (zeros for rows without a query).
+    // Q row r (this thread's half of the granules) into the swizzled tile, zeros without a query.
     {
       const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)(tok0 + tile * TQ + t) * p.q_st +
                       (int64_t)(head * G + gq) * p.q_sh;
 #pragma unroll
-      for (int c16 = 0; c16 < D / 8; ++c16) {
+      for (int k = 0; k < D / 16; ++k) {
+        const int c16 = hf * (D / 16) + k;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (valid) {
           if (p.q_vec16) {
@@ -244,26 +256,25 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
     __syncwarp();
     if (lane == 0) mbar_arrive(q_ready);
 
-    const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t tl = tmem + ((uint32_t)((warp % 4) * 32) << 16);
+    const int pair_bar = 1 + warp % 4;  // named barrier of warps w and w + 4
     float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    float acc[D];
+    float acc[DH];
 #pragma unroll
-    for (int e = 0; e < D; ++e) acc[e] = 0.f;
+    for (int e = 0; e < DH; ++e) acc[e] = 0.f;
     bool ok = true;
-    // acc = acc * alpha + O(j): the stage's P V, read from its TMEM buffer.
+    // acc = acc * alpha + O(j) (this thread's half of the columns), from its TMEM buffer.
     auto fold = [&](int j, float alpha) {
       const int b = j % 2;
       if (ok && !mbar_wait_until(&o_full[b], (j / 2) & 1, deadline)) ok = false;
       tc_fence_after_sync();
+      uint32_t ob[DH];
 #pragma unroll
-      for (int c2 = 0; c2 < D / 64; ++c2) {
-        uint32_t ob[64];
-        tmem_ld32(tl + o_col(b) + c2 * 64, *reinterpret_cast<uint32_t(*)[32]>(ob));
-        tmem_ld32(tl + o_col(b) + c2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(ob + 32));
-        tmem_wait_ld();
+      for (int c = 0; c < DH / 32; ++c)
+        tmem_ld32(tl + o_col(b) + hf * DH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(ob + c * 32));
+      tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 64; ++e) acc[c2 * 64 + e] = acc[c2 * 64 + e] * alpha + __uint_as_float(ob[e]);
-      }
+      for (int e = 0; e < DH; ++e) acc[e] = acc[e] * alpha + __uint_as_float(ob[e]);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[b]);
@@ -272,71 +283,78 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
       const int b = i % 2;
       if (ok && !mbar_wait_until(&s_full[b], (i / 2) & 1, deadline)) ok = false;
       tc_fence_after_sync();
-      const int key0 = i * kNK;
-      // All NK scores of the row in registers with one wait: scaled, masked to -inf.
-      uint32_t sa[kNK];
-#pragma unroll
-      for (int cc = 0; cc < kNK / 32; ++cc) tmem_ld32(tl + s_col(b) + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(sa + cc * 32));
+      const int key0 = i * kNK + hf * KH;
+      uint32_t sa[KH];
+      tmem_ld32(tl + s_col(b) + hf * KH, sa);
       tmem_wait_ld();
+      tc_fence_before_sync();  // S is in registers: its buffer may take S(i + 2)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
+      // Raw scores; the max is taken before scaling (the scale is positive). A stage whose
+      // every key is visible to every row of the tile needs no mask.
       float mx = -INFINITY;
+      if ((i + 1) * kNK - 1 <= q_first && (i + 1) * kNK <= kend) {
 #pragma unroll
-      for (int e = 0; e < kNK; ++e) {
-        const int key = key0 + e;
-        const float v = (valid && key <= qpos && key < kend) ? __uint_as_float(sa[e]) * p.scale_log2 : -INFINITY;
-        sa[e] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int e = 0; e < KH; ++e) mx = fmaxf(mx, __uint_as_float(sa[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < KH; ++e) {
+          const int key = key0 + e;
+          if (!(valid && key <= qpos && key < kend)) sa[e] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, __uint_as_float(sa[e]));
+        }
       }
+      mx *= p.scale_log2;  // -inf stays -inf
+      float* mxb = s_mx + (i % 2) * 256;
+      mxb[hf * 128 + r] = mx;
+      named_barrier_sync(pair_bar, 64);
+      mx = fmaxf(mx, mxb[(1 - hf) * 128 + r]);
       const float m_new = fmaxf(m, mx);
       const float mref = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet keeps p = 0
       const float alpha = ex2(m - mref);
       float lsum = 0.f;
       uint8_t* pb = sP + b * S::NP * S::PB;
-      tc_fence_before_sync();  // S is in registers: its buffer may take S(i + 2)
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[b]);
+      uint32_t pk[KH / 2], pl[KH / 2];
 #pragma unroll
-      for (int cc = 0; cc < kNK / 32; ++cc) {
-        uint32_t pk[16], pl[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ex2(__uint_as_float(sa[cc * 32 + e]) - mref);  // ex2(-inf) = 0 for masked keys
-          const float p1 = ex2(__uint_as_float(sa[cc * 32 + e + 1]) - mref);
-          pk[e / 2] = Dt<T>::pack(p0, p1);
-          const float2 hi = Dt<T>::unpack(pk[e / 2]);  // the sum uses the weights the MMA sees
-          if (kSplit) {
-            pl[e / 2] = Dt<T>::pack(p0 - hi.x, p1 - hi.y);
-            const float2 lo = Dt<T>::unpack(pl[e / 2]);
-            lsum += (hi.x + lo.x) + (hi.y + lo.y);
-          } else {
-            lsum += hi.x + hi.y;
-          }
+      for (int e = 0; e < KH; e += 2) {
+        // ex2(-inf) = 0 for masked keys
+        const float p0 = ex2(fmaf(__uint_as_float(sa[e]), p.scale_log2, -mref));
+        const float p1 = ex2(fmaf(__uint_as_float(sa[e + 1]), p.scale_log2, -mref));
+        pk[e / 2] = Dt<T>::pack(p0, p1);
+        if (kSplit) {
+          const float2 hi = Dt<T>::unpack(pk[e / 2]);
+          pl[e / 2] = Dt<T>::pack(p0 - hi.x, p1 - hi.y);
         }
-        // keys cc*32 .. cc*32+31 of row r: 16-byte granules 4*cc .. 4*cc+3 of the row
+        lsum += p0 + p1;
+      }
+      // keys 32 hf .. 32 hf + 31 of row r: 16-byte granules 4 hf .. 4 hf + 3 of the row
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int gr = cc * 4 + u;
-          const int off = (gr / 8) * 128 * 128 + r * 128 + (((gr % 8) ^ (r & 7)) * 16);
-          *reinterpret_cast<uint4*>(pb + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-          if (kSplit)
-            *reinterpret_cast<uint4*>(pb + S::PB + off) =
-                make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
-        }
+      for (int u = 0; u < 4; ++u) {
+        const int gr = hf * 4 + u;
+        const int off = (gr / 8) * 128 * 128 + r * 128 + (((gr % 8) ^ (r & 7)) * 16);
+        *reinterpret_cast<uint4*>(pb + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        if (kSplit)
+          *reinterpret_cast<uint4*>(pb + S::PB + off) = make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
-      l = l * alpha + lsum;
+      l = l * alpha + lsum;  // this half's keys; the halves share the row's scale
       if (i > 0) fold(i - 1, alpha_prev);
       alpha_prev = alpha;
       m = m_new;
     }
     if (nst > 0) fold(nst - 1, alpha_prev);
     if (!ok) report(p.status, PKV_ERR_TIMEOUT);
+    s_l[hf * 128 + r] = l;
+    named_barrier_sync(pair_bar, 64);
+    l += s_l[(1 - hf) * 128 + r];
     if (valid && ok) {
       const float inv = 1.f / l;
-      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(tok0 + tile * TQ + t) * p.out_st + (int64_t)(head * G + gq) * p.out_sh;
+      T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(tok0 + tile * TQ + t) * p.out_st +
+                (int64_t)(head * G + gq) * p.out_sh + hf * DH;
 #pragma unroll
-      for (int e = 0; e < D; e += 2) *reinterpret_cast<uint32_t*>(orow + e) = Dt<T>::pack(acc[e] * inv, acc[e + 1] * inv);
+      for (int e = 0; e < DH; e += 2) *reinterpret_cast<uint32_t*>(orow + e) = Dt<T>::pack(acc[e] * inv, acc[e + 1] * inv);
     }
   }
   __syncthreads();
