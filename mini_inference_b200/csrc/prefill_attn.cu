@@ -43,8 +43,8 @@ template <int D, bool SPLIT> struct PrefillShape {
   static constexpr int PB = (kNK / 64) * 128 * 128;  // P tile: [NK/64][128 rows][64]
   static constexpr int NP = SPLIT ? 2 : 1;           // P tiles per buffer (hi, lo)
   static constexpr int SMEM = 1024 + QB + 2 * kKST * KSB + 2 * NP * PB + 24 * 8 + 16 + 3 * 2 * 128 * 4;
-  // TMEM: S double-buffered at columns 0 and NK, O double-buffered at 2 NK and 2 NK + D.
-  static constexpr int COLS = 2 * kNK + 2 * D;
+  // TMEM: S double-buffered at columns 0 and NK, the O accumulator at 2 NK.
+  static constexpr int COLS = 2 * kNK + D;
   static constexpr int NCOLS = COLS <= 128 ? 128 : (COLS <= 256 ? 256 : 512);
   static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
 };
@@ -86,8 +86,7 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   uint64_t* s_full = bars + 6;     // [2] S = Q K^T done
   uint64_t* s_free = bars + 8;     // [2] S read out
   uint64_t* p_full = bars + 10;    // [2] P stored
-  uint64_t* o_full = bars + 12;    // [2] O(i) = P V done
-  uint64_t* o_free = bars + 14;    // [2] O(i) read out
+  uint64_t* o_full = bars + 12;    // [2] O += P(j) V(j) done, j even / odd
   uint64_t* q_ready = bars + 16;   // the softmax warps stored Q
   uint64_t* mma_done = bars + 17;  // every MMA of the CTA has completed (before TMEM is freed)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 24);
@@ -127,7 +126,6 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
       mbar_init(&s_free[i], kSoftWarps);
       mbar_init(&p_full[i], kSoftWarps);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], kSoftWarps);
     }
     mbar_init(q_ready, kSoftWarps);
     mbar_init(mma_done, 1);
@@ -142,7 +140,7 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   const uint32_t tmem = *tslot;
   const uint64_t deadline = global_ns() + kWaitBudgetNs;
   auto s_col = [](int b) { return (uint32_t)(b * kNK); };
-  auto o_col = [](int b) { return (uint32_t)(2 * kNK + b * D); };
+  constexpr uint32_t kOCol = 2 * kNK;
 
   if (warp == kSoftWarps) {
     // ---------------------------------------------------------------- TMA copies
@@ -198,7 +196,6 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
       auto issue_o = [&](int j) -> bool {
         const int st = j % kKST, b = j % 2;
         if (!mbar_wait_until(&p_full[b], (j / 2) & 1, deadline)) return false;
-        if (j >= 2 && !mbar_wait_until(&o_free[b], ((j / 2) - 1) & 1, deadline)) return false;
         tc_fence_after_sync();
         uint8_t* pb = sP + b * S::NP * S::PB;
 #pragma unroll
@@ -207,7 +204,7 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
           for (int kb = 0; kb < kNK / 16; ++kb) {
             const uint64_t a = umma_desc_sw128(smem_u32(pb + h * S::PB + (kb / 4) * 128 * 128 + (kb % 4) * 32), 16, 1024);
             const uint64_t bd = umma_desc_sw128(smem_u32(sV + st * S::KSB + kb * kBS * 128), kNK * 128, 1024);
-            umma_f16_ss(tmem + o_col(b), a, bd, idesc_o, h > 0 || kb > 0);
+            umma_f16_ss(tmem + kOCol, a, bd, idesc_o, j > 0 || h > 0 || kb > 0);
           }
         }
         umma_commit(&o_full[b]);
@@ -258,29 +255,23 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
 
     const uint32_t tl = tmem + ((uint32_t)((warp % 4) * 32) << 16);
     const int pair_bar = 1 + warp % 4;  // named barrier of warps w and w + 4
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-    float acc[DH];
-#pragma unroll
-    for (int e = 0; e < DH; ++e) acc[e] = 0.f;
+    // O accumulates in TMEM across stages against a reference max m that moves only when a
+    // row's max grows by more than kSlack (in log2 units): weights then stay below 2^kSlack
+    // and, in the common case, O needs no rescaling at all. When it does, the warps rescale
+    // their rows of O in TMEM after the previous P V completed and before this stage's P is
+    // released to the MMA thread. PV(j) completes on o_full[j % 2]; each is confirmed at the
+    // start of stage j + 2 (or when a rescale needs it), always before PV(j + 2), the next
+    // phase of the same barrier, can be issued: every parity wait is unambiguous.
+    constexpr float kSlack = 8.f;
+    float m = -INFINITY, l = 0.f;
     bool ok = true;
-    // acc = acc * alpha + O(j) (this thread's half of the columns), from its TMEM buffer.
-    auto fold = [&](int j, float alpha) {
-      const int b = j % 2;
-      if (ok && !mbar_wait_until(&o_full[b], (j / 2) & 1, deadline)) ok = false;
-      tc_fence_after_sync();
-      uint32_t ob[DH];
-#pragma unroll
-      for (int c = 0; c < DH / 32; ++c)
-        tmem_ld32(tl + o_col(b) + hf * DH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(ob + c * 32));
-      tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < DH; ++e) acc[e] = acc[e] * alpha + __uint_as_float(ob[e]);
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[b]);
+    auto confirm = [&](int j) {  // PV(j) has completed
+      if (ok && !mbar_wait_until(&o_full[j % 2], (j / 2) & 1, deadline)) ok = false;
     };
     for (int i = 0; i < nst; ++i) {
       const int b = i % 2;
+      // Before P(i) is released, so that PV(i) (the next phase of this barrier) cannot have run.
+      if (i >= 2) confirm(i - 2);
       if (ok && !mbar_wait_until(&s_full[b], (i / 2) & 1, deadline)) ok = false;
       tc_fence_after_sync();
       const int key0 = i * kNK + hf * KH;
@@ -309,15 +300,35 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
       mxb[hf * 128 + r] = mx;
       named_barrier_sync(pair_bar, 64);
       mx = fmaxf(mx, mxb[(1 - hf) * 128 + r]);
-      const float m_new = fmaxf(m, mx);
-      const float mref = m_new == -INFINITY ? 0.f : m_new;  // a row with nothing visible yet keeps p = 0
-      const float alpha = ex2(m - mref);
+      const float m_cand = fmaxf(m, mx);
+      float alpha = 1.f;
+      if (m_cand - m > kSlack) {  // false while both are -inf (nothing visible yet)
+        alpha = ex2(m - m_cand);  // 0 when m was -inf
+        m = m_cand;
+        l *= alpha;
+      }
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        confirm(i - 1);
+        tc_fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t ob[32];
+          tmem_ld32(tl + kOCol + hf * DH + c * 32, ob);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ob[e] = __float_as_uint(__uint_as_float(ob[e]) * alpha);
+          tmem_st32(tl + kOCol + hf * DH + c * 32, ob);
+        }
+        tmem_wait_st();
+        tc_fence_before_sync();
+      }
+      const float mref = m == -INFINITY ? 0.f : m;
       float lsum = 0.f;
       uint8_t* pb = sP + b * S::NP * S::PB;
       uint32_t pk[KH / 2], pl[KH / 2];
 #pragma unroll
       for (int e = 0; e < KH; e += 2) {
-        // ex2(-inf) = 0 for masked keys
+        // ex2(-inf) = 0 for masked keys; every weight is below 2^kSlack
         const float p0 = ex2(fmaf(__uint_as_float(sa[e]), p.scale_log2, -mref));
         const float p1 = ex2(fmaf(__uint_as_float(sa[e + 1]), p.scale_log2, -mref));
         pk[e / 2] = Dt<T>::pack(p0, p1);
@@ -339,12 +350,20 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
-      l = l * alpha + lsum;  // this half's keys; the halves share the row's scale
-      if (i > 0) fold(i - 1, alpha_prev);
-      alpha_prev = alpha;
-      m = m_new;
+      l += lsum;  // this half's keys; the halves share the row's reference max
     }
-    if (nst > 0) fold(nst - 1, alpha_prev);
+    if (nst >= 2) confirm(nst - 2);
+    if (nst >= 1) confirm(nst - 1);
+    tc_fence_after_sync();
+    float acc[DH];
+#pragma unroll
+    for (int c = 0; c < DH / 32; ++c) {
+      uint32_t ob[32];
+      tmem_ld32(tl + kOCol + hf * DH + c * 32, ob);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) acc[c * 32 + e] = __uint_as_float(ob[e]);
+    }
     if (!ok) report(p.status, PKV_ERR_TIMEOUT);
     s_l[hf * 128 + r] = l;
     named_barrier_sync(pair_bar, 64);

@@ -50,7 +50,9 @@ def make_pool(k: torch.Tensor, v: torch.Tensor) -> PkvPool:
     if not (k.is_contiguous() and v.is_contiguous()):
         raise ValueError("the KV pools must be contiguous")
     layers, nbt, hkv, bs, d = k.shape
-    return PkvPool(k.data_ptr(), v.data_ptr(), layers, nbt, hkv, bs, d, pkv_dtype(k.dtype))
+    pool = PkvPool(k.data_ptr(), v.data_ptr(), layers, nbt, hkv, bs, d, pkv_dtype(k.dtype))
+    pool._keep = (k, v)  # the struct holds raw pointers: keep the tensors alive with it
+    return pool
 
 
 def make_tables(block_tables: torch.Tensor, seq_rows: torch.Tensor | None = None) -> PkvTables:
@@ -60,7 +62,9 @@ def make_tables(block_tables: torch.Tensor, seq_rows: torch.Tensor | None = None
     if seq_rows is not None and (seq_rows.dtype != torch.int32 or not seq_rows.is_contiguous()):
         raise ValueError("seq_rows must be a contiguous int32 tensor")
     rows, cols = block_tables.shape
-    return PkvTables(block_tables.data_ptr(), block_tables.stride(0), rows, cols, _ptr(seq_rows))
+    tables = PkvTables(block_tables.data_ptr(), block_tables.stride(0), rows, cols, _ptr(seq_rows))
+    tables._keep = (block_tables, seq_rows)  # the struct holds raw pointers: keep the tensors alive with it
+    return tables
 
 
 def kv_append(pool: PkvPool, layer: int, k_rows: torch.Tensor, v_rows: torch.Tensor, slot_mapping: torch.Tensor,

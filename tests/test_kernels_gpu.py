@@ -147,6 +147,74 @@ def test_prefill_kernels_match_golden(dev, golden_dir, name):
     assert np.array_equal(bits(v_pool[0]), v_after.view(np.int16))
 
 
+@pytest.mark.parametrize("dtype,d", [("float16", 64), ("bfloat16", 128)])
+def test_prefill_scores_growing_along_the_keys(dev, dtype, d):
+    """Keys whose scores grow by far more than 2^8 from one 64-key stage to the next.
+
+    The tensor-core prefill keeps a reference max per row and rescales its TMEM
+    accumulator only when a row's max grows past it; random scores almost never do
+    that, these force it at every stage, with a prefix hit and a query tile cut by
+    the end of its sequence.
+    """
+    from mini_inference_b200 import ops
+
+    rng = np.random.default_rng(11)
+    hq, hkv, bs = 14, 2, 16
+    starts, lengths = [200, 0], [77, 150]
+    ends = [a + n for a, n in zip(starts, lengths)]
+    nblk = [(e + bs - 1) // bs for e in ends]
+    nb = sum(nblk) + 4
+    perm = rng.permutation(nb)
+    tables, at = [], 0
+    for n in nblk:
+        tables.append(perm[at:at + n].tolist())
+        at += n
+    kp = rng.standard_normal((nb + 1, hkv, bs, d)).astype(np.float32)
+    vp = rng.standard_normal((nb + 1, hkv, bs, d)).astype(np.float32)
+    q = rng.standard_normal((hq, sum(lengths), d)).astype(np.float32)
+    # The score of the key at position p scales with 1 + p / 8: the row max grows along the keys.
+    for table, e in zip(tables, ends):
+        for pos in range(e):
+            kp[table[pos // bs], :, pos % bs] *= 1.0 + pos / 8.0
+    k_new = np.zeros((hkv, sum(lengths), d), np.float32)
+    v_new = rng.standard_normal((hkv, sum(lengths), d)).astype(np.float32)
+    t0 = 0
+    for table, a, n in zip(tables, starts, lengths):
+        for i in range(n):
+            pos = a + i
+            k_new[:, t0 + i] = rng.standard_normal((hkv, d)) * (1.0 + pos / 8.0)
+        t0 += n
+    tdt = TORCH[dtype]
+    kq, vq, qq = round_to(kp, dtype), round_to(vp, dtype), round_to(q, dtype)
+    knq, vnq = round_to(k_new, dtype), round_to(v_new, dtype)
+    k_pool = torch.from_numpy(kq).to(tdt).to(dev)[None].contiguous()
+    v_pool = torch.from_numpy(vq).to(tdt).to(dev)[None].contiguous()
+    width = max(nblk)
+    tab = np.full((len(tables), width), -1, np.int32)
+    for i, t in enumerate(tables):
+        tab[i, :len(t)] = t
+    tabs = ops.make_tables(torch.from_numpy(tab).to(dev))
+    pool = ops.make_pool(k_pool, v_pool)
+    cu = torch.tensor([0, lengths[0], sum(lengths)], dtype=torch.int32, device=dev)
+    st = torch.tensor(starts, dtype=torch.int32, device=dev)
+    total = sum(lengths)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    positions = torch.empty(total, dtype=torch.int64, device=dev)
+    slot_mapping = torch.empty(total, dtype=torch.int64, device=dev)
+    ops.build_prefill_metadata(tabs, cu, st, bs, total, positions, slot_mapping, status)
+    kt = torch.from_numpy(knq).to(tdt).to(dev)
+    vt = torch.from_numpy(vnq).to(tdt).to(dev)
+    ops.kv_append(pool, 0, kt.transpose(0, 1), vt.transpose(0, 1), slot_mapping, status)
+    qt = torch.from_numpy(qq).to(tdt).to(dev)
+    out = ops.prefill_attention(pool, 0, tabs, qt.transpose(0, 1), cu, st, max(lengths), status=status)
+    ops.raise_device_errors(status)
+    got = to_np(out).transpose(1, 0, 2)
+    ref = packed_prefill_attend(kq.astype(np.float64), vq.astype(np.float64), tables, starts, lengths,
+                                qq.astype(np.float64), knq.astype(np.float64), vnq.astype(np.float64))
+    assert np.isfinite(got).all()
+    assert excess(got, round_to(ref, dtype), dtype) <= 0
+
+
 # ------------------------------------------------------------------ the micro-benchmark shape, full size
 
 
