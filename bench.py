@@ -72,6 +72,68 @@ def workload(seed: int):
     return ctx, tables
 
 
+def prefill_workload(seed: int, n_seq: int = 256):
+    """Config 4's prefill: a 1024-token cached prefix plus U{64..256} new tokens per sequence."""
+    g = torch.Generator().manual_seed(seed)
+    news = torch.randint(64, 257, (n_seq,), generator=g).tolist()
+    return [1024] * n_seq, news
+
+
+def run_prefill(dev, seed: int, layers: int = 2, reps: int = 10) -> dict:
+    """Time pkv_prefill_attention (tcgen05) on config 4's prefill over the cached prefix.
+
+    Two layer pools alternate (168 MB of K/V each, above L2). FLOPs count only the causal
+    products each query makes with the keys it sees: 4 * Hq * d per (query, key) pair.
+    """
+    from mini_inference_b200 import ops
+
+    starts, news = prefill_workload(seed)
+    ends = [a + n for a, n in zip(starts, news)]
+    nblk = [(e + BS - 1) // BS for e in ends]
+    nb = sum(nblk) + 1
+    g = torch.Generator().manual_seed(seed + 7)
+    perm = torch.randperm(nb, generator=g)
+    tab = torch.zeros(len(ends), max(nblk), dtype=torch.int32)
+    at = 0
+    for i, n in enumerate(nblk):
+        tab[i, :n] = perm[at:at + n]
+        at += n
+    gd = torch.Generator(device=dev).manual_seed(seed + 11)
+    k = torch.randn(layers, nb + 1, HKV, BS, D, generator=gd, device=dev, dtype=torch.float16)
+    v = torch.randn(layers, nb + 1, HKV, BS, D, generator=gd, device=dev, dtype=torch.float16)
+    q = torch.randn(layers, sum(news), HQ, D, generator=gd, device=dev, dtype=torch.float16)
+    out = torch.empty_like(q[0])
+    cu = torch.tensor([0] + torch.tensor(news).cumsum(0).tolist(), dtype=torch.int32, device=dev)
+    st = torch.tensor(starts, dtype=torch.int32, device=dev)
+    pool, tabs = ops.make_pool(k, v), ops.make_tables(tab.to(dev))
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def call(layer: int) -> None:
+        ops.prefill_attention(pool, layer, tabs, q[layer], cu, st, max(news), out=out, status=status)
+
+    for i in range(3):
+        call(i % layers)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(reps):
+        call(i % layers)
+    e1.record()
+    torch.cuda.synchronize()
+    ops.raise_device_errors(status)
+    ms = e0.elapsed_time(e1) / reps
+    pairs = sum(n * a + n * (n + 1) // 2 for a, n in zip(starts, news))
+    flops = 4 * HQ * D * pairs
+    peaks, kind = measured_peaks()
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {"workload": "config 4 prefill: 256 sequences x (1024 cached + U{64..256} new) tokens, fp16, "
+                        "Hq 14 / Hkv 2 / d 64, one layer call (tcgen05 kernel)",
+            "ms_per_call": round(ms, 4), "flops_per_call": flops, "tflops": round(tflops, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(tflops / peaks["bf16_tflops"], 4),
+                         "peak_kind": f"{kind} dense bf16 GEMM (burst)"}}
+
+
 def bytes_per_layer_call(ctx: list[int]) -> int:
     """Algorithmic bytes of one fused append + decode attention call over the batch.
 
@@ -303,6 +365,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "gpu_launches": args.steps * (1 + LAYERS * DECODE_KERNELS) + args.steps * LAYERS * DECODE_KERNELS + e2e_launches,
         "clocks": clocks.summary(),
     }
+    if not args.profile_case:
+        line["prefill"] = run_prefill(dev, seed=rank)
     if world == 1 and not args.profile_case:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -429,6 +493,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only the tcgen05 prefill leg (config 4's prefill), for ncu captures")
     ap.add_argument("--profile-case", action="store_true",
                     help="small case for ncu captures: 4 layer pools (536 MB, still above L2), no e2e / CPU legs")
     args = ap.parse_args()
@@ -436,6 +502,11 @@ def main() -> None:
     args.layers = 4 if args.profile_case else LAYERS
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.prefill_only:
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(dev)
+        print(json.dumps(run_prefill(dev, seed=0, reps=args.steps)), flush=True)
         return
     rank, world, local = dist_setup(args.gpus)
     try:
