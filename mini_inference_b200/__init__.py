@@ -11,6 +11,8 @@ metadata builder and block copy-on-write. Importing the package loads
 
 from ._lib import PkvError
 from .cache import NativeBlockManager, PackedPrefillContext, PagedDecodeContext, PagedKVCache
+from .cuda_graphs import GraphedDecoder
 
-__all__ = ["PagedKVCache", "PagedDecodeContext", "PackedPrefillContext", "NativeBlockManager", "PkvError"]
+__all__ = ["PagedKVCache", "PagedDecodeContext", "PackedPrefillContext", "NativeBlockManager", "GraphedDecoder",
+           "PkvError"]
 __version__ = "0.1.0"

@@ -463,7 +463,9 @@ def test_decode_graph_replays_stay_exact(dev):
     assert torch.equal(outs, first)
 
 
-@pytest.mark.parametrize("dtype,hq,hkv,d,ctx", [(torch.float16, 14, 2, 64, [4000]), (torch.bfloat16, 28, 4, 128, [3000, 37])])
+@pytest.mark.parametrize("dtype,hq,hkv,d,ctx", [(torch.float16, 14, 2, 64, [4000]), (torch.bfloat16, 28, 4, 128, [3000, 37]),
+                                              # the 7B long-context shape (config 5): tens of chunks per sequence
+                                              (torch.bfloat16, 28, 4, 128, [16000, 5000, 24000])])
 def test_decode_few_long_sequences_split_over_many_ctas(dev, dtype, hq, hkv, d, ctx):
     """A batch of one or two long sequences is spread over every CTA, so each is merged from
     more pieces than the merging CTA can stage at once (the multi-round merge path)."""
