@@ -13,14 +13,16 @@
 // accumulators in tensor memory. One CTA takes one KV head of one sequence and TQ of
 // its new tokens; the M = 128 rows of the MMA tile are those tokens x the GQA group's
 // query heads (16 x 7 = 112 rows for Qwen2's group of 7), so every K/V block read
-// serves the whole group. Keys stream in stages of NK = 64 (four blocks) through a
-// two-stage TMA ring: S = Q K^T (M 128 x N 64, fp32 in TMEM), an online softmax by
-// four warps that each own 32 TMEM lanes (one row per thread, no shuffles), P written
-// to shared memory as fp16/bf16, then O_stage = P V (M 128 x N head_dim, in TMEM),
-// which the softmax warps fold into their fp32 row accumulators with the running
-// rescale. One warp issues the TMA copies, one thread the MMAs; mbarriers (MMA
-// completion through tcgen05.commit) order the three roles. Only the causal part of
-// each sequence is visited; keys past a tile's last position are masked to -inf.
+// serves the whole group. Keys stream in stages of NK = 64 (four blocks) through TMA
+// rings with separate K and V stages: S = Q K^T (M 128 x N 64, fp32 in TMEM) frees its K
+// stage as soon as it completes, P V frees the V stage, so a K copy has two to three
+// stages of softmax time to land instead of one. Eight softmax warps (half a row per
+// thread) turn S into P, written to shared memory as fp16/bf16, and O += P V
+// accumulates in TMEM against a lazily moved reference max. One warp issues the TMA
+// copies (block ids looked up 32 at a time, ahead of use), one thread the MMAs;
+// mbarriers (MMA completion through tcgen05.commit) order the three roles. Only the
+// causal part of each sequence is visited; keys past a tile's last position are masked
+// to -inf.
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -28,25 +30,34 @@ namespace pkv {
 namespace {
 
 constexpr int kBS = 16;
-constexpr int kNK = 64;               // keys per stage
-constexpr int kKST = 3;               // K/V ring stages
-constexpr int kSoftWarps = 8;          // softmax warps: two per TMEM lane quarter (half a row each)
-constexpr int kPrefillThreads = (kSoftWarps + 2) * 32;  // + 1 copy warp, 1 MMA warp
+constexpr int kNK = 64;                      // keys per stage
+constexpr int kKS = 4;                       // K ring stages (freed when S = Q K^T completes)
+constexpr int kVS = 4;                       // V ring stages (freed when O += P V completes)
+constexpr int kBars = 2 * (kKS + kVS) + 8;   // + s_full, p_full, o_full (2 each), q_ready, mma_done
 constexpr float kLog2e = 1.4426950408889634f;
 
 // SPLIT: P goes to the tensor cores as hi + lo halves (bf16 keeps 8 bits of a weight;
 // the two halves together ~16, as the fp16 path has in one).
 template <int D, bool SPLIT> struct PrefillShape {
   static constexpr int DC = D / 64;                  // 64-wide head_dim chunks
-  static constexpr int QB = DC * 128 * 128;          // Q tile: [DC][128 rows][64]
-  static constexpr int KSB = DC * kNK * 128;         // one stage of K (or V): [DC][NK keys][64]
-  static constexpr int PB = (kNK / 64) * 128 * 128;  // P tile: [NK/64][128 rows][64]
-  static constexpr int NP = SPLIT ? 2 : 1;           // P tiles per buffer (hi, lo)
-  static constexpr int SMEM = 1024 + QB + 2 * kKST * KSB + 2 * NP * PB + 24 * 8 + 16 + 3 * 2 * 128 * 4;
-  // TMEM: S double-buffered at columns 0 and NK, the O accumulator at 2 NK.
-  static constexpr int COLS = 2 * kNK + D;
+  static constexpr int KSB = DC * kNK * 128;         // one stage of K (or V): [DC][NK keys][64], 128B-swizzled
+  static constexpr int QB = DC * 128 * 128;          // Q tile in shared memory: [DC][128 rows][64]
+  // TMEM columns: two S buffers at 0 and NK, O at 2 NK, then Q (packed 16-bit pairs, when
+  // it fits), then P (32 columns of packed pairs; bf16 adds its lo half in 32 more). At
+  // head_dim 64 with bf16, Q stays in shared memory so that a CTA needs 256 columns.
+  static constexpr bool QT = !(SPLIT && D == 64);
+  static constexpr int OCOL = 2 * kNK;
+  static constexpr int QCOL = OCOL + D;
+  static constexpr int PCOL = QCOL + (QT ? D / 2 : 0);
+  static constexpr int COLS = PCOL + (SPLIT ? 2 : 1) * (kNK / 2);
   static constexpr int NCOLS = COLS <= 128 ? 128 : (COLS <= 256 ? 256 : 512);
-  static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
+  static constexpr int MIN_BLOCKS = NCOLS <= 256 ? 2 : 1;
+  // Softmax warps: one per TMEM lane quarter (a whole row per thread) when two CTAs share an
+  // SM, else two per quarter (half a row each) so that an SM still runs eight.
+  static constexpr int SW = MIN_BLOCKS == 2 ? 4 : 8;
+  static constexpr int HALVES = SW / 4;
+  static constexpr int THREADS = (SW + 2) * 32;  // + 1 copy warp, 1 MMA warp
+  static constexpr int SMEM = 1024 + (QT ? 0 : QB) + (kKS + kVS) * KSB + (kBars + 2) * 8 + 3 * 2 * 128 * 4;
 };
 
 struct PrefillParams {
@@ -59,39 +70,45 @@ struct PrefillParams {
   int32_t* status;
   int64_t out_st, out_sh, q_st, q_sh, table_stride;
   int32_t table_rows, table_cols;
-  int32_t group, layer, nbt, q_vec16;
+  int32_t group, layer, nbt, q_vec16, out_vec16;
   float scale_log2;
 };
 
-// Pipeline (stage i = keys 64 i .. 64 i + 63): the MMA thread issues S(0), then for each
-// i: S(i+1) into the other S buffer, then O(i) = P(i) V(i) into O buffer i % 2 once the
-// softmax warps stored P(i). The softmax warps turn S(i) into P(i) while the tensor cores
-// compute S(i+1) and O(i-1), and fold O(i-1) into their accumulators one stage late.
+// Pipeline (stage i = keys 64 i .. 64 i + 63). The MMA thread issues S(0) and S(1), then
+// for each i, as one burst once the softmax warps stored P(i): O += P(i) V(i), then
+// S(i+2) = Q K(i+2)^T into the S buffer that P(i) was made from. The softmax warps turn
+// S(i) into P(i) while the tensor cores compute O(i-1) and S(i+1). P (and Q where it
+// fits) is the A operand straight from TMEM, so most MMAs read only K or V from shared
+// memory. An MMA burst costs several hundred cycles to issue however small it is
+// (measured), which is why each stage has one burst rather than two.
 template <typename T, int D, int TQ>
-__global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_BLOCKS)
+__global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, PrefillShape<D, !Dt<T>::kExactP>::MIN_BLOCKS)
     prefill_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                    const PrefillParams p) {
   constexpr bool kSplit = !Dt<T>::kExactP;
   using S = PrefillShape<D, kSplit>;
   constexpr int DC = S::DC;
+  constexpr bool kQT = S::QT;
+  constexpr int SW = S::SW, HALVES = S::HALVES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + S::QB;                 // [kKST][KSB]
-  uint8_t* sV = sK + kKST * S::KSB;         // [kKST][KSB]
-  uint8_t* sP = sV + kKST * S::KSB;         // [2][NP][PB]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * S::NP * S::PB);
-  uint64_t* kv_full = bars;        // [kKST] TMA bytes landed
-  uint64_t* kv_empty = bars + 3;   // [kKST] the stage's MMAs are done with it
-  uint64_t* s_full = bars + 6;     // [2] S = Q K^T done
-  uint64_t* s_free = bars + 8;     // [2] S read out
-  uint64_t* p_full = bars + 10;    // [2] P stored
-  uint64_t* o_full = bars + 12;    // [2] O += P(j) V(j) done, j even / odd
-  uint64_t* q_ready = bars + 16;   // the softmax warps stored Q
-  uint64_t* mma_done = bars + 17;  // every MMA of the CTA has completed (before TMEM is freed)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 24);
-  float* s_mx = reinterpret_cast<float*>(bars + 26);  // [2 stage parities][2 halves][128 rows] partial row maxima
-  float* s_l = s_mx + 2 * 2 * 128;                    // [2 halves][128 rows] final partial row sums
+  uint8_t* sQ = smem;                        // [QB] when Q is not in TMEM
+  uint8_t* sK = sQ + (kQT ? 0 : S::QB);      // [kKS][KSB]
+  uint8_t* sV = sK + kKS * S::KSB;           // [kVS][KSB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVS * S::KSB);
+  uint64_t* k_full = bars;                   // [kKS] TMA bytes of K landed
+  uint64_t* v_full = k_full + kKS;           // [kVS] TMA bytes of V landed
+  uint64_t* k_empty = v_full + kVS;          // [kKS] S = Q K^T of the stage is done
+  uint64_t* v_empty = k_empty + kKS;         // [kVS] O += P V of the stage is done
+  uint64_t* s_full = v_empty + kVS;          // [2] S = Q K^T done
+  uint64_t* p_full = s_full + 2;             // [2] P(j) stored in TMEM, j even / odd
+  uint64_t* o_full = p_full + 2;             // [2] O += P(j) V(j) done, j even / odd
+  uint64_t* q_ready = o_full + 2;            // the softmax warps stored Q
+  uint64_t* mma_done = q_ready + 1;          // every MMA of the CTA has completed (before TMEM is freed)
+  static_assert(kBars == 2 * (kKS + kVS) + 8, "barrier layout");
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + kBars);
+  float* s_mx = reinterpret_cast<float*>(bars + kBars + 2);  // [2 stage parities][2 halves][128 rows] partial row maxima
+  float* s_l = s_mx + 2 * 2 * 128;                           // [2 halves][128 rows] final partial row sums
 
   const int tile = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -117,17 +134,20 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   const int G = p.group;
 
   if (tid == 0) {
-    for (int i = 0; i < kKST; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < kKS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kVS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], kSoftWarps);
-      mbar_init(&p_full[i], kSoftWarps);
+      mbar_init(&p_full[i], SW);
       mbar_init(&o_full[i], 1);
     }
-    mbar_init(q_ready, kSoftWarps);
+    mbar_init(q_ready, SW);
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
@@ -140,128 +160,164 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
   const uint32_t tmem = *tslot;
   const uint64_t deadline = global_ns() + kWaitBudgetNs;
   auto s_col = [](int b) { return (uint32_t)(b * kNK); };
-  constexpr uint32_t kOCol = 2 * kNK;
 
-  if (warp == kSoftWarps) {
+  if (warp == SW) {
     // ---------------------------------------------------------------- TMA copies
-    // One copy per lane (a lane issues one (block, tensor, head_dim chunk) of the stage):
-    // a single issuing lane cannot keep up with 2 KB copies.
-    constexpr int kCopies = (kNK / kBS) * 2 * DC;
+    // One copy per lane (lane l < kCopies copies head_dim chunk l % DC of block l / DC of the
+    // stage; a single issuing lane cannot keep up with 2 KB copies), K of a stage as soon as
+    // its K stage is free, then V. Block ids come from a window of 32 looked up at once,
+    // the next window in flight meanwhile.
+    constexpr int kCopies = (kNK / kBS) * DC;
+    constexpr int kStagesPerWindow = 32 / (kNK / kBS);
+    auto lookup = [&](int kb) -> int {
+      // Blocks past the visible keys are masked; the scratch block keeps their rows finite.
+      int blk = (kb < nkb && table) ? table[kb] : p.nbt - 1;
+      if (blk < 0 || blk >= p.nbt) {
+        report(p.status, PKV_ERR_OUT_OF_RANGE);
+        blk = p.nbt - 1;
+      }
+      return blk;
+    };
+    int win = lookup(lane), win_next = lookup(32 + lane);
+    const int b = lane / DC, c = lane % DC;
     bool ok = true;
     for (int i = 0; i < nst && ok; ++i) {
-      const int st = i % kKST;
+      if (i > 0 && i % kStagesPerWindow == 0) {
+        win = win_next;
+        win_next = lookup(32 * (i / kStagesPerWindow + 1) + lane);
+      }
+      const int blk = __shfl_sync(0xffffffffu, win, (i * (kNK / kBS) + b) % 32);
+      const int c4 = p.layer * p.nbt + blk;
+      const int sk = i % kKS, sv = i % kVS;
       if (lane == 0) {
-        if (i >= kKST && !mbar_wait_until(&kv_empty[st], ((i / kKST) - 1) & 1, deadline)) {
+        if (i >= kKS && !mbar_wait_until(&k_empty[sk], ((i / kKS) - 1) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
           ok = false;
         }
-        if (ok) mbar_arrive_expect_tx(&kv_full[st], 2 * S::KSB);
+        if (ok) mbar_arrive_expect_tx(&k_full[sk], S::KSB);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (ok && lane < kCopies) {
-        const int b = lane / (2 * DC), tensor = (lane / DC) % 2, c = lane % DC;
-        const int kb = i * (kNK / kBS) + b;
-        // Blocks past the visible keys are masked; the scratch block keeps their rows finite.
-        int blk = (kb < nkb && table) ? table[kb] : p.nbt - 1;
-        if (blk < 0 || blk >= p.nbt) {
-          report(p.status, PKV_ERR_OUT_OF_RANGE);
-          blk = p.nbt - 1;
+      if (ok && lane < kCopies)
+        tma_load_5d(sK + sk * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_k, 0, 0, c, head, c4, &k_full[sk]);
+      if (lane == 0 && ok) {
+        if (i >= kVS && !mbar_wait_until(&v_empty[sv], ((i / kVS) - 1) & 1, deadline)) {
+          report(p.status, PKV_ERR_TIMEOUT);
+          ok = false;
         }
-        const int c4 = p.layer * p.nbt + blk;
-        uint8_t* dst = (tensor ? sV : sK) + st * S::KSB + c * kNK * 128 + b * kBS * 128;
-        tma_load_5d(dst, tensor ? &tmap_v : &tmap_k, 0, 0, c, head, c4, &kv_full[st]);
+        if (ok) mbar_arrive_expect_tx(&v_full[sv], S::KSB);
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok && lane < kCopies)
+        tma_load_5d(sV + sv * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_v, 0, 0, c, head, c4, &v_full[sv]);
     }
-  } else if (warp == kSoftWarps + 1) {
+  } else if (warp == SW + 1) {
     // ---------------------------------------------------------------- MMA issue
     if (lane == 0) {
       constexpr bool kBf16 = Dt<T>::code == PKV_BF16;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBf16, false, 128, kNK);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBf16, true, 128, D);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % kKST, b = j % 2;
-        if (!mbar_wait_until(&kv_full[st], (j / kKST) & 1, deadline)) return false;
-        if (j >= 2 && !mbar_wait_until(&s_free[b], ((j / 2) - 1) & 1, deadline)) return false;
+      constexpr int NP = kSplit ? 2 : 1;  // P as hi + lo halves for bf16
+      auto issue_s = [&](int j) -> bool {  // S(j) into buffer j % 2, whose S(j - 2) P(j - 2) was made from
+        const int st = j % kKS, b = j % 2;
+        if (!mbar_wait_until(&k_full[st], (j / kKS) & 1, deadline)) return false;
         tc_fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int c = kk / 4, k16 = kk % 4;
-          const uint64_t a = umma_desc_sw128(smem_u32(sQ + c * 128 * 128 + k16 * 32), 16, 1024);
           const uint64_t bd = umma_desc_sw128(smem_u32(sK + st * S::KSB + c * kNK * 128 + k16 * 32), 16, 1024);
-          umma_f16_ss(tmem + s_col(b), a, bd, idesc_s, kk > 0);
+          if (kQT) {
+            umma_f16_ts(tmem + s_col(b), tmem + S::QCOL + kk * 8, bd, idesc_s, kk > 0);
+          } else {
+            const uint64_t a = umma_desc_sw128(smem_u32(sQ + c * 128 * 128 + k16 * 32), 16, 1024);
+            umma_f16_ss(tmem + s_col(b), a, bd, idesc_s, kk > 0);
+          }
         }
         umma_commit(&s_full[b]);
+        umma_commit(&k_empty[st]);
         return true;
       };
       auto issue_o = [&](int j) -> bool {
-        const int st = j % kKST, b = j % 2;
+        const int st = j % kVS, b = j % 2;
         if (!mbar_wait_until(&p_full[b], (j / 2) & 1, deadline)) return false;
+        if (!mbar_wait_until(&v_full[st], (j / kVS) & 1, deadline)) return false;
         tc_fence_after_sync();
-        uint8_t* pb = sP + b * S::NP * S::PB;
 #pragma unroll
-        for (int h = 0; h < S::NP; ++h) {
+        for (int h = 0; h < NP; ++h) {
 #pragma unroll
           for (int kb = 0; kb < kNK / 16; ++kb) {
-            const uint64_t a = umma_desc_sw128(smem_u32(pb + h * S::PB + (kb / 4) * 128 * 128 + (kb % 4) * 32), 16, 1024);
             const uint64_t bd = umma_desc_sw128(smem_u32(sV + st * S::KSB + kb * kBS * 128), kNK * 128, 1024);
-            umma_f16_ss(tmem + kOCol, a, bd, idesc_o, j > 0 || h > 0 || kb > 0);
+            umma_f16_ts(tmem + S::OCOL, tmem + S::PCOL + h * (kNK / 2) + kb * 8, bd, idesc_o, j > 0 || h > 0 || kb > 0);
           }
         }
         umma_commit(&o_full[b]);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
         return true;
       };
-      bool ok = mbar_wait_until(q_ready, 0, deadline) && (nst == 0 || issue_s(0));
+      // p_full(i) also means the softmax warps have read S(i), so S(i + 2) may overwrite it.
+      bool ok = mbar_wait_until(q_ready, 0, deadline) && issue_s(0) && (nst < 2 || issue_s(1));
       for (int i = 0; i < nst && ok; ++i) {
-        ok = (i + 1 >= nst || issue_s(i + 1)) && issue_o(i);
+        ok = issue_o(i) && (i + 2 >= nst || issue_s(i + 2));
       }
       if (!ok) report(p.status, PKV_ERR_TIMEOUT);
       umma_commit(mma_done);
     }
   } else {
-    // ---------------------------------------------------------------- softmax warps: half a row per thread
-    // Warps w and w + 4 read TMEM lanes 32 (w % 4) .. + 31: the same rows. Half hf of a row
-    // owns keys 32 hf .. 32 hf + 31 of every stage and output columns hf D/2 .. + D/2; the
-    // two halves trade their partial maxima through shared memory once per stage.
-    constexpr int KH = kNK / 2, DH = D / 2;
+    // ---------------------------------------------------------------- softmax warps
+    // Warp w reads TMEM lanes 32 (w % 4) .. + 31: tile rows. With two warps per lane quarter
+    // (HALVES = 2), half hf = w / 4 of a row owns keys KH hf .. KH hf + KH - 1 of every stage
+    // and output columns DH hf .. + DH - 1, and the two halves trade their partial maxima
+    // through shared memory once per stage; with one, a thread owns its whole row.
+    constexpr int KH = kNK / HALVES, DH = D / HALVES;
     const int hf = warp / 4;
     const int r = (warp % 4) * 32 + lane;  // TMEM lane = tile row
     const int t = r / G, gq = r - t * G;
     const bool valid = r < TQ * G && t < rows_here;
     const int qpos = q_first + t;
-    // Q row r (this thread's half of the granules) into the swizzled tile, zeros without a query.
+    const uint32_t tl = tmem + ((uint32_t)((warp % 4) * 32) << 16);
+    // Q row r, this thread's half of head_dim, as the S MMAs' A operand: into TMEM (packed
+    // 16-bit pairs) or into the swizzled shared-memory tile; zeros for rows without a query.
     {
       const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)(tok0 + tile * TQ + t) * p.q_st +
-                      (int64_t)(head * G + gq) * p.q_sh;
+                      (int64_t)(head * G + gq) * p.q_sh + hf * DH;
 #pragma unroll
-      for (int k = 0; k < D / 16; ++k) {
-        const int c16 = hf * (D / 16) + k;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) {
-          if (p.q_vec16) {
-            v = *reinterpret_cast<const uint4*>(qrow + 8 * c16);
+      for (int c = 0; c < DH / 32; ++c) {  // 32 elements = 16 columns = 4 granules of 16 bytes
+        uint32_t qv[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (valid) {
+            if (p.q_vec16) {
+              v = *reinterpret_cast<const uint4*>(qrow + c * 32 + 8 * k);
+            } else {
+              const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qrow + c * 32 + 8 * k);
+              v = make_uint4(q32[0], q32[1], q32[2], q32[3]);
+            }
+          }
+          if (kQT) {
+            qv[4 * k] = v.x, qv[4 * k + 1] = v.y, qv[4 * k + 2] = v.z, qv[4 * k + 3] = v.w;
           } else {
-            const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qrow + 8 * c16);
-            v = make_uint4(q32[0], q32[1], q32[2], q32[3]);
+            const int c16 = (hf * DH + c * 32) / 8 + k;  // granule of the row
+            const int cc = c16 / 8, gr = c16 % 8;
+            *reinterpret_cast<uint4*>(sQ + cc * 128 * 128 + r * 128 + ((gr ^ (r & 7)) * 16)) = v;
           }
         }
-        const int c = c16 / 8, gr = c16 % 8;
-        *reinterpret_cast<uint4*>(sQ + c * 128 * 128 + r * 128 + ((gr ^ (r & 7)) * 16)) = v;
+        if (kQT) tmem_st16(tl + S::QCOL + hf * (DH / 2) + c * 16, qv);
       }
     }
-    fence_proxy_async_smem();
+    if (!kQT) fence_proxy_async_smem();
+    tmem_wait_st();
+    tc_fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive(q_ready);
 
-    const uint32_t tl = tmem + ((uint32_t)((warp % 4) * 32) << 16);
     const int pair_bar = 1 + warp % 4;  // named barrier of warps w and w + 4
     // O accumulates in TMEM across stages against a reference max m that moves only when a
     // row's max grows by more than kSlack (in log2 units): weights then stay below 2^kSlack
     // and, in the common case, O needs no rescaling at all. When it does, the warps rescale
     // their rows of O in TMEM after the previous P V completed and before this stage's P is
-    // released to the MMA thread. PV(j) completes on o_full[j % 2]; each is confirmed at the
-    // start of stage j + 2 (or when a rescale needs it), always before PV(j + 2), the next
-    // phase of the same barrier, can be issued: every parity wait is unambiguous.
+    // released to the MMA thread. PV(j) completes on o_full[j % 2] and is waited for before
+    // P(j + 1) is written (P has one buffer), so PV(j + 2), the next phase of that barrier,
+    // cannot have been issued: every parity wait is unambiguous.
     constexpr float kSlack = 8.f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -270,36 +326,37 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
     };
     for (int i = 0; i < nst; ++i) {
       const int b = i % 2;
-      // Before P(i) is released, so that PV(i) (the next phase of this barrier) cannot have run.
-      if (i >= 2) confirm(i - 2);
       if (ok && !mbar_wait_until(&s_full[b], (i / 2) & 1, deadline)) ok = false;
       tc_fence_after_sync();
       const int key0 = i * kNK + hf * KH;
       uint32_t sa[KH];
-      tmem_ld32(tl + s_col(b) + hf * KH, sa);
+#pragma unroll
+      for (int c = 0; c < KH / 32; ++c) tmem_ld32(tl + s_col(b) + hf * KH + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sa + c * 32));
       tmem_wait_ld();
-      tc_fence_before_sync();  // S is in registers: its buffer may take S(i + 2)
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[b]);
       // Raw scores; the max is taken before scaling (the scale is positive). A stage whose
       // every key is visible to every row of the tile needs no mask.
-      float mx = -INFINITY;
-      if ((i + 1) * kNK - 1 <= q_first && (i + 1) * kNK <= kend) {
-#pragma unroll
-        for (int e = 0; e < KH; ++e) mx = fmaxf(mx, __uint_as_float(sa[e]));
-      } else {
+      if (!((i + 1) * kNK - 1 <= q_first && (i + 1) * kNK <= kend)) {
 #pragma unroll
         for (int e = 0; e < KH; ++e) {
           const int key = key0 + e;
           if (!(valid && key <= qpos && key < kend)) sa[e] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, __uint_as_float(sa[e]));
         }
       }
-      mx *= p.scale_log2;  // -inf stays -inf
-      float* mxb = s_mx + (i % 2) * 256;
-      mxb[hf * 128 + r] = mx;
-      named_barrier_sync(pair_bar, 64);
-      mx = fmaxf(mx, mxb[(1 - hf) * 128 + r]);
+      float mt[KH / 2];
+#pragma unroll
+      for (int e = 0; e < KH / 2; ++e) mt[e] = fmaxf(__uint_as_float(sa[e]), __uint_as_float(sa[e + KH / 2]));
+#pragma unroll
+      for (int w = KH / 4; w > 0; w >>= 1) {
+#pragma unroll
+        for (int e = 0; e < w; ++e) mt[e] = fmaxf(mt[e], mt[e + w]);
+      }
+      float mx = mt[0] * p.scale_log2;  // -inf stays -inf
+      if (HALVES == 2) {
+        float* mxb = s_mx + (i % 2) * 256;
+        mxb[hf * 128 + r] = mx;
+        named_barrier_sync(pair_bar, 64);
+        mx = fmaxf(mx, mxb[(1 - hf) * 128 + r]);
+      }
       const float m_cand = fmaxf(m, mx);
       float alpha = 1.f;
       if (m_cand - m > kSlack) {  // false while both are -inf (nothing visible yet)
@@ -313,18 +370,15 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
 #pragma unroll
         for (int c = 0; c < DH / 32; ++c) {
           uint32_t ob[32];
-          tmem_ld32(tl + kOCol + hf * DH + c * 32, ob);
+          tmem_ld32(tl + S::OCOL + hf * DH + c * 32, ob);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) ob[e] = __float_as_uint(__uint_as_float(ob[e]) * alpha);
-          tmem_st32(tl + kOCol + hf * DH + c * 32, ob);
+          tmem_st32(tl + S::OCOL + hf * DH + c * 32, ob);
         }
-        tmem_wait_st();
-        tc_fence_before_sync();
       }
       const float mref = m == -INFINITY ? 0.f : m;
       float lsum = 0.f;
-      uint8_t* pb = sP + b * S::NP * S::PB;
       uint32_t pk[KH / 2], pl[KH / 2];
 #pragma unroll
       for (int e = 0; e < KH; e += 2) {
@@ -338,42 +392,53 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
         }
         lsum += p0 + p1;
       }
-      // keys 32 hf .. 32 hf + 31 of row r: 16-byte granules 4 hf .. 4 hf + 3 of the row
+      // P(i) replaces P(i - 1), which O(i - 1) must have consumed: keys KH hf .. + KH - 1
+      // are packed columns KH / 2 hf .. + KH / 2 - 1 (lo half NK / 2 further).
+      if (i > 0) confirm(i - 1);
+      tc_fence_after_sync();
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int gr = hf * 4 + u;
-        const int off = (gr / 8) * 128 * 128 + r * 128 + (((gr % 8) ^ (r & 7)) * 16);
-        *reinterpret_cast<uint4*>(pb + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      for (int c = 0; c < KH / 32; ++c) {
+        tmem_st16(tl + S::PCOL + hf * (KH / 2) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + c * 16));
         if (kSplit)
-          *reinterpret_cast<uint4*>(pb + S::PB + off) = make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
+          tmem_st16(tl + S::PCOL + kNK / 2 + hf * (KH / 2) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(pl + c * 16));
       }
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
       l += lsum;  // this half's keys; the halves share the row's reference max
     }
-    if (nst >= 2) confirm(nst - 2);
-    if (nst >= 1) confirm(nst - 1);
+    confirm(nst - 1);  // nst >= 1; PV(nst - 2) was confirmed before P(nst - 1) was written
     tc_fence_after_sync();
     float acc[DH];
 #pragma unroll
     for (int c = 0; c < DH / 32; ++c) {
       uint32_t ob[32];
-      tmem_ld32(tl + kOCol + hf * DH + c * 32, ob);
+      tmem_ld32(tl + S::OCOL + hf * DH + c * 32, ob);
       tmem_wait_ld();
 #pragma unroll
       for (int e = 0; e < 32; ++e) acc[c * 32 + e] = __uint_as_float(ob[e]);
     }
     if (!ok) report(p.status, PKV_ERR_TIMEOUT);
-    s_l[hf * 128 + r] = l;
-    named_barrier_sync(pair_bar, 64);
-    l += s_l[(1 - hf) * 128 + r];
+    if (HALVES == 2) {
+      s_l[hf * 128 + r] = l;
+      named_barrier_sync(pair_bar, 64);
+      l += s_l[(1 - hf) * 128 + r];
+    }
     if (valid && ok) {
       const float inv = 1.f / l;
       T* orow = reinterpret_cast<T*>(p.out) + (int64_t)(tok0 + tile * TQ + t) * p.out_st +
                 (int64_t)(head * G + gq) * p.out_sh + hf * DH;
+      if (p.out_vec16) {
 #pragma unroll
-      for (int e = 0; e < DH; e += 2) *reinterpret_cast<uint32_t*>(orow + e) = Dt<T>::pack(acc[e] * inv, acc[e + 1] * inv);
+        for (int e = 0; e < DH; e += 8)
+          *reinterpret_cast<uint4*>(orow + e) =
+              make_uint4(Dt<T>::pack(acc[e] * inv, acc[e + 1] * inv), Dt<T>::pack(acc[e + 2] * inv, acc[e + 3] * inv),
+                         Dt<T>::pack(acc[e + 4] * inv, acc[e + 5] * inv), Dt<T>::pack(acc[e + 6] * inv, acc[e + 7] * inv));
+      } else {
+#pragma unroll
+        for (int e = 0; e < DH; e += 2) *reinterpret_cast<uint32_t*>(orow + e) = Dt<T>::pack(acc[e] * inv, acc[e + 1] * inv);
+      }
     }
   }
   __syncthreads();
@@ -383,6 +448,7 @@ __global__ void __launch_bounds__(kPrefillThreads, PrefillShape<D, false>::MIN_B
     tmem_dealloc(tmem, S::NCOLS);
   }
 }
+
 
 template <typename T, int D, int TQ>
 int launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& p, int max_new, int hkv,
@@ -396,7 +462,7 @@ int launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillPa
     configured = true;
   }
   dim3 grid((max_new + TQ - 1) / TQ, hkv, seqs);
-  prefill_kernel<T, D, TQ><<<grid, kPrefillThreads, S::SMEM, st>>>(tk, tv, p);
+  prefill_kernel<T, D, TQ><<<grid, S::THREADS, S::SMEM, st>>>(tk, tv, p);
   return launch_status();
 }
 
@@ -456,6 +522,7 @@ extern "C" int pkv_prefill_attention(const pkv_pool* pool, int32_t layer, const 
   p.nbt = pool->num_blocks_total;
   p.scale_log2 = scale * kLog2e;
   p.q_vec16 = (reinterpret_cast<uintptr_t>(q) & 15) == 0 && ((q_stride_t | q_stride_h) & 7) == 0;
+  p.out_vec16 = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && ((out_stride_t | out_stride_h) & 7) == 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (pool->dtype == PKV_F16)
     return d == 64 ? launch_group<__half, 64>(tk, tv, p, max_new_tokens, hkv, num_seqs, st)

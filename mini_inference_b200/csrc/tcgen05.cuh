@@ -2,7 +2,7 @@
 // written from the PTX ISA's description of these instructions.
 //
 // Conventions used by the kernels here:
-//  * Operands A and B live in shared memory in the 128-byte-swizzled layout that TMA
+//  * Operand B, and A when it is not in TMEM, live in shared memory in the 128-byte-swizzled layout that TMA
 //    writes with CU_TENSOR_MAP_SWIZZLE_128B: 128-byte rows, 8-row atoms of 1024 bytes,
 //    16-byte granule g of row r stored at granule g ^ (r % 8). A tile's base is
 //    1024-byte aligned.
@@ -51,6 +51,18 @@ __device__ inline void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A is K-major in TMEM (lane = row, two 16-bit K
+// elements per 32-bit column, the lower K index in the low half), so one K step of 16
+// spans 8 columns from a_tmem.
+__device__ inline void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                   bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
 // The mbarrier gets one arrival when every tcgen05 operation this thread issued before
 // has completed.
 __device__ inline void umma_commit(uint64_t* bar) {
@@ -94,6 +106,15 @@ __device__ inline void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
       "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// Store 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ inline void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 __device__ inline void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
