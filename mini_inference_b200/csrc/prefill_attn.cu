@@ -378,19 +378,20 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
         }
       }
       const float mref = m == -INFINITY ? 0.f : m;
-      float lsum = 0.f;
+      float2 lsum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // independent paired chains
+      const float2 scale2 = make_float2(p.scale_log2, p.scale_log2), negm2 = make_float2(-mref, -mref);
       uint32_t pk[KH / 2], pl[KH / 2];
 #pragma unroll
       for (int e = 0; e < KH; e += 2) {
         // ex2(-inf) = 0 for masked keys; every weight is below 2^kSlack
-        const float p0 = ex2(fmaf(__uint_as_float(sa[e]), p.scale_log2, -mref));
-        const float p1 = ex2(fmaf(__uint_as_float(sa[e + 1]), p.scale_log2, -mref));
+        const float2 x = ffma2(make_float2(__uint_as_float(sa[e]), __uint_as_float(sa[e + 1])), scale2, negm2);
+        const float p0 = ex2(x.x), p1 = ex2(x.y);
         pk[e / 2] = Dt<T>::pack(p0, p1);
         if (kSplit) {
           const float2 hi = Dt<T>::unpack(pk[e / 2]);
           pl[e / 2] = Dt<T>::pack(p0 - hi.x, p1 - hi.y);
         }
-        lsum += p0 + p1;
+        lsum[(e / 2) % 2] = fadd2(lsum[(e / 2) % 2], make_float2(p0, p1));
       }
       // P(i) replaces P(i - 1), which O(i - 1) must have consumed: keys KH hf .. + KH - 1
       // are packed columns KH / 2 hf .. + KH / 2 - 1 (lo half NK / 2 further).
@@ -406,9 +407,9 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
-      l += lsum;  // this half's keys; the halves share the row's reference max
+      l += (lsum[0].x + lsum[1].x) + (lsum[0].y + lsum[1].y);  // this thread's keys; halves share the reference max
     }
-    confirm(nst - 1);  // nst >= 1; PV(nst - 2) was confirmed before P(nst - 1) was written
+    confirm(nst - 1);  // nst >= 1; the commit of PV(nst - 1) tracks every earlier MMA as well
     tc_fence_after_sync();
     float acc[DH];
 #pragma unroll
