@@ -33,7 +33,7 @@ constexpr int kBS = 16;
 constexpr int kNK = 64;                      // keys per stage
 constexpr int kKS = 4;                       // K ring stages (freed when S = Q K^T completes)
 constexpr int kVS = 4;                       // V ring stages (freed when O += P V completes)
-constexpr int kBars = 2 * (kKS + kVS) + 8;   // + s_full, p_full, o_full (2 each), q_ready, mma_done
+constexpr int kBars = 2 * (kKS + kVS) + 4;   // + p_full (2), q_ready, mma_done
 constexpr float kLog2e = 1.4426950408889634f;
 
 // SPLIT: P goes to the tensor cores as hi + lo halves (bf16 keeps 8 bits of a weight;
@@ -98,14 +98,14 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kVS * S::KSB);
   uint64_t* k_full = bars;                   // [kKS] TMA bytes of K landed
   uint64_t* v_full = k_full + kKS;           // [kVS] TMA bytes of V landed
-  uint64_t* k_empty = v_full + kVS;          // [kKS] S = Q K^T of the stage is done
-  uint64_t* v_empty = k_empty + kKS;         // [kVS] O += P V of the stage is done
-  uint64_t* s_full = v_empty + kVS;          // [2] S = Q K^T done
-  uint64_t* p_full = s_full + 2;             // [2] P(j) stored in TMEM, j even / odd
-  uint64_t* o_full = p_full + 2;             // [2] O += P(j) V(j) done, j even / odd
-  uint64_t* q_ready = o_full + 2;            // the softmax warps stored Q
+  // One commit per MMA group: S(j) done tells the softmax warps that S(j) is ready and the
+  // copy warp that K stage j % kKS is free; O(j) done frees V stage j % kVS (and O).
+  uint64_t* s_done = v_full + kVS;           // [kKS] S(j) = Q K(j)^T done, j % kKS
+  uint64_t* o_done = s_done + kKS;           // [kVS] O += P(j) V(j) done, j % kVS
+  uint64_t* p_full = o_done + kVS;           // [2] P(j) stored in TMEM, j even / odd
+  uint64_t* q_ready = p_full + 2;            // the softmax warps stored Q
   uint64_t* mma_done = q_ready + 1;          // every MMA of the CTA has completed (before TMEM is freed)
-  static_assert(kBars == 2 * (kKS + kVS) + 8, "barrier layout");
+  static_assert(kBars == 2 * (kKS + kVS) + 4, "barrier layout");
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + kBars);
   float* s_mx = reinterpret_cast<float*>(bars + kBars + 2);  // [2 stage parities][2 halves][128 rows] partial row maxima
   float* s_l = s_mx + 2 * 2 * 128;                           // [2 halves][128 rows] final partial row sums
@@ -136,16 +136,14 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
   if (tid == 0) {
     for (int i = 0; i < kKS; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
+      mbar_init(&s_done[i], 1);
     }
     for (int i = 0; i < kVS; ++i) {
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&o_done[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], SW);
-      mbar_init(&o_full[i], 1);
     }
     mbar_init(q_ready, SW);
     mbar_init(mma_done, 1);
@@ -190,7 +188,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       const int c4 = p.layer * p.nbt + blk;
       const int sk = i % kKS, sv = i % kVS;
       if (lane == 0) {
-        if (i >= kKS && !mbar_wait_until(&k_empty[sk], ((i / kKS) - 1) & 1, deadline)) {
+        if (i >= kKS && !mbar_wait_until(&s_done[sk], ((i / kKS) - 1) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
           ok = false;
         }
@@ -200,7 +198,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       if (ok && lane < kCopies)
         tma_load_5d(sK + sk * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_k, 0, 0, c, head, c4, &k_full[sk]);
       if (lane == 0 && ok) {
-        if (i >= kVS && !mbar_wait_until(&v_empty[sv], ((i / kVS) - 1) & 1, deadline)) {
+        if (i >= kVS && !mbar_wait_until(&o_done[sv], ((i / kVS) - 1) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
           ok = false;
         }
@@ -232,8 +230,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
             umma_f16_ss(tmem + s_col(b), a, bd, idesc_s, kk > 0);
           }
         }
-        umma_commit(&s_full[b]);
-        umma_commit(&k_empty[st]);
+        umma_commit(&s_done[st]);
         return true;
       };
       auto issue_o = [&](int j) -> bool {
@@ -249,8 +246,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
             umma_f16_ts(tmem + S::OCOL, tmem + S::PCOL + h * (kNK / 2) + kb * 8, bd, idesc_o, j > 0 || h > 0 || kb > 0);
           }
         }
-        umma_commit(&o_full[b]);
-        umma_commit(&v_empty[st]);
+        umma_commit(&o_done[st]);
         return true;
       };
       // p_full(i) also means the softmax warps have read S(i), so S(i + 2) may overwrite it.
@@ -315,18 +311,18 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
     // row's max grows by more than kSlack (in log2 units): weights then stay below 2^kSlack
     // and, in the common case, O needs no rescaling at all. When it does, the warps rescale
     // their rows of O in TMEM after the previous P V completed and before this stage's P is
-    // released to the MMA thread. PV(j) completes on o_full[j % 2] and is waited for before
-    // P(j + 1) is written (P has one buffer), so PV(j + 2), the next phase of that barrier,
-    // cannot have been issued: every parity wait is unambiguous.
+    // released to the MMA thread. Parity waits stay unambiguous: S(i + kKS) cannot be issued
+    // before P(i + kKS - 2) exists, and the softmax warps wait for O(j) only before P(j + 1)
+    // is released, when O(j + kVS) cannot have been issued.
     constexpr float kSlack = 8.f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     auto confirm = [&](int j) {  // PV(j) has completed
-      if (ok && !mbar_wait_until(&o_full[j % 2], (j / 2) & 1, deadline)) ok = false;
+      if (ok && !mbar_wait_until(&o_done[j % kVS], (j / kVS) & 1, deadline)) ok = false;
     };
     for (int i = 0; i < nst; ++i) {
       const int b = i % 2;
-      if (ok && !mbar_wait_until(&s_full[b], (i / 2) & 1, deadline)) ok = false;
+      if (ok && !mbar_wait_until(&s_done[i % kKS], (i / kKS) & 1, deadline)) ok = false;
       tc_fence_after_sync();
       const int key0 = i * kNK + hf * KH;
       uint32_t sa[KH];
