@@ -190,6 +190,14 @@ __device__ inline void cp_async_wait_all() {
 
 // Acquire-release fence at GPU scope (cheaper than the sequentially consistent __threadfence).
 __device__ inline void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// Atomic add with acquire and release semantics at GPU scope: earlier writes (of this
+// thread, and of threads that synchronized with it first) are visible to whoever reads
+// the counter afterwards, and later reads see what earlier releasers published.
+__device__ inline int atom_add_acq_rel_gpu(int32_t* ptr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
+}
 __device__ inline int ld_acquire_gpu(const int32_t* ptr) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");

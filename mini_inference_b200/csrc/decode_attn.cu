@@ -436,24 +436,22 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   if (npend == 0) return;
 
   // Tickets for this CTA's chunks; the CTA holding the last ticket of an item merges it.
-  // The barrier orders every consumer's partial writes before thread 0's release fence;
-  // the last holder's acquire fence orders them before its CTA's reads.
+  // The barrier orders every consumer's partial writes before thread 0's tickets, whose
+  // release publishes them; for the last holder the same atomic's acquire (then the
+  // barrier below) orders the other chunks' partials before its threads' reads. One
+  // acquire-release atomic per ticket measured faster than fence + atomic + fence.
   if (tid == 0) {
-    fence_acq_rel_gpu();
     int ticket[kMaxPending];
 #pragma unroll
     for (int k = 0; k < kMaxPending; ++k)  // all in flight together
-      if (k < npend) ticket[k] = atomicAdd(p.counters + s_pend[k].x, 1);
-    bool any = false;
+      if (k < npend) ticket[k] = atom_add_acq_rel_gpu(p.counters + s_pend[k].x, 1);
 #pragma unroll
     for (int k = 0; k < kMaxPending; ++k) {
       if (k >= npend) break;
       const bool last = ticket[k] == s_pend[k].y - 1;
       if (last) p.counters[s_pend[k].x] = 0;  // ready for the next call
       s_last[k] = last;
-      any |= last;
     }
-    if (any) fence_acq_rel_gpu();
   }
   __syncthreads();
   if (warp == kNC || s_bad) return;
