@@ -135,6 +135,66 @@ def run_prefill(dev, seed: int, layers: int = 2, reps: int = 10) -> dict:
                          "peak_kind": f"{kind} dense bf16 GEMM (burst)"}}
 
 
+def run_long_context(dev, seed: int, reps: int = 10) -> dict:
+    """Config 5's attention kernel alone: 7B shapes (Hq 28 / Hkv 4 / d 128, bf16), 64
+    sequences with contexts U{8192..32768}, one fused append + decode attention call per
+    rep over one ~2.7 GB layer pool (far above L2). Bytes as ``bytes_per_layer_call`` with
+    the 7B dims.
+    """
+    from mini_inference_b200 import ops
+
+    hq, hkv, d, batch = 28, 4, 128, 64
+    g = torch.Generator().manual_seed(seed + 5)
+    ctx = torch.randint(8192, 32769, (batch,), generator=g).tolist()
+    nblk = [(c + 1 + BS - 1) // BS for c in ctx]
+    nb = sum(nblk) + 8
+    perm = torch.randperm(nb, generator=g)
+    tab = torch.zeros(batch, max(nblk), dtype=torch.int32)
+    at = 0
+    for i, n in enumerate(nblk):
+        tab[i, :n] = perm[at:at + n]
+        at += n
+    gd = torch.Generator(device=dev).manual_seed(seed + 13)
+    k = torch.randn(1, nb + 1, hkv, BS, d, generator=gd, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(1, nb + 1, hkv, BS, d, generator=gd, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(batch, hq, d, generator=gd, device=dev, dtype=torch.bfloat16)
+    kn = torch.randn(batch, hkv, d, generator=gd, device=dev, dtype=torch.bfloat16)
+    vn = torch.randn(batch, hkv, d, generator=gd, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    tab_d = tab.to(dev)
+    slot = torch.tensor([int(tab[i, c // BS]) * BS + c % BS for i, c in enumerate(ctx)], dtype=torch.int64, device=dev)
+    lens = torch.tensor([c + 1 for c in ctx], dtype=torch.int32, device=dev)
+    ws = torch.zeros(ops.decode_workspace_bytes(batch, hkv, max(nblk), BS, d, hq), dtype=torch.uint8, device=dev)
+    pool, tabs = ops.make_pool(k, v), ops.make_tables(tab_d)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def call() -> None:  # the append rewrites the same row every rep: the keys do not change
+        ops.decode_attention(pool, 0, tabs, q, lens, ws, k_new=kn, v_new=vn, slot_mapping=slot, out=out,
+                             status=status)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ops.raise_device_errors(status)
+    ms = e0.elapsed_time(e1) / reps
+    elt = 2
+    nbytes = (sum(c + 1 for c in ctx) * hkv * d * elt * 2 + batch * hq * d * elt * 2 + batch * hkv * d * elt * 2
+              + sum(nblk) * 4)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    peaks, kind = measured_peaks()
+    return {"workload": "config 5 attention kernel: 64 sequences, context U{8192..32768}, bf16, Hq 28 / Hkv 4 / "
+                        "d 128, one fused append + decode attention call over a 2.7 GB layer pool",
+            "ms_per_call": round(ms, 4), "bytes_per_call": nbytes, "gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": f"{kind} copy bandwidth"}}
+
+
 def bytes_per_layer_call(ctx: list[int]) -> int:
     """Algorithmic bytes of one fused append + decode attention call over the batch.
 
@@ -370,6 +430,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     }
     if not args.profile_case:
         line["prefill"] = run_prefill(dev, seed=rank)
+        line["long_context"] = run_long_context(dev, seed=rank)
     if world == 1 and not args.profile_case:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -552,6 +613,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the tcgen05 prefill leg (config 4's prefill), for ncu captures")
+    ap.add_argument("--long-only", action="store_true",
+                    help="only config 5's attention kernel (7B bf16, contexts 8k..32k), for ncu captures")
     ap.add_argument("--profile-case", action="store_true",
                     help="small case for ncu captures: 4 layer pools (536 MB, still above L2), no e2e / CPU legs")
     args = ap.parse_args()
@@ -560,10 +623,11 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.prefill_only:
+    if args.prefill_only or args.long_only:
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         torch.cuda.set_device(dev)
-        print(json.dumps(run_prefill(dev, seed=0, reps=args.steps)), flush=True)
+        run = run_prefill if args.prefill_only else run_long_context
+        print(json.dumps(run(dev, seed=0, reps=args.steps)), flush=True)
         return
     rank, world, local = dist_setup(args.gpus)
     try:
