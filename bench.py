@@ -417,7 +417,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": f"{peak_kind} copy bandwidth",
                      "traffic": traffic, "algorithmic_bytes_per_launch": call_bytes,
-                     "kernel": "pkv decode_kernel<half,64> (fused append + paged attention, split items merged)",
+                     "kernel": "pkv decode_kernel<half,64,2,8> (fused append + paged attention, split items merged)",
                      "launch_us": round(per_launch_ms * 1e3, 3)},
         "e2e": {"value": round(world * step_bytes * args.e2e_steps / (ms_e2e_job * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -428,7 +428,9 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "gpu_launches": args.steps * (1 + LAYERS * DECODE_KERNELS) + args.steps * LAYERS * DECODE_KERNELS + e2e_launches,
         "clocks": clocks.summary(),
     }
-    if not args.profile_case:
+    if args.profile_case:  # no end-to-end leg in the capture case
+        line["e2e"] = None
+    else:
         line["prefill"] = run_prefill(dev, seed=rank)
         line["long_context"] = run_long_context(dev, seed=rank)
     if world == 1 and not args.profile_case:
