@@ -180,6 +180,33 @@ PKV_API int pkv_prefill_attention(const pkv_pool* pool, int32_t layer, const pkv
                           const void* q, int64_t q_stride_t, int64_t q_stride_h, float scale,
                           int32_t* status_dev, pkv_stream_t stream);
 
+/*
+ * Rotary position embedding of q and k, fused with the KV append (the "qkv-post"
+ * step). Replaces the split and head views of Attention.forward, the table lookup of
+ * RotaryEmbedding.forward and apply_rope (engine/model.py:201-224, 236-249) and, with
+ * slot_mapping, the index_put append of the new K/V rows (engine/kv_cache.py:288-289,
+ * 613-614). q and k come out bit-identical to the reference's eager ops on the same
+ * tables: r(r(x*cos) + r(rotate_half(x)*sin)), each step in float32, rounded once.
+ *
+ *   qkv   : token t's row [q (Hq*d) | k (Hkv*d) | v (Hkv*d)] at qkv + t*qkv_stride
+ *           (the qkv_proj output, bias included), storage dtype of the pool
+ *   positions : int64 [n_tokens], each in [0, max_positions)
+ *   cos_table, sin_table : [max_positions, d] in the storage dtype (the reference's
+ *           float32 tables cast to it, engine/model.py:190-210)
+ *   q_out : token t, query head h at q_out + t*q_out_stride_t + h*q_out_stride_h
+ *   k_out (NULL = not written): token t, kv head j at k_out + t*k_out_stride_t + j*k_out_stride_h
+ *   slot_mapping (NULL = no append): rotated k and v of token t written to the pool at
+ *           (layer, slot); a negative slot is skipped. At least one of k_out and
+ *           slot_mapping must be given. The decode path passes k_out and lets
+ *           pkv_decode_attention append (k_new = k_out, v_new = the v columns of qkv).
+ * Out-of-range positions or slots are reported in status (PKV_ERR_OUT_OF_RANGE).
+ */
+PKV_API int pkv_rope_append(const pkv_pool* pool, int32_t layer, const void* qkv, int64_t qkv_stride,
+                    int64_t n_tokens, int32_t num_q_heads, const int64_t* positions, const void* cos_table,
+                    const void* sin_table, int64_t max_positions, void* q_out, int64_t q_out_stride_t,
+                    int64_t q_out_stride_h, void* k_out, int64_t k_out_stride_t, int64_t k_out_stride_h,
+                    const int64_t* slot_mapping, int32_t* status_dev, pkv_stream_t stream);
+
 /* ------------------------------------------------------------------ metadata builder (GPU) */
 /*
  * Decode metadata from a device-resident table mirror, instead of host lists

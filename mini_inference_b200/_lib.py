@@ -1,6 +1,6 @@
 """ctypes binding of ``libpkv.so``, the C ABI declared in ``include/pkv.h``.
 
-The library is built in-tree (``python -m mini_inference_b200.build``). There is
+The library is built in-tree (``python mini_inference_b200/build.py``). There is
 no fallback: if it is missing or fails to load, importing this module raises,
 and every op of the package is unusable.
 """
@@ -53,6 +53,9 @@ SIGNATURES: dict[str, tuple] = {
     "pkv_version": (c_int32, []),
     "pkv_kv_append": (c_int32, [P_POOL, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                 c_void_p]),
+    "pkv_rope_append": (c_int32, [P_POOL, c_int32, c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
+                                  c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                                  c_void_p]),
     "pkv_decode_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64, c_int64,
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                        c_void_p, c_float, c_int32, c_void_p, c_int64, c_void_p, c_void_p]),
@@ -96,7 +99,7 @@ SIGNATURES: dict[str, tuple] = {
 
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
-        raise ImportError(f"{LIB_PATH.name} is not built; run `python -m mini_inference_b200.build` "
+        raise ImportError(f"{LIB_PATH.name} is not built; run `python mini_inference_b200/build.py` "
                           "(the paged-KV path has no fallback without it)")
     lib = ctypes.CDLL(str(LIB_PATH))
     for name, (res, args) in SIGNATURES.items():

@@ -1,6 +1,6 @@
 """Build the sm_100a shared library ``libpkv.so`` in-tree with nvcc.
 
-    python -m mini_inference_b200.build        # or: python mini_inference_b200/build.py
+    python mini_inference_b200/build.py        # runs without importing the package (which loads the library)
 
 Every ``csrc/*.cu`` and ``csrc/*.cpp`` is compiled for
 ``-gencode arch=compute_100a,code=sm_100a`` into ``_build/`` (in parallel; a file

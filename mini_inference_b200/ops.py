@@ -82,6 +82,65 @@ def kv_append(pool: PkvPool, layer: int, k_rows: torch.Tensor, v_rows: torch.Ten
                             k_rows.stride(1), slot_mapping.data_ptr(), _ptr(status), _stream()), "kv_append")
 
 
+def rope_tables(head_dim: int, max_positions: int, theta: float, dtype: torch.dtype,
+                device: torch.device | str) -> tuple[torch.Tensor, torch.Tensor]:
+    """The reference's cos / sin tables ``[max_positions, head_dim]``, cast to ``dtype``.
+
+    The same torch calls as ``RotaryEmbedding._build`` (engine/model.py:190-199): one
+    frequency ``theta^(-2i/d)`` per feature pair computed on the host in float32, positions
+    times frequencies on ``device``, the half-table repeated twice, cos and sin in float32,
+    then the cast the reference applies per lookup (engine/model.py:208-210). Built on the
+    same device, the tables are bit-identical to the reference's.
+    """
+    exponents = torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim
+    inv_freq = (1.0 / (theta**exponents)).to(device)
+    positions = torch.arange(max_positions, device=device, dtype=torch.float32)
+    freqs = torch.outer(positions, inv_freq)
+    angles = torch.cat([freqs, freqs], dim=-1)
+    return angles.cos().to(dtype).contiguous(), angles.sin().to(dtype).contiguous()
+
+
+def rope_append(pool: PkvPool, layer: int, qkv: torch.Tensor, positions: torch.Tensor, cos: torch.Tensor,
+                sin: torch.Tensor, num_q_heads: int, q_out: torch.Tensor | None = None, k_out: torch.Tensor | bool = False,
+                slot_mapping: torch.Tensor | None = None,
+                status: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Rotate q and k of ``qkv`` rows ``[N, (Hq + 2 Hkv) * d]`` by ``positions`` (int64 [N]).
+
+    Returns ``(q_out [N, Hq, d], k_out [N, Hkv, d] or None)``. With ``slot_mapping``
+    (int64 [N]) the rotated k and the v columns are also written to the pool at
+    ``layer``; ``k_out=True`` allocates the rotated keys, a tensor receives them. The
+    results are bit-identical to the reference's ``apply_rope`` on the same tables.
+    """
+    _require_cuda(qkv, positions, cos, sin, q_out, slot_mapping, k_out if isinstance(k_out, torch.Tensor) else None)
+    n = qkv.shape[0]
+    hkv, d = pool.num_kv_heads, pool.head_dim
+    if qkv.dim() != 2 or qkv.shape[1] != (num_q_heads + 2 * hkv) * d or qkv.stride(1) != 1:
+        raise ValueError("qkv must be [N, (Hq + 2 Hkv) * head_dim] with a contiguous last dimension")
+    if cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] != d or not (cos.is_contiguous() and sin.is_contiguous()):
+        raise ValueError("cos / sin must be contiguous [max_positions, head_dim] tables")
+    if cos.dtype != qkv.dtype or sin.dtype != qkv.dtype or pkv_dtype(qkv.dtype) != pool.dtype:
+        raise ValueError("qkv, the tables and the pool must share one dtype")
+    if positions.dtype != torch.int64 or not positions.is_contiguous() or positions.numel() != n:
+        raise ValueError("positions must be a contiguous int64 tensor with one entry per row")
+    if slot_mapping is not None and (slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous()):
+        raise ValueError("slot_mapping must be a contiguous int64 tensor")
+    if q_out is None:
+        q_out = torch.empty(n, num_q_heads, d, dtype=qkv.dtype, device=qkv.device)
+    if k_out is True:
+        k_out = torch.empty(n, hkv, d, dtype=qkv.dtype, device=qkv.device)
+    elif k_out is False:
+        k_out = None
+    for t in (q_out, k_out):
+        if t is not None and t.stride(-1) != 1:
+            raise ValueError("q_out / k_out must have a contiguous last dimension")
+    check(lib.pkv_rope_append(
+        ctypes.byref(pool), layer, qkv.data_ptr(), qkv.stride(0), n, num_q_heads, positions.data_ptr(),
+        cos.data_ptr(), sin.data_ptr(), cos.shape[0], q_out.data_ptr(), q_out.stride(0), q_out.stride(1),
+        _ptr(k_out), k_out.stride(0) if k_out is not None else 0, k_out.stride(1) if k_out is not None else 0,
+        _ptr(slot_mapping), _ptr(status), _stream()), "rope_append")
+    return q_out, k_out
+
+
 def decode_workspace_bytes(batch: int, num_kv_heads: int, max_blocks: int, block_size: int, head_dim: int,
                            num_q_heads: int) -> int:
     return int(lib.pkv_decode_workspace_bytes(batch, num_kv_heads, max_blocks, block_size, head_dim, num_q_heads))

@@ -23,6 +23,9 @@ Ham12-3/mini-inference (pure Python + PyTorch, run on the CPU) and records:
 * ``prefill_<name>.npz`` -- ``PackedPrefillContext(...).attend`` without a prefix
   (several prompts and one prompt alone) and with prefix-cache hits
   (``engine/kv_cache.py:252-297``).
+* ``rope_<name>.npz`` -- ``RotaryEmbedding`` and ``apply_rope``
+  (``engine/model.py:169-224``) on seeded q / k at scattered positions: the float32
+  table rows, the rows cast to the model dtype, q, k and the rotated q, k.
 
 The reference does not travel with this repository, so the fixtures are
 committed and this script is only rerun by hand.
@@ -344,14 +347,41 @@ def make_prefill_case(PagedKVCache, name: str, dtype, hq: int, hkv: int, d: int,
     )
 
 
+def make_rope_case(RotaryEmbedding, apply_rope, name: str, dtype, hq: int, hkv: int, d: int, n: int,
+                   max_positions: int, theta: float, seed: int) -> None:
+    g = torch.Generator().manual_seed(seed)
+    rope = RotaryEmbedding(d, max_positions, theta)
+    positions = torch.randint(0, max_positions, (1, n), generator=g)
+    positions[0, :3] = torch.tensor([0, 1, max_positions - 1])  # both ends of the table
+    cos, sin = rope(positions, dtype)  # [1, 1, n, d] in the model dtype
+    q = (torch.randn(1, hq, n, d, generator=g) * 2).to(dtype)
+    k = (torch.randn(1, hkv, n, d, generator=g) * 2).to(dtype)
+    q_rot, k_rot = apply_rope(q, k, cos, sin)
+    np.savez_compressed(
+        HERE / f"rope_{name}.npz",
+        dtype=np.array(str(dtype).replace("torch.", "")), theta=np.array(theta), max_positions=np.array(max_positions),
+        positions=positions[0].numpy(), cos_f32=rope._cos[positions[0]].numpy(), sin_f32=rope._sin[positions[0]].numpy(),
+        cos=_np(cos[0, 0]), sin=_np(sin[0, 0]), q=_np(q[0].transpose(0, 1)), k=_np(k[0].transpose(0, 1)),
+        q_rot=_np(q_rot[0].transpose(0, 1)), k_rot=_np(k_rot[0].transpose(0, 1)),
+    )
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True, help="path of a Ham12-3/mini-inference checkout")
+    ap.add_argument("--only", choices=["rope"], help="write only these fixtures")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     from engine.kv_cache import PagedKVCache  # noqa: E402  (the reference's own class)
+    from engine.model import RotaryEmbedding, apply_rope  # noqa: E402
 
     torch.set_num_threads(4)
+    # Qwen2.5-0.5B (d 64, theta 1e6) and 7B (d 128) rotary shapes; tokens as rows [n, heads, d].
+    make_rope_case(RotaryEmbedding, apply_rope, "fp16_h14_d64", torch.float16, 14, 2, 64, 37, 32768, 1e6, seed=11)
+    make_rope_case(RotaryEmbedding, apply_rope, "bf16_h28_d128", torch.bfloat16, 28, 4, 128, 21, 33024, 1e6, seed=12)
+    if args.only == "rope":
+        print("rope fixtures written to", HERE)
+        return
     make_allocator_traces(PagedKVCache)
     make_write_index(PagedKVCache)
     # The reference's own tiny test shapes (tests/test_kv_cache.py:158-160,179-207): 4 / 2 heads, dim 8, blocks of 4.

@@ -22,7 +22,7 @@ def test_header_declares_the_entry_points():
     names = declared_functions()
     for required in ("pkv_kv_append", "pkv_decode_attention", "pkv_prefill_attention", "pkv_build_decode_metadata",
                      "pkv_build_prefill_metadata", "pkv_copy_blocks", "pkv_bm_allocate", "pkv_bm_free",
-                     "pkv_bm_register_prefix", "pkv_bm_ensure_capacity"):
+                     "pkv_bm_register_prefix", "pkv_bm_ensure_capacity", "pkv_rope_append"):
         assert required in names
     assert len(names) >= 30
 
