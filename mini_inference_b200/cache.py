@@ -440,6 +440,33 @@ class PagedDecodeContext:
         self._attends += 1
         return out.transpose(1, 2)
 
+    def attend_qkv(self, layer_idx: int, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                   num_q_heads: int) -> torch.Tensor:
+        """The ``qkv_proj`` output ``[B, 1, (Hq + 2 Hkv) d]`` -> ``[B, Hq, 1, d]``, RoPE included.
+
+        Replaces the split, head views and ``apply_rope`` of Attention.forward
+        (engine/model.py:241-250) plus :meth:`attend`: ``pkv_rope_append`` rotates q and k
+        (bit-identical to the reference's) on the full ``cos`` / ``sin`` tables of
+        ``ops.rope_tables``, then the fused append + paged attention kernel runs on them.
+        """
+        batch = qkv.shape[0]
+        rows = qkv.reshape(batch, -1)
+        hkv, d = self.cache.num_kv_heads, self.cache.head_dim
+        # The rotated keys get the v columns' row stride, so the decode kernel reads both
+        # through one (row, head) stride pair and nothing is copied.
+        k_store = torch.empty_like(rows)
+        k_rot = k_store[:, :hkv * d].view(batch, hkv, d)
+        q_rot, _ = ops.rope_append(self.cache.pool, layer_idx, rows, self.positions, cos, sin, num_q_heads,
+                                   k_out=k_rot, status=self.cache.status)
+        v_new = rows[:, (num_q_heads + hkv) * d:].view(batch, hkv, d)
+        ws = self.cache.workspace(self.cache.max_seqs, num_q_heads)
+        out = torch.empty(batch, 1, num_q_heads, d, dtype=qkv.dtype, device=qkv.device)
+        ops.decode_attention(self.cache.pool, layer_idx, self.tables, q_rot, self.context_lens, ws, k_new=k_rot,
+                             v_new=v_new, slot_mapping=self.slot_mapping, out=out[:, 0], status=self.cache.status,
+                             inputs_ready=self._attends > 0)  # the rotation writes only q and k_new, read later
+        self._attends += 1
+        return out.transpose(1, 2)
+
     def commit(self) -> None:
         self.cache._bm.commit_decode(self._slots_np)
 
@@ -489,6 +516,24 @@ class PackedPrefillContext:
         out = torch.empty(n, hq, d, dtype=q.dtype, device=q.device)
         ops.prefill_attention(self.cache.pool, layer_idx, self.tables, q[0].transpose(0, 1), self.cu_seqlens,
                               self.starts_dev, self.max_new, out=out, status=self.cache.status)
+        return out.unsqueeze(0).transpose(1, 2)
+
+    def attend_qkv(self, layer_idx: int, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                   num_q_heads: int) -> torch.Tensor:
+        """The ``qkv_proj`` output ``[1, N, (Hq + 2 Hkv) d]`` -> ``[1, Hq, N, d]``, RoPE included.
+
+        ``pkv_rope_append`` rotates q and k (bit-identical to the reference's
+        ``apply_rope``, engine/model.py:214-224) and writes the rotated keys and the
+        values to their slots in one pass, replacing :meth:`attend`'s separate append;
+        then the varlen paged kernel reads every sequence's keys in place.
+        """
+        rows = qkv.reshape(-1, qkv.shape[-1])
+        d = self.cache.head_dim
+        q_rot, _ = ops.rope_append(self.cache.pool, layer_idx, rows, self.positions, cos, sin, num_q_heads,
+                                   slot_mapping=self.slot_mapping, status=self.cache.status)
+        out = torch.empty(rows.shape[0], num_q_heads, d, dtype=qkv.dtype, device=qkv.device)
+        ops.prefill_attention(self.cache.pool, layer_idx, self.tables, q_rot, self.cu_seqlens, self.starts_dev,
+                              self.max_new, out=out, status=self.cache.status)
         return out.unsqueeze(0).transpose(1, 2)
 
     def commit(self) -> None:

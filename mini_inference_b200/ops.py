@@ -69,13 +69,16 @@ def make_tables(block_tables: torch.Tensor, seq_rows: torch.Tensor | None = None
 
 def kv_append(pool: PkvPool, layer: int, k_rows: torch.Tensor, v_rows: torch.Tensor, slot_mapping: torch.Tensor,
               status: torch.Tensor | None = None) -> None:
-    """Write rows ``[N, kv_heads, head_dim]`` (any token/head strides) to ``slot_mapping`` (int64 [N])."""
+    """Write rows ``[N, kv_heads, head_dim]`` (any strides; k and v are copied contiguous when
+    theirs differ) to ``slot_mapping`` (int64 [N])."""
     _require_cuda(k_rows, v_rows, slot_mapping)
-    if k_rows.shape != v_rows.shape or k_rows.stride() != v_rows.stride():
-        raise ValueError("k and v rows must have the same shape and strides")
+    if k_rows.shape != v_rows.shape:
+        raise ValueError("k and v rows must have the same shape")
     if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
         raise ValueError("slot_mapping must be a contiguous int64 tensor")
-    if k_rows.stride(-1) != 1:
+    # One (token, head) stride pair serves both: the reference hands over k as apply_rope's
+    # fresh output and v as a view of the projection, whose strides differ.
+    if k_rows.stride(-1) != 1 or k_rows.stride() != v_rows.stride():
         k_rows, v_rows = k_rows.contiguous(), v_rows.contiguous()
     n = k_rows.shape[0]
     check(lib.pkv_kv_append(ctypes.byref(pool), layer, k_rows.data_ptr(), v_rows.data_ptr(), n, k_rows.stride(0),

@@ -179,3 +179,45 @@ def test_out_of_range_position_is_reported(dev):
     ops.rope_append(pool, 0, qkv, positions, cos, sin, hq, k_out=True, status=status)
     with pytest.raises((IndexError, PkvError)):
         ops.raise_device_errors(status)
+
+
+@pytest.mark.parametrize("dtype,hq,hkv,d", SHAPES)
+def test_contexts_attend_qkv_equals_rope_then_attend(dev, dtype, hq, hkv, d):
+    """attend_qkv (qkv-post + kernels) = the reference's apply_rope + attend, bit for bit, pools included."""
+    from mini_inference_b200 import PagedKVCache, ops
+
+    def cache():
+        return PagedKVCache(2, hkv, d, num_blocks=48, block_size=16, max_seqs=4, max_len=512, dtype=dtype, device=dev)
+
+    ca, cb = cache(), cache()
+    cos, sin = ops.rope_tables(d, 4096, 1e6, dtype, dev)
+    g = torch.Generator(device=dev).manual_seed(9)
+    lengths = [40, 23, 7]
+    slots_a = [ca.allocate(n + 1) for n in lengths]
+    slots_b = [cb.allocate(n + 1) for n in lengths]
+    width = (hq + 2 * hkv) * d
+    pa = ca.packed_prefill_context(slots_a, lengths)
+    pb = cb.packed_prefill_context(slots_b, lengths)
+    for layer in range(2):  # prefill
+        qkv = (torch.randn(1, sum(lengths), width, generator=g, device=dev) * 2).to(dtype)
+        out_a = pa.attend_qkv(layer, qkv, cos, sin, hq)
+        q, k, v = qkv.view(1, -1, hq + 2 * hkv, d).transpose(1, 2).split([hq, hkv, hkv], dim=1)
+        c, s = cos[pb.positions][None, None], sin[pb.positions][None, None]
+        out_b = pb.attend(layer, _eager(q, c, s), _eager(k, c, s), v)
+        assert torch.equal(out_a, out_b)
+    pa.commit(), pb.commit()
+    for step in range(3):  # decode
+        for c_, ss in ((ca, slots_a), (cb, slots_b)):
+            for s_ in ss:
+                assert c_.ensure_capacity(s_, c_.lengths[s_] + 1)
+        da, db = ca.decode_context(slots_a), cb.decode_context(slots_b)
+        for layer in range(2):
+            qkv = (torch.randn(len(lengths), 1, width, generator=g, device=dev) * 2).to(dtype)
+            out_a = da.attend_qkv(layer, qkv, cos, sin, hq)
+            q, k, v = qkv.view(len(lengths), 1, hq + 2 * hkv, d).transpose(1, 2).split([hq, hkv, hkv], dim=1)
+            c, s = cos[db.positions][:, None, None], sin[db.positions][:, None, None]
+            out_b = db.attend(layer, _eager(q, c, s), _eager(k, c, s), v)
+            assert torch.equal(out_a, out_b), (step, layer)
+        da.commit(), db.commit()
+    ca.raise_device_errors(), cb.raise_device_errors()
+    assert torch.equal(ca.k, cb.k) and torch.equal(ca.v, cb.v)
