@@ -195,6 +195,91 @@ def run_long_context(dev, seed: int, reps: int = 10) -> dict:
                          "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": f"{kind} copy bandwidth"}}
 
 
+def run_qkv_post(dev, seed: int, reps: int = 50) -> dict:
+    """``pkv_rope_append`` at 0.5B shapes (Hq 14 / Hkv 2 / d 64, fp16), beside the reference's
+    eager path for the same work on the same GPU: the split and head views, ``apply_rope``
+    (engine/model.py:214-224) as torch ops, and the index_put append (engine/kv_cache.py:288-289).
+
+    Prefill: a 4096-token pack (``max_num_batched_tokens``) with the append into the pool.
+    Decode: 64 tokens, rotated keys handed to the fused decode append (nothing written to the pool).
+    """
+    from mini_inference_b200 import ops
+
+    hq, hkv, d, dtype = HQ, HKV, D, torch.float16
+    width = (hq + 2 * hkv) * d
+    cos, sin = ops.rope_tables(d, 32768, 1e6, dtype, dev)
+    g = torch.Generator(device=dev).manual_seed(seed + 17)
+    peaks, kind = measured_peaks()
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def timed(fn) -> float:
+        """Device time per call: 10 calls recorded as one CUDA graph (the host's ~10 us per
+        Python-issued call would otherwise be what is measured), replayed ``reps`` times."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(10):
+                fn()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / (reps * 10) * 1e3  # us
+
+    def eager_rope(x, c, s):
+        x1, x2 = x.chunk(2, dim=-1)
+        return x * c + torch.cat([-x2, x1], dim=-1) * s
+
+    result = {}
+    for name, n, append in (("prefill_4096", 4096, True), ("decode_64", BATCH, False)):
+        qkv = torch.randn(n, width, generator=g, device=dev).to(dtype)
+        positions = torch.randint(0, 2048, (n,), generator=g, device=dev)
+        nb = n // BS + 2
+        k = torch.zeros(1, nb + 1, hkv, BS, d, dtype=dtype, device=dev)
+        v = torch.zeros_like(k)
+        pool = ops.make_pool(k, v)
+        slots = torch.randperm(nb * BS, device=dev)[:n] if append else None
+        q_out = torch.empty(n, hq, d, dtype=dtype, device=dev)
+        k_out = None if append else torch.empty(n, hkv, d, dtype=dtype, device=dev)
+
+        def ours():
+            ops.rope_append(pool, 0, qkv, positions, cos, sin, hq, q_out=q_out, k_out=k_out if k_out is not None else False,
+                            slot_mapping=slots, status=status)
+
+        def eager():  # the reference's ops on the same tensors (engine/model.py:201-250, engine/kv_cache.py:288-289)
+            q, kk, vv = qkv.view(1, n, hq + 2 * hkv, d).transpose(1, 2).split([hq, hkv, hkv], dim=1)
+            c, s = cos[positions][None, None], sin[positions][None, None]
+            q_rot, k_rot = eager_rope(q, c, s), eager_rope(kk, c, s)
+            if append:
+                blocks, offs = slots // BS, slots % BS
+                k[0][blocks, :, offs] = k_rot[0].transpose(0, 1)
+                v[0][blocks, :, offs] = vv[0].transpose(0, 1)
+            return q_rot
+
+        us, us_eager = timed(ours), timed(eager)
+        ops.raise_device_errors(status)
+        nbytes = n * (width * 2 + hq * d * 2 + (2 if append else 1) * hkv * d * 2 + 2 * d * 2)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        result[name] = {"tokens": n, "us_per_call": round(us, 2), "bytes_per_call": nbytes, "gbs": round(gbs, 1),
+                        "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "reference_eager_torch_us": round(us_eager, 2)}
+    result["workload"] = ("pkv_rope_append (RoPE fused with the KV append), 0.5B shapes fp16; the reference's eager "
+                          "torch ops for the same work timed beside it on the same GPU; both as CUDA-graph replays "
+                          "of 10 calls (device time)")
+    result["peak_kind"] = f"{kind} copy bandwidth"
+    return result
+
+
 def bytes_per_layer_call(ctx: list[int]) -> int:
     """Algorithmic bytes of one fused append + decode attention call over the batch.
 
@@ -433,6 +518,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     else:
         line["prefill"] = run_prefill(dev, seed=rank)
         line["long_context"] = run_long_context(dev, seed=rank)
+        line["qkv_post"] = run_qkv_post(dev, seed=rank)
     if world == 1 and not args.profile_case:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
