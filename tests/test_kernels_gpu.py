@@ -499,3 +499,39 @@ def test_decode_few_long_sequences_split_over_many_ctas(dev, dtype, hq, hkv, d, 
     name = "float16" if dtype == torch.float16 else "bfloat16"
     ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
     assert excess(to_np(out), round_to(ref, name), name) <= 0
+
+
+def test_chunked_prefill_matches_one_shot(dev):
+    """A long prompt prefilled in chunks (each chunk attends to the cached earlier ones) = one pass.
+
+    The varlen kernel takes any start per sequence, so chunked prefill (listed as missing in
+    the reference, README.md:470-473) is a scheduling choice: the pools come out bit-identical
+    and the outputs agree within the attention tolerance.
+    """
+    from mini_inference_b200 import PagedKVCache
+
+    hq, hkv, d = 14, 2, 64
+    n, chunks = 300, [128, 100, 72]
+    g = torch.Generator(device=dev).manual_seed(21)
+    q = torch.randn(1, hq, n, d, generator=g, device=dev).half()
+    k = torch.randn(1, hkv, n, d, generator=g, device=dev).half()
+    v = torch.randn(1, hkv, n, d, generator=g, device=dev).half()
+    caches = [PagedKVCache(1, hkv, d, num_blocks=32, block_size=16, max_seqs=2, max_len=512, dtype=torch.float16,
+                           device=dev) for _ in range(2)]
+    one, chunked = caches
+    s1 = one.allocate(n)
+    ctx = one.packed_prefill_context([s1], [n])
+    out_one = ctx.attend(0, q, k, v)
+    ctx.commit()
+    s2 = chunked.allocate(chunks[0])
+    outs, at = [], 0
+    for c in chunks:
+        ctx = chunked.packed_prefill_context([s2], [c])
+        outs.append(ctx.attend(0, q[:, :, at:at + c], k[:, :, at:at + c], v[:, :, at:at + c]))
+        ctx.commit()
+        at += c
+    one.raise_device_errors(), chunked.raise_device_errors()
+    assert chunked.lengths[s2] == one.lengths[s1] == n
+    assert chunked.block_tables[s2] == one.block_tables[s1]
+    assert torch.equal(chunked.k, one.k) and torch.equal(chunked.v, one.v)
+    torch.testing.assert_close(torch.cat(outs, dim=2), out_one, atol=2e-3, rtol=2e-3)
