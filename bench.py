@@ -363,10 +363,12 @@ def dist_setup(n_gpus: int):
 
         import torch.distributed as dist
 
-        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        timeout = datetime.timedelta(seconds=120)
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=timeout)
     return rank, world, local
 
 
