@@ -215,19 +215,29 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       constexpr uint32_t idesc_s = umma_idesc_f16(kBf16, false, 128, kNK);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBf16, true, 128, D);
       constexpr int NP = kSplit ? 2 : 1;  // P as hi + lo halves for bf16
+      // Descriptors of a group are computed before its barrier waits and pinned there, so
+      // the MMAs of a group issue back to back (a probe measured ~45 cycles per MMA that way
+      // against ~120 with each descriptor computed just before its MMA).
+      auto pin = [](uint64_t& x) { asm volatile("" : "+l"(x)); };
       auto issue_s = [&](int j) -> bool {  // S(j) into buffer j % 2, whose S(j - 2) P(j - 2) was made from
         const int st = j % kKS, b = j % 2;
+        uint64_t bk[D / 16], aq[D / 16];
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c = kk / 4, k16 = kk % 4;
+          bk[kk] = umma_desc_sw128(smem_u32(sK + st * S::KSB + c * kNK * 128 + k16 * 32), 16, 1024);
+          aq[kk] = kQT ? 0 : umma_desc_sw128(smem_u32(sQ + c * 128 * 128 + k16 * 32), 16, 1024);
+          pin(bk[kk]);
+          pin(aq[kk]);
+        }
         if (!mbar_wait_until(&k_full[st], (j / kKS) & 1, deadline)) return false;
         tc_fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const int c = kk / 4, k16 = kk % 4;
-          const uint64_t bd = umma_desc_sw128(smem_u32(sK + st * S::KSB + c * kNK * 128 + k16 * 32), 16, 1024);
           if (kQT) {
-            umma_f16_ts(tmem + s_col(b), tmem + S::QCOL + kk * 8, bd, idesc_s, kk > 0);
+            umma_f16_ts(tmem + s_col(b), tmem + S::QCOL + kk * 8, bk[kk], idesc_s, kk > 0);
           } else {
-            const uint64_t a = umma_desc_sw128(smem_u32(sQ + c * 128 * 128 + k16 * 32), 16, 1024);
-            umma_f16_ss(tmem + s_col(b), a, bd, idesc_s, kk > 0);
+            umma_f16_ss(tmem + s_col(b), aq[kk], bk[kk], idesc_s, kk > 0);
           }
         }
         umma_commit(&s_done[st]);
@@ -235,16 +245,21 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       };
       auto issue_o = [&](int j) -> bool {
         const int st = j % kVS, b = j % 2;
+        uint64_t bv[kNK / 16];
+#pragma unroll
+        for (int kb = 0; kb < kNK / 16; ++kb) {
+          bv[kb] = umma_desc_sw128(smem_u32(sV + st * S::KSB + kb * kBS * 128), kNK * 128, 1024);
+          pin(bv[kb]);
+        }
         if (!mbar_wait_until(&p_full[b], (j / 2) & 1, deadline)) return false;
         if (!mbar_wait_until(&v_full[st], (j / kVS) & 1, deadline)) return false;
         tc_fence_after_sync();
 #pragma unroll
         for (int h = 0; h < NP; ++h) {
 #pragma unroll
-          for (int kb = 0; kb < kNK / 16; ++kb) {
-            const uint64_t bd = umma_desc_sw128(smem_u32(sV + st * S::KSB + kb * kBS * 128), kNK * 128, 1024);
-            umma_f16_ts(tmem + S::OCOL, tmem + S::PCOL + h * (kNK / 2) + kb * 8, bd, idesc_o, j > 0 || h > 0 || kb > 0);
-          }
+          for (int kb = 0; kb < kNK / 16; ++kb)
+            umma_f16_ts(tmem + S::OCOL, tmem + S::PCOL + h * (kNK / 2) + kb * 8, bv[kb], idesc_o,
+                        j > 0 || h > 0 || kb > 0);
         }
         umma_commit(&o_done[st]);
         return true;
