@@ -12,7 +12,7 @@
 // The contraction runs on the fifth-generation tensor cores (tcgen05) with the
 // accumulators in tensor memory. One CTA takes one KV head of one sequence and TQ of
 // its new tokens; the M = 128 rows of the MMA tile are those tokens x the GQA group's
-// query heads (16 x 7 = 112 rows for Qwen2's group of 7), so every K/V block read
+// query heads (18 x 7 = 126 rows for Qwen2's group of 7), so every K/V block read
 // serves the whole group. Keys stream in stages of NK = 64 (four blocks) through TMA
 // rings with separate K and V stages: S = Q K^T (M 128 x N 64, fp32 in TMEM) frees its K
 // stage as soon as it completes, P V frees the V stage, so a K copy has two to three
@@ -482,6 +482,9 @@ int launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillPa
 template <typename T, int D>
 int launch_group(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillParams& p, int max_new, int hkv,
                  int seqs, cudaStream_t st) {
+  // As many tokens as fill the 128 rows: 18 x 7 = 126 for Qwen2's group of 7 (16 tokens
+  // would leave 16 rows idle), 16 x 8, 8 x 9..16.
+  if (p.group == 7) return launch_prefill<T, D, 18>(tk, tv, p, max_new, hkv, seqs, st);
   return p.group <= 8 ? launch_prefill<T, D, 16>(tk, tv, p, max_new, hkv, seqs, st)
                       : launch_prefill<T, D, 8>(tk, tv, p, max_new, hkv, seqs, st);
 }
