@@ -47,6 +47,7 @@ constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
 constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared memory
 constexpr int kMinCap = 16;        // items of up to 16 blocks are never split
+constexpr int kLongUnit = 256;     // blocks per CTA above which the split cap is tightened
 constexpr int kIssueLanes = 4;     // producer lanes issuing copies together
 constexpr int kMergeBatch = 4;     // chunk states a merging thread loads at once
 constexpr int kMaxPending = 8;     // split units of one CTA whose tickets are taken at the end
@@ -118,6 +119,29 @@ __device__ inline int warp_scan(int v, int lane) {
 struct Unit {
   int b, c, nch, i0, i1;
 };
+
+// Smallest cap in [max(kMinCap, ceil(T / C)), cap] whose units (ceil(n / cap) per item of
+// n blocks) fit C CTAs, by binary search; `cap` itself if even it does not fit. Run by one
+// warp over the clamped context lengths.
+__device__ __noinline__ int tightest_cap(const int* sCtx, int B, int C, int cap, int lane) {
+  auto units_at = [&](int c) {
+    int u = 0;
+    for (int i = lane; i < B; i += 32) {
+      const int n = (sCtx[i] + kBS - 1) / kBS;
+      u += n == 0 ? 0 : (n <= c ? 1 : (n + c - 1) / c);
+    }
+    return warp_sum(u);
+  };
+  if (units_at(cap) > C) return cap;
+  int tiles = 0;
+  for (int i = lane; i < B; i += 32) tiles += (sCtx[i] + kBS - 1) / kBS;
+  int lo = max(kMinCap, (warp_sum(tiles) + C - 1) / C);
+  while (lo < cap) {
+    const int mid = (lo + cap) / 2;
+    if (units_at(mid) <= C) cap = mid; else lo = mid + 1;
+  }
+  return cap;
+}
 
 template <typename T, int D, int NH, int RK>
 __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
@@ -193,7 +217,13 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     tiles = warp_sum(tiles);
     items = warp_sum(items);
     const int free_ctas = max(C - items, max(C / 4, 1));
-    const int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
+    int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
+    // The cap above budgets a whole extra chunk per item, which can leave CTAs without a
+    // unit. When units are long (more than kLongUnit blocks per CTA on average) the merges
+    // are cheap next to the streaming, so the smallest cap whose units still fit one wave
+    // is taken instead: every SM streams. (For short units the extra merges cost more than
+    // the shorter longest unit saves, measured; the search stays out of line for them.)
+    if (p.cap_override <= 0 && tiles > kLongUnit * C) cap = tightest_cap(sCtx, B, C, cap, lane);
     int carry_u = 0, carry_s = 0;
     for (int base = 0; base < B; base += 32) {
       const int i = base + lane;
