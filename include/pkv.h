@@ -116,7 +116,9 @@ PKV_API int pkv_kv_append(const pkv_pool* pool, int32_t layer, const void* k_new
  *   workspace: >= pkv_decode_workspace_bytes(...) bytes, 256-byte aligned, zeroed once
  *             before first use; every call leaves it ready for the next, whatever the
  *             next call's batch or table width. Calls that share a workspace must not
- *             overlap on the GPU. num_kv_heads <= 16.
+ *             overlap on the GPU.
+ * Supported: fp16 / bf16, block_size 16, head_dim 64 or 128, num_kv_heads 1, 2, 4 or 8,
+ * query heads per KV head <= 16, batch <= 1024; anything else returns PKV_ERR_UNSUPPORTED.
  * Query head h reads KV head h / (num_q_heads / num_kv_heads), as the reference's regrouping.
  */
 PKV_API int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
