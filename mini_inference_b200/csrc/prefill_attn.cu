@@ -23,6 +23,8 @@
 // mbarriers (MMA completion through tcgen05.commit) order the three roles. Only the
 // causal part of each sequence is visited; keys past a tile's last position are masked
 // to -inf.
+#include <algorithm>
+
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -34,6 +36,7 @@ constexpr int kNK = 64;                      // keys per stage
 constexpr int kKS = 4;                       // K ring stages (freed when S = Q K^T completes)
 constexpr int kVS = 4;                       // V ring stages (freed when O += P V completes)
 constexpr int kBars = 2 * (kKS + kVS) + 4;   // + p_full (2), q_ready, mma_done
+constexpr int kMaxSeqs = 2048;               // sequences per launch (the host splits larger packs)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // SPLIT: P goes to the tensor cores as hi + lo halves (bf16 keeps 8 bits of a weight;
@@ -57,7 +60,8 @@ template <int D, bool SPLIT> struct PrefillShape {
   static constexpr int SW = MIN_BLOCKS == 2 ? 4 : 8;
   static constexpr int HALVES = SW / 4;
   static constexpr int THREADS = (SW + 2) * 32;  // + 1 copy warp, 1 MMA warp
-  static constexpr int SMEM = 1024 + (QT ? 0 : QB) + (kKS + kVS) * KSB + (kBars + 2) * 8 + 3 * 2 * 128 * 4;
+  static constexpr int SMEM = 1024 + (QT ? 0 : QB) + (kKS + kVS) * KSB + (kBars + 2) * 8 + 3 * 2 * 128 * 4 +
+                              (kMaxSeqs + 1) * 4;  // + tiles before each sequence
 };
 
 struct PrefillParams {
@@ -71,6 +75,7 @@ struct PrefillParams {
   int64_t out_st, out_sh, q_st, q_sh, table_stride;
   int32_t table_rows, table_cols;
   int32_t group, layer, nbt, q_vec16, out_vec16;
+  int32_t num_seqs, seq_base, hkv;  // sequences of this launch; table row = seq_base + s without seq_rows
   float scale_log2;
 };
 
@@ -110,29 +115,25 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
   float* s_mx = reinterpret_cast<float*>(bars + kBars + 2);  // [2 stage parities][2 halves][128 rows] partial row maxima
   float* s_l = s_mx + 2 * 2 * 128;                           // [2 halves][128 rows] final partial row sums
 
-  const int tile = blockIdx.x, head = blockIdx.y, s = blockIdx.z;
+  int* sTiles = reinterpret_cast<int*>(s_l + 2 * 128);  // [num_seqs + 1] tiles before sequence s
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tok0 = p.cu[s];
-  const int n_new = p.cu[s + 1] - tok0;
-  if (tile * TQ >= n_new) return;
-  const int start = p.starts[s];
-  const int rows_here = min(TQ, n_new - tile * TQ);
-  const int q_first = start + tile * TQ;  // position of the tile's first query
-  int kend = q_first + rows_here;         // keys 0 .. kend-1 are visible to the tile
-  if (kend > p.table_cols * kBS) {
-    if (tid == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
-    kend = p.table_cols * kBS;
+  const int B = p.num_seqs, G = p.group;
+  if (warp == SW) {  // tiles per sequence, prefix-summed (a sequence without new tokens has none)
+    int carry = 0;
+    for (int base = 0; base < B; base += 32) {
+      const int i = base + lane;
+      const int n = i < B ? p.cu[i + 1] - p.cu[i] : 0;
+      int inc = n > 0 ? (n + TQ - 1) / TQ : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {  // inclusive warp scan
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      if (i < B) sTiles[i + 1] = carry + inc;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) sTiles[0] = 0;
   }
-  const int nkb = (kend + kBS - 1) / kBS;
-  const int nst = (kend + kNK - 1) / kNK;
-  int row = p.seq_rows ? p.seq_rows[s] : s;
-  if (row < 0 || row >= p.table_rows) {
-    if (tid == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
-    row = -1;
-  }
-  const int32_t* table = row >= 0 ? p.tables + row * p.table_stride : nullptr;
-  const int G = p.group;
-
   if (tid == 0) {
     for (int i = 0; i < kKS; ++i) {
       mbar_init(&k_full[i], 1);
@@ -159,6 +160,47 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
   const uint64_t deadline = global_ns() + kWaitBudgetNs;
   auto s_col = [](int b) { return (uint32_t)(b * kNK); };
 
+  // Work items: (sequence, 16-18-token tile, KV head), heads fastest; CTA g takes items g,
+  // g + gridDim.x, ... Every role walks the same items and numbers stages across them
+  // (stage j of the CTA = its item's stage j - base), so ring slots and barrier parities
+  // simply continue from one item to the next.
+  const int n_items = sTiles[B] * p.hkv;
+  struct Item {
+    int s, head, tile, tok0, n_new, start, rows_here, q_first, kend, nkb, nst;
+    const int32_t* table;
+  };
+  auto item_at = [&](int w) {
+    Item it;
+    it.head = w % p.hkv;
+    const int tw = w / p.hkv;
+    int lo = 0, hi = B - 1;  // the largest s with sTiles[s] <= tw: the sequence holding tile tw
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sTiles[mid] <= tw) lo = mid; else hi = mid - 1;
+    }
+    it.s = lo;
+    it.tile = tw - sTiles[lo];
+    it.tok0 = p.cu[lo];
+    it.n_new = p.cu[lo + 1] - it.tok0;
+    it.start = p.starts[lo];
+    it.rows_here = min(TQ, it.n_new - it.tile * TQ);
+    it.q_first = it.start + it.tile * TQ;  // position of the tile's first query
+    it.kend = it.q_first + it.rows_here;   // keys 0 .. kend-1 are visible to the tile
+    if (it.kend > p.table_cols * kBS) {
+      if (lane == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
+      it.kend = p.table_cols * kBS;
+    }
+    it.nkb = (it.kend + kBS - 1) / kBS;
+    it.nst = (it.kend + kNK - 1) / kNK;
+    int row = p.seq_rows ? p.seq_rows[lo] : p.seq_base + lo;
+    if (row < 0 || row >= p.table_rows) {
+      if (lane == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
+      row = -1;
+    }
+    it.table = row >= 0 ? p.tables + (int64_t)row * p.table_stride : nullptr;
+    return it;
+  };
+
   if (warp == SW) {
     // ---------------------------------------------------------------- TMA copies
     // One copy per lane (lane l < kCopies copies head_dim chunk l % DC of block l / DC of the
@@ -167,6 +209,13 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
     // the next window in flight meanwhile.
     constexpr int kCopies = (kNK / kBS) * DC;
     constexpr int kStagesPerWindow = 32 / (kNK / kBS);
+    const int b = lane / DC, c = lane % DC;
+    bool ok = true;
+    int gs = 0;  // stages of earlier items
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+    const Item it = item_at(w);
+    const int nst = it.nst, nkb = it.nkb, head = it.head;
+    const int32_t* table = it.table;
     auto lookup = [&](int kb) -> int {
       // Blocks past the visible keys are masked; the scratch block keeps their rows finite.
       int blk = (kb < nkb && table) ? table[kb] : p.nbt - 1;
@@ -177,8 +226,6 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       return blk;
     };
     int win = lookup(lane), win_next = lookup(32 + lane);
-    const int b = lane / DC, c = lane % DC;
-    bool ok = true;
     for (int i = 0; i < nst && ok; ++i) {
       if (i > 0 && i % kStagesPerWindow == 0) {
         win = win_next;
@@ -186,9 +233,10 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       }
       const int blk = __shfl_sync(0xffffffffu, win, (i * (kNK / kBS) + b) % 32);
       const int c4 = p.layer * p.nbt + blk;
-      const int sk = i % kKS, sv = i % kVS;
+      const int j = gs + i;  // the CTA's stage
+      const int sk = j % kKS, sv = j % kVS;
       if (lane == 0) {
-        if (i >= kKS && !mbar_wait_until(&s_done[sk], ((i / kKS) - 1) & 1, deadline)) {
+        if (j >= kKS && !mbar_wait_until(&s_done[sk], ((j / kKS) - 1) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
           ok = false;
         }
@@ -198,7 +246,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       if (ok && lane < kCopies)
         tma_load_5d(sK + sk * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_k, 0, 0, c, head, c4, &k_full[sk]);
       if (lane == 0 && ok) {
-        if (i >= kVS && !mbar_wait_until(&o_done[sv], ((i / kVS) - 1) & 1, deadline)) {
+        if (j >= kVS && !mbar_wait_until(&o_done[sv], ((j / kVS) - 1) & 1, deadline)) {
           report(p.status, PKV_ERR_TIMEOUT);
           ok = false;
         }
@@ -207,6 +255,8 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (ok && lane < kCopies)
         tma_load_5d(sV + sv * S::KSB + c * kNK * 128 + b * kBS * 128, &tmap_v, 0, 0, c, head, c4, &v_full[sv]);
+    }
+    gs += nst;
     }
   } else if (warp == SW + 1) {
     // ---------------------------------------------------------------- MMA issue
@@ -243,7 +293,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
         umma_commit(&s_done[st]);
         return true;
       };
-      auto issue_o = [&](int j) -> bool {
+      auto issue_o = [&](int j, bool first) -> bool {  // first: the item's first stage overwrites O
         const int st = j % kVS, b = j % 2;
         uint64_t bv[kNK / 16];
 #pragma unroll
@@ -259,18 +309,24 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
 #pragma unroll
           for (int kb = 0; kb < kNK / 16; ++kb)
             umma_f16_ts(tmem + S::OCOL, tmem + S::PCOL + h * (kNK / 2) + kb * 8, bv[kb], idesc_o,
-                        j > 0 || h > 0 || kb > 0);
+                        !first || h > 0 || kb > 0);
         }
         umma_commit(&o_done[st]);
         return true;
       };
-      // p_full(i) also means the softmax warps have read S(i), so S(i + 2) may overwrite it.
-      bool ok = mbar_wait_until(q_ready, 0, deadline) && issue_s(0) && (nst < 2 || issue_s(1));
-      for (int i = 0; i < nst && ok; ++i) {
-        ok = issue_o(i) && (i + 2 >= nst || issue_s(i + 2));
+      // p_full(j) also means the softmax warps have read S(j), so S(j + 2) may overwrite it.
+      // q_ready(k) comes after the softmax warps read item k - 1's O and waited for all its
+      // S: item k's first S and its O-overwriting first P V may go.
+      bool ok = true;
+      int gs = 0, k = 0;
+      for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++k) {
+        const int nst = item_at(w).nst;
+        ok = mbar_wait_until(q_ready, k & 1, deadline) && issue_s(gs) && (nst < 2 || issue_s(gs + 1));
+        for (int i = 0; i < nst && ok; ++i) ok = issue_o(gs + i, i == 0) && (i + 2 >= nst || issue_s(gs + i + 2));
+        gs += nst;
       }
       if (!ok) report(p.status, PKV_ERR_TIMEOUT);
-      umma_commit(mma_done);
+      if (k > 0) umma_commit(mma_done); else mbar_arrive(mma_done);
     }
   } else {
     // ---------------------------------------------------------------- softmax warps
@@ -282,9 +338,27 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
     const int hf = warp / 4;
     const int r = (warp % 4) * 32 + lane;  // TMEM lane = tile row
     const int t = r / G, gq = r - t * G;
-    const bool valid = r < TQ * G && t < rows_here;
-    const int qpos = q_first + t;
     const uint32_t tl = tmem + ((uint32_t)((warp % 4) * 32) << 16);
+    const int pair_bar = 1 + warp % 4;  // named barrier of warps w and w + 4
+    // O accumulates in TMEM across stages against a reference max m that moves only when a
+    // row's max grows by more than kSlack (in log2 units): weights then stay below 2^kSlack
+    // and, in the common case, O needs no rescaling at all. When it does, the warps rescale
+    // their rows of O in TMEM after the previous P V completed and before this stage's P is
+    // released to the MMA thread. Parity waits stay unambiguous: S(j + kKS) cannot be issued
+    // before P(j + kKS - 2) exists, and the softmax warps wait for O(j) only before P(j + 1)
+    // is released (or, for an item's last stage, before reading O), when O(j + kVS) cannot
+    // have been issued.
+    constexpr float kSlack = 8.f;
+    bool ok = true;
+    auto confirm = [&](int j) {  // PV(j) has completed
+      if (ok && !mbar_wait_until(&o_done[j % kVS], (j / kVS) & 1, deadline)) ok = false;
+    };
+    int gs = 0;  // stages of earlier items
+    for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
+    const Item it = item_at(w);
+    const int nst = it.nst, q_first = it.q_first, kend = it.kend, tok0 = it.tok0, tile = it.tile, head = it.head;
+    const bool valid = r < TQ * G && t < it.rows_here;
+    const int qpos = q_first + t;
     // Q row r, this thread's half of head_dim, as the S MMAs' A operand: into TMEM (packed
     // 16-bit pairs) or into the swizzled shared-memory tile; zeros for rows without a query.
     {
@@ -321,23 +395,11 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
     __syncwarp();
     if (lane == 0) mbar_arrive(q_ready);
 
-    const int pair_bar = 1 + warp % 4;  // named barrier of warps w and w + 4
-    // O accumulates in TMEM across stages against a reference max m that moves only when a
-    // row's max grows by more than kSlack (in log2 units): weights then stay below 2^kSlack
-    // and, in the common case, O needs no rescaling at all. When it does, the warps rescale
-    // their rows of O in TMEM after the previous P V completed and before this stage's P is
-    // released to the MMA thread. Parity waits stay unambiguous: S(i + kKS) cannot be issued
-    // before P(i + kKS - 2) exists, and the softmax warps wait for O(j) only before P(j + 1)
-    // is released, when O(j + kVS) cannot have been issued.
-    constexpr float kSlack = 8.f;
     float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    auto confirm = [&](int j) {  // PV(j) has completed
-      if (ok && !mbar_wait_until(&o_done[j % kVS], (j / kVS) & 1, deadline)) ok = false;
-    };
     for (int i = 0; i < nst; ++i) {
-      const int b = i % 2;
-      if (ok && !mbar_wait_until(&s_done[i % kKS], (i / kKS) & 1, deadline)) ok = false;
+      const int j = gs + i;  // the CTA's stage
+      const int b = j % 2;
+      if (ok && !mbar_wait_until(&s_done[j % kKS], (j / kKS) & 1, deadline)) ok = false;
       tc_fence_after_sync();
       const int key0 = i * kNK + hf * KH;
       uint32_t sa[KH];
@@ -363,7 +425,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       }
       float mx = mt[0] * p.scale_log2;  // -inf stays -inf
       if (HALVES == 2) {
-        float* mxb = s_mx + (i % 2) * 256;
+        float* mxb = s_mx + (j % 2) * 256;
         mxb[hf * 128 + r] = mx;
         named_barrier_sync(pair_bar, 64);
         mx = fmaxf(mx, mxb[(1 - hf) * 128 + r]);
@@ -376,7 +438,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
         l *= alpha;
       }
       if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        confirm(i - 1);
+        confirm(j - 1);
         tc_fence_after_sync();
 #pragma unroll
         for (int c = 0; c < DH / 32; ++c) {
@@ -406,7 +468,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       }
       // P(i) replaces P(i - 1), which O(i - 1) must have consumed: keys KH hf .. + KH - 1
       // are packed columns KH / 2 hf .. + KH / 2 - 1 (lo half NK / 2 further).
-      if (i > 0) confirm(i - 1);
+      if (i > 0) confirm(j - 1);  // the item's first P follows the previous item's last O, confirmed
       tc_fence_after_sync();
 #pragma unroll
       for (int c = 0; c < KH / 32; ++c) {
@@ -420,7 +482,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       if (lane == 0) mbar_arrive(&p_full[b]);
       l += (lsum[0].x + lsum[1].x) + (lsum[0].y + lsum[1].y);  // this thread's keys; halves share the reference max
     }
-    confirm(nst - 1);  // nst >= 1; the commit of PV(nst - 1) tracks every earlier MMA as well
+    confirm(gs + nst - 1);  // nst >= 1; the commit of this PV tracks every earlier MMA as well
     tc_fence_after_sync();
     float acc[DH];
 #pragma unroll
@@ -452,6 +514,8 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
         for (int e = 0; e < DH; e += 2) *reinterpret_cast<uint32_t*>(orow + e) = Dt<T>::pack(acc[e] * inv, acc[e + 1] * inv);
       }
     }
+    gs += nst;
+    }  // items
   }
   __syncthreads();
   if (warp == 0) {
@@ -473,9 +537,26 @@ int launch_prefill(const CUtensorMap& tk, const CUtensorMap& tv, const PrefillPa
     if (e != cudaSuccess) return cuda_status(e);
     configured = true;
   }
-  dim3 grid((max_new + TQ - 1) / TQ, hkv, seqs);
-  prefill_kernel<T, D, TQ><<<grid, S::THREADS, S::SMEM, st>>>(tk, tv, p);
-  return launch_status();
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  // Persistent CTAs: as many as are resident at once, or as many items as there can be.
+  // The work split is read from cu_seqlens on the device, kMaxSeqs sequences per launch.
+  for (int s0 = 0; s0 < seqs; s0 += kMaxSeqs) {
+    PrefillParams q = p;
+    q.num_seqs = min(kMaxSeqs, seqs - s0);
+    q.cu = p.cu + s0;
+    q.starts = p.starts + s0;
+    q.seq_base = s0;
+    if (p.seq_rows) q.seq_rows = p.seq_rows + s0;
+    const int64_t items = (int64_t)q.num_seqs * ((max_new + TQ - 1) / TQ) * hkv;
+    const int grid = (int)std::min<int64_t>(items, (int64_t)sms * S::MIN_BLOCKS);
+    prefill_kernel<T, D, TQ><<<grid, S::THREADS, S::SMEM, st>>>(tk, tv, q);
+    const int rc = launch_status();
+    if (rc != PKV_OK) return rc;
+  }
+  return PKV_OK;
 }
 
 // Query tokens per CTA: the tile's rows are tokens x group <= 128.
@@ -536,6 +617,9 @@ extern "C" int pkv_prefill_attention(const pkv_pool* pool, int32_t layer, const 
   p.layer = layer;
   p.nbt = pool->num_blocks_total;
   p.scale_log2 = scale * kLog2e;
+  p.hkv = hkv;
+  p.num_seqs = num_seqs;
+  p.seq_base = 0;
   p.q_vec16 = (reinterpret_cast<uintptr_t>(q) & 15) == 0 && ((q_stride_t | q_stride_h) & 7) == 0;
   p.out_vec16 = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && ((out_stride_t | out_stride_h) & 7) == 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
