@@ -120,6 +120,8 @@ def packed_prefill_attend(k_layer: np.ndarray, v_layer: np.ndarray, tables: Sequ
     out = np.zeros((hq, n_tok, d), dtype=acc)
     at = 0
     for table, a, n in zip(tables, starts, lengths):
+        if n == 0:  # no query: nothing to attend (the reference packs only sequences with tokens)
+            continue
         end = a + n
         rb, ro = write_index([table], [0], [end], bs)
         keys = k_layer[rb, :, ro].transpose(1, 0, 2)  # [Hkv, end, d]

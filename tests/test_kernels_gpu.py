@@ -535,3 +535,53 @@ def test_chunked_prefill_matches_one_shot(dev):
     assert chunked.block_tables[s2] == one.block_tables[s1]
     assert torch.equal(chunked.k, one.k) and torch.equal(chunked.v, one.v)
     torch.testing.assert_close(torch.cat(outs, dim=2), out_one, atol=2e-3, rtol=2e-3)
+
+
+def test_prefill_more_sequences_than_one_launch_holds(dev):
+    """2100 short sequences (some without new tokens): the host splits them over two persistent launches."""
+    from mini_inference_b200 import ops
+
+    rng = np.random.default_rng(13)
+    hq, hkv, d, bs = 14, 2, 64, 16
+    n_seq = 2100
+    lengths = rng.integers(0, 4, n_seq).tolist()  # 0..3 new tokens
+    starts = rng.integers(0, 20, n_seq).tolist()
+    ends = [a + n for a, n in zip(starts, lengths)]
+    nblk = [max(1, (e + bs - 1) // bs) for e in ends]
+    nb = sum(nblk) + 2
+    perm = rng.permutation(nb)
+    tables, at = [], 0
+    for n in nblk:
+        tables.append(perm[at:at + n].tolist())
+        at += n
+    kp = rng.standard_normal((nb + 1, hkv, bs, d)).astype(np.float32)
+    vp = rng.standard_normal((nb + 1, hkv, bs, d)).astype(np.float32)
+    total = sum(lengths)
+    q = rng.standard_normal((hq, total, d)).astype(np.float32)
+    k_new = rng.standard_normal((hkv, total, d)).astype(np.float32)
+    v_new = rng.standard_normal((hkv, total, d)).astype(np.float32)
+    kq, vq, qq = round_to(kp, "float16"), round_to(vp, "float16"), round_to(q, "float16")
+    knq, vnq = round_to(k_new, "float16"), round_to(v_new, "float16")
+    k_pool = torch.from_numpy(kq).half().to(dev)[None].contiguous()
+    v_pool = torch.from_numpy(vq).half().to(dev)[None].contiguous()
+    tab = np.full((n_seq, max(nblk)), -1, np.int32)
+    for i, t in enumerate(tables):
+        tab[i, :len(t)] = t
+    tabs = ops.make_tables(torch.from_numpy(tab).to(dev))  # no seq_rows: row = sequence index
+    pool = ops.make_pool(k_pool, v_pool)
+    cu = torch.tensor([0] + np.cumsum(lengths).tolist(), dtype=torch.int32, device=dev)
+    st = torch.tensor(starts, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    positions = torch.empty(total, dtype=torch.int64, device=dev)
+    slot_mapping = torch.empty(total, dtype=torch.int64, device=dev)
+    ops.build_prefill_metadata(tabs, cu, st, bs, total, positions, slot_mapping, status)
+    ops.kv_append(pool, 0, torch.from_numpy(knq).half().to(dev).transpose(0, 1),
+                  torch.from_numpy(vnq).half().to(dev).transpose(0, 1), slot_mapping, status)
+    qt = torch.from_numpy(qq).half().to(dev)
+    out = ops.prefill_attention(pool, 0, tabs, qt.transpose(0, 1), cu, st, max(lengths), status=status)
+    ops.raise_device_errors(status)
+    got = to_np(out).transpose(1, 0, 2)
+    ref = packed_prefill_attend(kq.astype(np.float64), vq.astype(np.float64), tables, starts, lengths,
+                                qq.astype(np.float64), knq.astype(np.float64), vnq.astype(np.float64))
+    assert np.isfinite(got).all()
+    assert excess(got, round_to(ref, "float16"), "float16") <= 0
