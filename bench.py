@@ -280,6 +280,74 @@ def run_qkv_post(dev, seed: int, reps: int = 50) -> dict:
     return result
 
 
+def run_lm_head(dev, seed: int, reps: int = 20) -> dict:
+    """``pkv_lm_head_argmax`` (the LM head fused with greedy selection) at Qwen2.5-0.5B's tied
+    151936 x 896 fp16 embedding, beside the reference's path for the same tokens on the same GPU:
+    ``compute_logits(hidden).float()`` then ``argmax`` (engine/model.py:321-323, engine/sampler.py:27-31).
+
+    Two weight copies alternate (544 MB, above L2), so every call streams its weight from HBM.
+    Batches: 64 (config 2's decode batch) and 256 (``max_num_seqs``).
+    """
+    from mini_inference_b200 import ops
+
+    vocab, hidden, dtype = 151936, 896, torch.float16
+    g = torch.Generator(device=dev).manual_seed(seed + 29)
+    weights = [(torch.randn(vocab, hidden, generator=g, device=dev) * 0.02).to(dtype) for _ in range(2)]
+    peaks, kind = measured_peaks()
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def timed(fns) -> float:
+        """Device time per call: the calls recorded as one CUDA graph, replayed ``reps`` times."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                for fn in fns:
+                    fn()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(5):
+                for fn in fns:
+                    fn()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / (reps * 5 * len(fns)) * 1e3  # us
+
+    result = {}
+    for batch in (BATCH, 256):
+        h = torch.randn(batch, hidden, generator=g, device=dev).to(dtype)
+        ws = ops.lm_head_argmax_workspace(batch, dev)
+        out = torch.empty(batch, dtype=torch.int64, device=dev)
+        ref_out = torch.empty(batch, dtype=torch.int64, device=dev)
+        ours = [lambda w=w: ops.lm_head_argmax(h, w, ws, out=out, status=status, weight_ready=True) for w in weights]
+        ref = [lambda w=w: ref_out.copy_(torch.nn.functional.linear(h, w).float().argmax(dim=-1)) for w in weights]
+        us, us_ref = timed(ours), timed(ref)
+        ops.raise_device_errors(status)
+        same = int((out == ref_out).sum())
+        nbytes = vocab * hidden * 2 + batch * hidden * 2 + batch * 8
+        gbs = nbytes / (us * 1e-6) / 1e9
+        result[f"batch_{batch}"] = {
+            "us_per_call": round(us, 2), "bytes_per_call": nbytes, "gbs": round(gbs, 1),
+            "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "reference_torch_us": round(us_ref, 2),
+            "same_tokens_as_reference": f"{same}/{batch}"}
+    result["workload"] = ("pkv_lm_head_argmax at Qwen2.5-0.5B's tied 151936 x 896 fp16 embedding (tcgen05, "
+                          "weight streamed once, no logits written); the reference's compute_logits + float + "
+                          "argmax by torch (cuBLAS) timed beside it on the same GPU; CUDA-graph replays, two "
+                          "alternating weight copies above L2 (device time)")
+    result["kernel"] = "pkv lm_head_argmax_kernel<half,1> (batch 64), <half,2> (batch 256)"
+    result["peak_kind"] = f"{kind} copy bandwidth"
+    return result
+
+
 def bytes_per_layer_call(ctx: list[int]) -> int:
     """Algorithmic bytes of one fused append + decode attention call over the batch.
 
@@ -521,6 +589,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         line["prefill"] = run_prefill(dev, seed=rank)
         line["long_context"] = run_long_context(dev, seed=rank)
         line["qkv_post"] = run_qkv_post(dev, seed=rank)
+        line["lm_head"] = run_lm_head(dev, seed=rank)
     if world == 1 and not args.profile_case:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -705,6 +774,8 @@ def main() -> None:
                     help="only the tcgen05 prefill leg (config 4's prefill), for ncu captures")
     ap.add_argument("--long-only", action="store_true",
                     help="only config 5's attention kernel (7B bf16, contexts 8k..32k), for ncu captures")
+    ap.add_argument("--lm-head-only", action="store_true",
+                    help="only the greedy LM-head leg (0.5B embedding, batches 64 and 256), for ncu captures")
     ap.add_argument("--profile-case", action="store_true",
                     help="small case for ncu captures: 4 layer pools (536 MB, still above L2), no e2e / CPU legs")
     args = ap.parse_args()
@@ -713,10 +784,10 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.prefill_only or args.long_only:
+    if args.prefill_only or args.long_only or args.lm_head_only:
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         torch.cuda.set_device(dev)
-        run = run_prefill if args.prefill_only else run_long_context
+        run = run_prefill if args.prefill_only else run_long_context if args.long_only else run_lm_head
         print(json.dumps(run(dev, seed=0, reps=args.steps)), flush=True)
         return
     rank, world, local = dist_setup(args.gpus)

@@ -209,6 +209,35 @@ PKV_API int pkv_rope_append(const pkv_pool* pool, int32_t layer, const void* qkv
                     int64_t q_out_stride_h, void* k_out, int64_t k_out_stride_t, int64_t k_out_stride_h,
                     const int64_t* slot_mapping, int32_t* status_dev, pkv_stream_t stream);
 
+/* ------------------------------------------------------------------ greedy LM head */
+/*
+ * The LM head fused with greedy selection: for each of the batch's hidden rows,
+ *   token_ids[b] = argmax_v round(hidden[b] . weight[v])
+ * with the logit rounded to the model dtype (fp32 accumulation) and the smallest index
+ * among equal maxima (NaN counts as the largest), which is what the reference computes for
+ * an all-greedy batch: Qwen2ForCausalLM.compute_logits = F.linear(hidden, weight) in the
+ * model dtype, .float(), then Sampler's logits.argmax(dim=-1) (engine/model.py:321-323,
+ * engine/engine.py:97-123, engine/sampler.py:27-31) -- without writing the [B, vocab]
+ * logits. max_logits (NULL = not written) receives each row's largest rounded logit.
+ *
+ *   hidden : [batch, hidden_size] at hidden + b*hidden_stride (elements), 16-byte aligned
+ *   weight : [vocab, hidden_size] at weight + v*weight_stride (the tied embedding or lm_head)
+ *   dtype  : PKV_F16 or PKV_BF16 (both operands)
+ *   batch <= 256, hidden_size a multiple of 64, strides multiples of 8 elements
+ *   workspace : pkv_lm_head_argmax_workspace_bytes(batch) bytes, zeroed once before the
+ *           first call; every call leaves it zeroed (one workspace per stream)
+ *   flags  : PKV_LM_WEIGHT_READY or 0: the weight was not written by the kernel launched
+ *           just before on this stream, so its first stages may be read while that kernel
+ *           drains (programmatic dependent launch)
+ * Unsupported shapes return PKV_ERR_UNSUPPORTED; a timed-out device wait sets status.
+ */
+enum { PKV_LM_WEIGHT_READY = 1 };
+PKV_API int64_t pkv_lm_head_argmax_workspace_bytes(int32_t batch);
+PKV_API int pkv_lm_head_argmax(const void* hidden, int64_t hidden_stride, int32_t batch, const void* weight,
+                       int64_t weight_stride, int32_t vocab, int32_t hidden_size, int32_t dtype,
+                       int64_t* token_ids, float* max_logits, void* workspace, int64_t workspace_bytes,
+                       int32_t flags, int32_t* status_dev, pkv_stream_t stream);
+
 /* ------------------------------------------------------------------ metadata builder (GPU) */
 /*
  * Decode metadata from a device-resident table mirror, instead of host lists

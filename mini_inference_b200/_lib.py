@@ -28,6 +28,7 @@ PKV_F16 = 0
 PKV_BF16 = 1
 
 PKV_DECODE_INPUTS_READY = 1
+PKV_LM_WEIGHT_READY = 1
 PKV_DECODE_STATIC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 
@@ -56,6 +57,9 @@ SIGNATURES: dict[str, tuple] = {
     "pkv_rope_append": (c_int32, [P_POOL, c_int32, c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p,
                                   c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                                   c_void_p]),
+    "pkv_lm_head_argmax_workspace_bytes": (c_int64, [c_int32]),
+    "pkv_lm_head_argmax": (c_int32, [c_void_p, c_int64, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int32,
+                                     c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_void_p, c_void_p]),
     "pkv_decode_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64, c_int64,
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                        c_void_p, c_float, c_int32, c_void_p, c_int64, c_void_p, c_void_p]),

@@ -167,6 +167,17 @@ __device__ inline void tma_load_5d(void* smem_dst, const CUtensorMap* map, int c
       : "memory");
 }
 
+// 2-D bulk tensor copy global -> shared (no multicast) with an L2 cache policy; c0 is the
+// innermost coordinate (elements), c1 the row.
+__device__ inline void tma_load_2d(void* smem_dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar,
+                                   uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Bulk (non-tensor) copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
 // global -> shared, completing on an mbarrier (no multicast).
 __device__ inline void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
@@ -209,6 +220,12 @@ __device__ inline void st_relaxed_gpu(int32_t* ptr, int v) {
 
 __device__ inline void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ inline uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 __device__ inline uint64_t policy_evict_first() {
@@ -290,6 +307,11 @@ int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& poo
 // Cached K and V maps of a pool (one encode per pool and box shape).
 bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box = 1,
                    int chunks_per_box = 0);
+// 2-D tensor map over a row-major [rows, inner] matrix of 16-bit elements (row stride in
+// bytes, a multiple of 16) with a box of box_rows x box_inner (box_inner * 2 = 128 bytes
+// for the 128-byte swizzle). Rows past `rows` read as zeros.
+int make_matrix_tensor_map(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t rows,
+                           uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows);
 // Streaming multiprocessors of the current device (queried once).
 int num_sms();
 

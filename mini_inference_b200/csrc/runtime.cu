@@ -86,6 +86,27 @@ int make_pool_tensor_map(CUtensorMap* map, const void* base, const pkv_pool& poo
   return PKV_OK;
 }
 
+int make_matrix_tensor_map(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t rows,
+                           uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) {
+    g_last_cuda_error = "cuTensorMapEncodeTiled is not available from the driver";
+    return PKV_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == PKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    g_last_cuda_error = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r);
+    return PKV_ERR_CUDA;
+  }
+  return PKV_OK;
+}
+
 bool get_pool_maps(const pkv_pool& pool, CUtensorMap* tk, CUtensorMap* tv, int heads_per_box, int chunks_per_box) {
   std::lock_guard<std::mutex> lock(g_map_mutex);
   for (const MapEntry& e : g_maps) {

@@ -14,7 +14,7 @@ import math
 import torch
 
 from ._lib import (PKV_BF16, PKV_DECODE_INPUTS_READY, PKV_DECODE_STATIC_SCRATCH_BYTES, PKV_ERR_WORKSPACE, PKV_F16,
-                   PkvError, PkvPool, PkvTables, check, lib)
+                   PKV_LM_WEIGHT_READY, PkvError, PkvPool, PkvTables, check, lib)
 
 _DTYPES = {torch.float16: PKV_F16, torch.bfloat16: PKV_BF16}
 
@@ -232,6 +232,45 @@ def prefill_attention(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Ten
         starts.data_ptr(), max_new_tokens, hq, out.data_ptr(), out.stride(0), out.stride(1), q.data_ptr(),
         q.stride(0), q.stride(1), scale, _ptr(status), _stream()), "prefill_attention")
     return out
+
+
+def lm_head_argmax_workspace(max_batch: int, device: torch.device | str) -> torch.Tensor:
+    """A zeroed workspace for :func:`lm_head_argmax` of up to ``max_batch`` rows (each call leaves it zeroed)."""
+    nbytes = int(lib.pkv_lm_head_argmax_workspace_bytes(max_batch))
+    return torch.zeros((nbytes + 7) // 8, dtype=torch.int64, device=device)
+
+
+def lm_head_argmax(hidden: torch.Tensor, weight: torch.Tensor, workspace: torch.Tensor,
+                   out: torch.Tensor | None = None, max_logits: torch.Tensor | None = None,
+                   status: torch.Tensor | None = None, weight_ready: bool = False) -> torch.Tensor:
+    """Greedy tokens of ``hidden`` ``[B, H]`` under the LM head ``weight`` ``[V, H]``: int64 ``[B]`` on the device.
+
+    The reference's ``compute_logits(hidden).float().argmax(-1)`` (engine/model.py:321-323,
+    engine/sampler.py:27-31) in one kernel: logits rounded to the model dtype, the first index
+    among equal maxima, no logits written. ``max_logits`` (float32 ``[B]``, optional) receives
+    each row's largest rounded logit. ``weight_ready`` promises that the weight was not written
+    by the previous kernel in the stream (see PKV_LM_WEIGHT_READY in include/pkv.h).
+    """
+    _require_cuda(hidden, weight, workspace, out, max_logits)
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise ValueError("hidden must be [B, H] and weight [V, H]")
+    if hidden.dtype != weight.dtype:
+        raise ValueError("hidden and weight must have the same dtype")
+    if hidden.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("hidden and weight rows must be contiguous")
+    batch = hidden.shape[0]
+    if out is None:
+        out = torch.empty(batch, dtype=torch.int64, device=hidden.device)
+    if out.dtype != torch.int64 or out.numel() < batch:
+        raise ValueError("out must be int64 with one entry per row")
+    if max_logits is not None and (max_logits.dtype != torch.float32 or max_logits.numel() < batch):
+        raise ValueError("max_logits must be float32 with one entry per row")
+    check(lib.pkv_lm_head_argmax(
+        hidden.data_ptr(), hidden.stride(0), batch, weight.data_ptr(), weight.stride(0), weight.shape[0],
+        weight.shape[1], pkv_dtype(hidden.dtype), out.data_ptr(), _ptr(max_logits), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), PKV_LM_WEIGHT_READY if weight_ready else 0, _ptr(status),
+        _stream()), "lm_head_argmax")
+    return out[:batch]
 
 
 def build_decode_metadata(tables: PkvTables, lengths: torch.Tensor, block_size: int, scratch_block: int,

@@ -366,16 +366,54 @@ def make_rope_case(RotaryEmbedding, apply_rope, name: str, dtype, hq: int, hkv: 
     )
 
 
+def make_lm_head_case(engine_model, engine_sampler, name: str, dtype, vocab: int, hidden: int, batch: int,
+                      tie: bool, seed: int) -> None:
+    """``compute_logits`` + the greedy ``Sampler`` on seeded hidden rows, with an exact tie and a NaN row."""
+    torch.manual_seed(seed)
+    cfg = engine_model.Qwen2Config(vocab_size=vocab, hidden_size=hidden, intermediate_size=4 * hidden, num_layers=0,
+                                   num_heads=2, num_kv_heads=1, head_dim=hidden // 2, rms_norm_eps=1e-6,
+                                   rope_theta=1e6, max_position_embeddings=64, tie_word_embeddings=tie,
+                                   attention_bias=True)
+    model = engine_model.Qwen2ForCausalLM(cfg)
+    for _, prm in model.named_parameters():
+        prm.data.normal_(0, 0.02)
+    model = model.to(dtype)
+    weight = model.embed_tokens.weight if model.lm_head is None else model.lm_head.weight
+    g = torch.Generator().manual_seed(seed + 1)
+    h = torch.randn(batch, hidden, generator=g).to(dtype)
+    with torch.no_grad():
+        # row 1: vocab entries 3 and vocab - 2 get the same, dominant weight row (an exact tie);
+        # the reference returns the first.
+        weight[vocab - 2] = weight[3] = (h[1].float() * 0.05).to(dtype)
+        h[batch - 1, 5] = float("nan")  # a NaN row: every logit is NaN, argmax returns 0
+        logits = model.compute_logits(h).float()
+    params = [engine_sampler.SamplingParams() for _ in range(batch)]
+    tokens = engine_sampler.Sampler(0, "cpu")(logits, params)
+    np.savez_compressed(
+        HERE / f"lm_head_{name}.npz", dtype=np.array(str(dtype).replace("torch.", "")),
+        hidden=_np(h), weight=_np(weight.detach()), logits=logits.numpy(), tokens=np.array(tokens, np.int64),
+    )
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True, help="path of a Ham12-3/mini-inference checkout")
-    ap.add_argument("--only", choices=["rope"], help="write only these fixtures")
+    ap.add_argument("--only", choices=["rope", "lm_head"], help="write only these fixtures")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     from engine.kv_cache import PagedKVCache  # noqa: E402  (the reference's own class)
     from engine.model import RotaryEmbedding, apply_rope  # noqa: E402
 
     torch.set_num_threads(4)
+    if args.only == "lm_head":
+        import engine.model as engine_model  # noqa: E402
+        import engine.sampler as engine_sampler  # noqa: E402  (it imports SamplingParams)
+        # Qwen2.5-0.5B style (tied embedding, fp16) and 7B style (separate lm_head, bf16), small sizes;
+        # vocabularies that are not multiples of 64.
+        make_lm_head_case(engine_model, engine_sampler, "fp16_tied", torch.float16, 1000, 128, 7, True, seed=13)
+        make_lm_head_case(engine_model, engine_sampler, "bf16", torch.bfloat16, 777, 192, 5, False, seed=14)
+        print("lm_head fixtures written to", HERE)
+        return
     # Qwen2.5-0.5B (d 64, theta 1e6) and 7B (d 128) rotary shapes; tokens as rows [n, heads, d].
     make_rope_case(RotaryEmbedding, apply_rope, "fp16_h14_d64", torch.float16, 14, 2, 64, 37, 32768, 1e6, seed=11)
     make_rope_case(RotaryEmbedding, apply_rope, "bf16_h28_d128", torch.bfloat16, 28, 4, 128, 21, 33024, 1e6, seed=12)

@@ -22,7 +22,8 @@ def test_header_declares_the_entry_points():
     names = declared_functions()
     for required in ("pkv_kv_append", "pkv_decode_attention", "pkv_prefill_attention", "pkv_build_decode_metadata",
                      "pkv_build_prefill_metadata", "pkv_copy_blocks", "pkv_bm_allocate", "pkv_bm_free",
-                     "pkv_bm_register_prefix", "pkv_bm_ensure_capacity", "pkv_rope_append"):
+                     "pkv_bm_register_prefix", "pkv_bm_ensure_capacity", "pkv_rope_append",
+                     "pkv_lm_head_argmax", "pkv_lm_head_argmax_workspace_bytes"):
         assert required in names
     assert len(names) >= 30
 
@@ -72,3 +73,27 @@ def test_import_fails_loudly_without_the_library(tmp_path, monkeypatch):
     with pytest.raises(ImportError, match="not built"):
         spec.loader.exec_module(mod)
     sys.modules.pop("pkv_lib_without_so", None)
+
+
+def test_lm_head_argmax_validates_on_the_host():
+    from mini_inference_b200 import _lib
+
+    L = _lib.lib
+    assert L.pkv_lm_head_argmax_workspace_bytes(64) == 8 + 8 * 64
+    # Null pointers, then shapes the kernel does not take (checked before any CUDA call).
+    assert L.pkv_lm_head_argmax(None, 896, 4, None, 896, 1000, 896, _lib.PKV_F16, None, None, None, 0, 0, None,
+                                None) == _lib.PKV_ERR_INVALID_ARGUMENT
+    fake = ctypes.c_void_p(1 << 20)  # aligned, never dereferenced: validation returns first
+    args = dict(hidden_stride=896, batch=4, weight_stride=896, vocab=1000, hidden=896, dtype=_lib.PKV_F16, ws=4096)
+
+    def call(**kw):
+        a = {**args, **kw}
+        return L.pkv_lm_head_argmax(fake, a["hidden_stride"], a["batch"], fake, a["weight_stride"], a["vocab"],
+                                    a["hidden"], a["dtype"], fake, None, fake, a["ws"], 0, None, None)
+
+    assert call(hidden=96, hidden_stride=96, weight_stride=96) == _lib.PKV_ERR_UNSUPPORTED  # not a multiple of 64
+    assert call(batch=257, ws=1 << 16) == _lib.PKV_ERR_UNSUPPORTED
+    assert call(dtype=7) == _lib.PKV_ERR_UNSUPPORTED
+    assert call(hidden_stride=900) == _lib.PKV_ERR_INVALID_ARGUMENT  # rows not 16-byte aligned
+    assert call(ws=16) == _lib.PKV_ERR_WORKSPACE
+    assert call(batch=0) == _lib.PKV_OK
