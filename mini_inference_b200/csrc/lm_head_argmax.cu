@@ -9,17 +9,18 @@
 // It is HBM-bound on the weight (vocab x hidden 16-bit values, 272 MB for Qwen2.5-0.5B's
 // tied 151936 x 896 embedding), which is streamed exactly once. CTA g of the persistent
 // grid owns a contiguous range of 64-row vocab units and walks it in chunks of up to 256
-// rows (128 when the batch needs two 128-row M tiles):
+// rows:
 //   * one copy warp streams 64-wide K stages of the chunk's weight rows and of the hidden
 //     states (re-read from L2 per chunk; rows past the batch arrive as zeros) by TMA into
 //     a 4-stage ring; with PKV_LM_WEIGHT_READY the weight of the first stages is requested
 //     before the wait for the previous kernel (programmatic dependent launch), the hidden
 //     states always after it;
-//   * one thread issues tcgen05.mma kind::f16 (A = hidden rows, M = 128; B = weight rows,
-//     N = the chunk's rows; fp32 accumulators in TMEM, two chunk buffers of 256 columns);
+//   * one thread issues tcgen05.mma kind::f16 (A = hidden rows, M = 128 per tile; B = weight
+//     rows, N = the chunk's rows; fp32 accumulators in TMEM: two 256-column chunk buffers
+//     for one M tile, one 512-column buffer for two);
 //   * four epilogue warps own one batch row per TMEM lane: each rounds its row's logits
-//     to the model dtype and keeps the largest (first on ties) while the next chunk's MMAs
-//     run.
+//     to the model dtype and keeps the largest (first on ties), with one M tile while the
+//     next chunk's MMAs run.
 // The CTAs combine through a 64-bit atomic max per batch row on (ordered logit bits,
 // ~index); the last CTA to take the ticket writes the token ids and leaves the workspace
 // zeroed for the next call.
@@ -36,22 +37,27 @@ namespace {
 
 constexpr int kUnit = 64;     // vocab rows per unit (one TMA box of the weight)
 constexpr int kKB = 64;       // K elements per stage: one 128-byte swizzled row
-constexpr int kStages = 4;
+constexpr int kRingBytes = 192 * 1024;  // shared-memory ring of K stages
 constexpr int kThreads = 192;  // copy warp, MMA warp, 4 epilogue warps
 constexpr int kMaxBatch = 256;
 
+// MT 128-row M tiles of batch rows. Chunks are 256 vocab rows; their fp32 accumulators
+// (MT x 256 columns) fill the 512 TMEM columns twice over for one M tile, so the epilogue of
+// one chunk overlaps the MMAs of the next, and once for two (measured: faster than two
+// buffers of 128-row chunks, whose hidden rows, re-read per chunk, cost twice as much).
 template <int MT>
 struct LmShape {
-  static constexpr int CU = MT == 1 ? 4 : 2;          // units per chunk
-  static constexpr int NC = CU * kUnit;               // vocab rows per chunk (MMA N)
+  static constexpr int NCOLS = 512;
+  static constexpr int NC = 256;                      // vocab rows per chunk (MMA N)
+  static constexpr int CU = NC / kUnit;               // units per chunk
+  static constexpr int BUF_COLS = MT * NC;            // TMEM columns per chunk buffer
+  static constexpr int NBUF = NCOLS / BUF_COLS;       // 2 for one M tile, 1 for two
   static constexpr int A_BYTES = MT * 128 * 128;      // hidden: MT tiles of 128 rows x 64 K
   static constexpr int B_BYTES = NC * 128;            // weight: NC rows x 64 K
-  static constexpr int STAGE = A_BYTES + B_BYTES;     // 48 KB
-  static constexpr int BUF_COLS = MT * NC;            // 256 TMEM columns per chunk buffer
-  static constexpr int NCOLS = 2 * BUF_COLS;          // 512
-  static constexpr int NBARS = 2 * kStages + 5;
-  static constexpr int SMEM = 1024 + kStages * STAGE + NBARS * 8 + 16;
-  static_assert(BUF_COLS == 256, "two chunk buffers fill the 512 TMEM columns");
+  static constexpr int STAGE = A_BYTES + B_BYTES;     // 48 KB (one M tile) or 64 KB (two)
+  static constexpr int STAGES = kRingBytes / STAGE;   // 4 or 3
+  static constexpr int NBARS = 2 * STAGES + 2 * NBUF + 1;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + NBARS * 8 + 16;
 };
 
 struct LmParams {
@@ -93,14 +99,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     lm_head_argmax_kernel(const __grid_constant__ CUtensorMap tmap_h, const __grid_constant__ CUtensorMap tmap_w,
                           const LmParams p) {
   using S = LmShape<MT>;
+  constexpr int kStages = S::STAGES, NBUF = S::NBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * S::STAGE);
   uint64_t* full = bars;                  // [kStages] a stage's bytes landed
   uint64_t* empty = full + kStages;       // [kStages] the MMAs reading a stage completed
-  uint64_t* acc_full = empty + kStages;   // [2] a chunk's accumulators are final
-  uint64_t* acc_empty = acc_full + 2;     // [2] the epilogue warps read a chunk buffer
-  uint64_t* mma_done = acc_empty + 2;     // every MMA of the CTA completed (before TMEM is freed)
+  uint64_t* acc_full = empty + kStages;   // [NBUF] a chunk's accumulators are final
+  uint64_t* acc_empty = acc_full + NBUF;  // [NBUF] the epilogue warps read a chunk buffer
+  uint64_t* mma_done = acc_empty + NBUF;  // every MMA of the CTA completed (before TMEM is freed)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + S::NBARS);
   int* s_last = reinterpret_cast<int*>(tslot + 1);
   auto stage_a = [&](int s) { return smem + s * S::STAGE; };
@@ -121,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NBUF; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
     }
@@ -178,9 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int j = 0;
       for (int c = 0; c < n_chunks && ok; ++c) {
-        const int b = c % 2;
+        const int b = c % NBUF;
         const uint32_t idesc = umma_idesc_f16(kBf16, false, 128, chunk_units(c) * kUnit);
-        if (c >= 2 && !mbar_wait_until(&acc_empty[b], ((c / 2) - 1) & 1, deadline)) ok = false;
+        if (c >= NBUF && !mbar_wait_until(&acc_empty[b], ((c / NBUF) - 1) & 1, deadline)) ok = false;
         tc_fence_after_sync();
         const uint32_t d0 = tmem + (uint32_t)(b * S::BUF_COLS);
         for (int ks = 0; ks < kst && ok; ++ks, ++j) {
@@ -217,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int mt = 0; mt < MT; ++mt) bk[mt] = 0, bi[mt] = -1;
     bool ok = true;
     for (int c = 0; c < n_chunks; ++c) {
-      const int b = c % 2, cu = chunk_units(c);
-      if (ok && !mbar_wait_until(&acc_full[b], (c / 2) & 1, deadline)) ok = false;
+      const int b = c % NBUF, cu = chunk_units(c);
+      if (ok && !mbar_wait_until(&acc_full[b], (c / NBUF) & 1, deadline)) ok = false;
       tc_fence_after_sync();
       const int v0 = (u0 + c * S::CU) * kUnit;  // vocab index of the chunk's first row
 #pragma unroll
