@@ -348,6 +348,104 @@ def run_lm_head(dev, seed: int, reps: int = 20) -> dict:
     return result
 
 
+def run_scheduler(seed: int, steps: int = 400) -> dict:
+    """Host time of one scheduler step at config 3's request mix: 200 requests at t=0, prompts
+    round(exp(U(ln 16, ln 1024))) tokens, outputs U{16..512} (ignore_eos), max_num_seqs 256,
+    max_num_batched_tokens 4096, max_model_len 2048, blocks of 16 and a pool for every request.
+
+    A step is ``schedule()`` plus the step's ``append_token`` calls (the scheduler's share of
+    ``LLMEngine.step``, engine/engine.py:281-312), with the engine's cache commits in between.
+    The native scheduler (C++ over the C++ block manager, one call each) is timed beside the
+    reference's algorithm in Python over its allocator (``oracle/scheduler.py`` and
+    ``oracle/block_manager.py``, the reference's own code path restated: the reference does not
+    travel to the GPU box) on the same requests and tokens.
+    """
+    import random
+    from types import SimpleNamespace
+
+    from mini_inference_b200 import PagedKVCache
+    from mini_inference_b200.scheduler import Scheduler, SequenceStatus
+    from oracle.block_manager import OracleBlockManager
+    from oracle.scheduler import OracleSampling, OracleScheduler, OracleSequence
+
+    rng = random.Random(seed + 3)
+    reqs = [([rng.randrange(2, 151936) for _ in range(round(math.exp(rng.uniform(math.log(16), math.log(1024)))))],
+             rng.randint(16, 512)) for _ in range(200)]
+    max_seqs, budget, max_len, bs = 256, 4096, 2048, 16
+    blocks = sum(-(-(len(p) + m) // bs) for p, m in reqs)
+
+    class Seq:
+        __slots__ = ("seq_id", "prompt_token_ids", "sampling", "output_token_ids", "status", "slot", "finish_reason",
+                     "first_token_time", "finish_time", "num_preemptions", "num_cached_tokens")
+
+        def __init__(self, i, prompt, max_tokens):
+            self.seq_id, self.prompt_token_ids = i, prompt
+            self.sampling = OracleSampling(max_tokens, True)
+            self.output_token_ids, self.status, self.slot, self.finish_reason = [], SequenceStatus.WAITING, None, None
+            self.first_token_time = self.finish_time = None
+            self.num_preemptions = self.num_cached_tokens = 0
+
+        @property
+        def prompt_len(self):
+            return len(self.prompt_token_ids)
+
+        @property
+        def num_tokens(self):
+            return len(self.prompt_token_ids) + len(self.output_token_ids)
+
+        @property
+        def token_ids(self):
+            return self.prompt_token_ids + self.output_token_ids
+
+        @property
+        def is_finished(self):
+            return self.status is SequenceStatus.FINISHED
+
+    def run(native: bool) -> tuple[float, float]:
+        if native:
+            cache = PagedKVCache(1, 1, 4, blocks, bs, max_seqs, max_len, torch.float16, "cpu", True)
+            sched = Scheduler(SimpleNamespace(max_num_seqs=max_seqs, max_num_batched_tokens=budget,
+                                              max_model_len=max_len, scheduling="continuous"), cache)
+            seqs = [Seq(i, list(p), m) for i, (p, m) in enumerate(reqs)]
+        else:
+            cache = OracleBlockManager(blocks, bs, max_seqs, max_len, True)
+            sched = OracleScheduler(max_seqs, budget, max_len, cache)
+            seqs = [OracleSequence(i, list(p), OracleSampling(m, True)) for i, (p, m) in enumerate(reqs)]
+        for s in seqs:
+            sched.add(s)
+        total, n, running = 0.0, 0, 0
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            out = sched.schedule()
+            t1 = time.perf_counter()
+            for s in out.prefills:
+                cache.lengths[s.slot] = s.num_tokens
+            for s in out.decodes:
+                cache.lengths[s.slot] += 1
+            step = list(out.prefills) + list(out.decodes)
+            toks = [(s.seq_id * 7919 + s.num_tokens) % 151936 for s in step]
+            t2 = time.perf_counter()
+            if native:
+                sched.append_tokens(step, toks, t2)
+            else:
+                for s, tok in zip(step, toks):
+                    sched.append_token(s, tok, t2)
+            t3 = time.perf_counter()
+            total += (t1 - t0) + (t3 - t2)
+            n += 1
+            running += len(out.decodes)
+        return total / n * 1e6, running / n
+
+    native_us, running = run(True)
+    ref_us, _ = run(False)
+    return {"us_per_step": round(native_us, 1), "reference_us_per_step": round(ref_us, 1),
+            "mean_decodes_per_step": round(running, 1), "steps": steps,
+            "workload": "config 3's 200 requests at t=0 (prompts round(exp(U(ln16, ln1024))), outputs U{16..512}), "
+                        "max_num_seqs 256, budget 4096, blocks of 16; schedule() + the step's append_token calls, "
+                        "host time; reference = the reference's scheduler and allocator algorithm in Python "
+                        "(oracle/scheduler.py, oracle/block_manager.py)"}
+
+
 def bytes_per_layer_call(ctx: list[int]) -> int:
     """Algorithmic bytes of one fused append + decode attention call over the batch.
 
@@ -590,6 +688,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         line["long_context"] = run_long_context(dev, seed=rank)
         line["qkv_post"] = run_qkv_post(dev, seed=rank)
         line["lm_head"] = run_lm_head(dev, seed=rank)
+        line["scheduler"] = run_scheduler(seed=rank)
     if world == 1 and not args.profile_case:
         line["cpu_baseline"] = cpu_baseline(args)
     return line

@@ -39,7 +39,9 @@ enum pkv_status {
   PKV_ERR_DOUBLE_FREE = 6,        /* "slot freed twice" (engine/kv_cache.py:556) */
   PKV_ERR_UNKNOWN_SLOT = 7,       /* slot id that does not own a block table */
   PKV_ERR_UNSUPPORTED = 8,        /* head_dim / group size / dtype combination not built */
-  PKV_ERR_TIMEOUT = 9             /* a bounded device-side wait gave up */
+  PKV_ERR_TIMEOUT = 9,            /* a bounded device-side wait gave up */
+  PKV_ERR_EMPTY_PROMPT = 10,      /* "prompt is empty" (engine/scheduler.py:57-58) */
+  PKV_ERR_PROMPT_TOO_LONG = 11    /* prompt_len >= max_model_len (engine/scheduler.py:59-63) */
 };
 
 /* Human-readable name of a status code (static string). */
@@ -334,6 +336,54 @@ PKV_API int pkv_bm_set_journal(pkv_block_manager* bm, int32_t enable);
  */
 PKV_API int pkv_bm_drain_table_edits(pkv_block_manager* bm, int32_t* out, int32_t cap_triples, int32_t* out_len,
                              int32_t* overflow);
+
+/* ------------------------------------------------------------------ scheduler (host) */
+/*
+ * The reference's continuous-batching Scheduler (engine/scheduler.py:42-169) over a
+ * native block manager: the same admission, token-budget, preemption and finish
+ * decisions, one call per step. Requests are the caller's sequence ids; the scheduler
+ * keeps their tokens (prompt, then outputs) for the prefix lookup at (re)admission.
+ * The caller keeps the block manager alive longer than the scheduler; cache calls the
+ * engine makes itself (register_prefix, length commits) go to the block manager as before.
+ */
+typedef struct pkv_scheduler pkv_scheduler;
+enum pkv_seq_status { PKV_SEQ_WAITING = 0, PKV_SEQ_RUNNING = 1, PKV_SEQ_FINISHED = 2 };
+enum pkv_finish_reason {
+  PKV_FINISH_NONE = 0, PKV_FINISH_EOS = 1, PKV_FINISH_LENGTH = 2, PKV_FINISH_MAX_MODEL_LEN = 3, PKV_FINISH_ABORT = 4
+};
+/* One step's decisions; the caller provides the arrays, `capacity` entries each. */
+typedef struct pkv_sched_step {
+  int32_t capacity;
+  int64_t* prefill_ids;            /* admitted this step, in admission order */
+  int32_t* prefill_slots;
+  int64_t* prefill_cached_tokens;  /* lengths[slot] after allocate: prefix-cache hit tokens */
+  int64_t* decode_ids;             /* running before admission (oldest first): one token each */
+  int32_t* decode_slots;
+  int64_t* preempted_ids;          /* preempted while making room, in order (now waiting) */
+  int32_t n_prefills, n_decodes, n_preempted;
+} pkv_sched_step;
+
+/* static_batching: the reference's scheduling == "static" (nobody joins a running batch) */
+PKV_API int pkv_sched_create(pkv_block_manager* bm, int32_t max_num_seqs, int64_t max_num_batched_tokens,
+                     int64_t max_model_len, int32_t static_batching, const int64_t* eos_token_ids,
+                     int32_t n_eos, pkv_scheduler** out);
+PKV_API void pkv_sched_destroy(pkv_scheduler* s);
+/* Scheduler.add (engine/scheduler.py:55-64): PKV_ERR_EMPTY_PROMPT / PKV_ERR_PROMPT_TOO_LONG */
+PKV_API int pkv_sched_add(pkv_scheduler* s, int64_t seq_id, const int64_t* prompt_ids, int64_t n,
+                  int32_t max_tokens, int32_t ignore_eos);
+/* Scheduler.schedule (engine/scheduler.py:68-111); PKV_ERR_WORKSPACE if capacity is too small */
+PKV_API int pkv_sched_schedule(pkv_scheduler* s, pkv_sched_step* out);
+/* Scheduler.append_token for n (seq_id, token) pairs in order (engine/scheduler.py:143-159):
+ * finish_reasons[i] = PKV_FINISH_*; finished sequences leave running and free their slot. */
+PKV_API int pkv_sched_append_tokens(pkv_scheduler* s, const int64_t* seq_ids, const int64_t* tokens, int32_t n,
+                            int32_t* finish_reasons);
+/* Scheduler.abort (engine/scheduler.py:150-159): *where = PKV_SEQ_WAITING or PKV_SEQ_RUNNING
+ * (it was there and is now finished) or PKV_SEQ_FINISHED (already done: nothing happened). */
+PKV_API int pkv_sched_abort(pkv_scheduler* s, int64_t seq_id, int32_t* where);
+PKV_API int pkv_sched_counts(const pkv_scheduler* s, int32_t* n_waiting, int32_t* n_running,
+                     int64_t* num_preemptions);
+/* The queues' sequence ids: waiting front first, running oldest first (cap entries each). */
+PKV_API int pkv_sched_queues(const pkv_scheduler* s, int64_t* waiting, int64_t* running, int32_t cap);
 
 #ifdef __cplusplus
 }

@@ -23,6 +23,10 @@ PKV_ERR_DOUBLE_FREE = 6
 PKV_ERR_UNKNOWN_SLOT = 7
 PKV_ERR_UNSUPPORTED = 8
 PKV_ERR_TIMEOUT = 9
+PKV_ERR_EMPTY_PROMPT = 10
+PKV_ERR_PROMPT_TOO_LONG = 11
+
+PKV_SEQ_WAITING, PKV_SEQ_RUNNING, PKV_SEQ_FINISHED = 0, 1, 2
 
 PKV_F16 = 0
 PKV_BF16 = 1
@@ -40,6 +44,13 @@ class PkvPool(ctypes.Structure):
 class PkvTables(ctypes.Structure):
     _fields_ = [("block_tables", c_void_p), ("stride", c_int64), ("rows", c_int32), ("cols", c_int32),
                 ("seq_rows", c_void_p)]
+
+
+class PkvSchedStep(ctypes.Structure):
+    _fields_ = [("capacity", c_int32), ("prefill_ids", c_void_p), ("prefill_slots", c_void_p),
+                ("prefill_cached_tokens", c_void_p), ("decode_ids", c_void_p), ("decode_slots", c_void_p),
+                ("preempted_ids", c_void_p), ("n_prefills", c_int32), ("n_decodes", c_int32),
+                ("n_preempted", c_int32)]
 
 
 P_POOL = POINTER(PkvPool)
@@ -77,6 +88,15 @@ SIGNATURES: dict[str, tuple] = {
     "pkv_commit_decode": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p]),
     "pkv_update_tables": (c_int32, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p]),
     "pkv_copy_blocks": (c_int32, [P_POOL, c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
+    "pkv_sched_create": (c_int32, [c_void_p, c_int32, c_int64, c_int64, c_int32, c_void_p, c_int32,
+                                   POINTER(c_void_p)]),
+    "pkv_sched_destroy": (None, [c_void_p]),
+    "pkv_sched_add": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32]),
+    "pkv_sched_schedule": (c_int32, [c_void_p, POINTER(PkvSchedStep)]),
+    "pkv_sched_append_tokens": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p]),
+    "pkv_sched_abort": (c_int32, [c_void_p, c_int64, P_I32]),
+    "pkv_sched_counts": (c_int32, [c_void_p, P_I32, P_I32, P_I64]),
+    "pkv_sched_queues": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32]),
     "pkv_bm_create": (c_int32, [c_int32, c_int32, c_int32, c_int32, c_int32, POINTER(c_void_p)]),
     "pkv_bm_destroy": (None, [c_void_p]),
     "pkv_bm_can_allocate": (c_int32, [c_void_p, c_int64, P_I32]),

@@ -144,6 +144,8 @@ extern "C" const char* pkv_status_string(int status) {
     case PKV_ERR_UNKNOWN_SLOT: return "unknown slot";
     case PKV_ERR_UNSUPPORTED: return "unsupported shape or dtype";
     case PKV_ERR_TIMEOUT: return "device wait timed out";
+    case PKV_ERR_EMPTY_PROMPT: return "prompt is empty";
+    case PKV_ERR_PROMPT_TOO_LONG: return "prompt leaves no room to generate (prompt_len >= max_model_len)";
     default: return "unknown status";
   }
 }

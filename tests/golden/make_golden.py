@@ -27,6 +27,12 @@ Ham12-3/mini-inference (pure Python + PyTorch, run on the CPU) and records:
   (``engine/model.py:169-224``) on seeded q / k at scattered positions: the float32
   table rows, the rows cast to the model dtype, q, k and the rotated q, k.
 
+* ``lm_head_<name>.npz`` -- ``Qwen2ForCausalLM.compute_logits`` and the greedy ``Sampler``
+  (``engine/model.py:321-323``, ``engine/sampler.py:27-31``) on seeded hidden rows.
+* ``scheduler_traces.json`` -- the reference's ``Scheduler`` over its ``PagedKVCache``
+  (``engine/scheduler.py``) on seeded workloads from ``sched_driver.py``: every step's
+  prefills, decodes, finishes, queues, preemptions and cache counters.
+
 The reference does not travel with this repository, so the fixtures are
 committed and this script is only rerun by hand.
 """
@@ -395,16 +401,62 @@ def make_lm_head_case(engine_model, engine_sampler, name: str, dtype, vocab: int
     )
 
 
+# (name, seed, requests, steps, cache blocks, block size, max_seqs, token budget, max_model_len, static,
+#  prefix caching, max_tokens range, aborts)
+SCHED_CASES = [
+    ("continuous_prefix", 21, 40, 160, 40, 8, 8, 192, 160, False, True, (1, 80), 8),
+    ("continuous_tight", 22, 30, 280, 20, 4, 6, 96, 72, False, True, (1, 60), 8),  # preemptions, rejections
+    ("continuous_plain", 23, 30, 120, 64, 16, 16, 4096, 128, False, False, (1, 40), 6),
+    ("static", 24, 30, 220, 30, 8, 6, 64, 160, True, True, (1, 60), 8),
+]
+
+
+def make_scheduler_traces(Scheduler, Sequence, SamplingParams, PagedKVCache) -> None:
+    """The reference's Scheduler + PagedKVCache over seeded workloads (``sched_driver``)."""
+    from types import SimpleNamespace
+
+    from sched_driver import drive, make_workload
+
+    traces = []
+    for name, seed, n_req, steps, blocks, bs, max_seqs, budget, max_len, static, prefix, mt, n_ab in SCHED_CASES:
+        workload = make_workload(seed, n_req, steps, max_tokens=mt, n_aborts=n_ab)
+        config = SimpleNamespace(max_num_seqs=max_seqs, max_num_batched_tokens=budget, max_model_len=max_len,
+                                 scheduling="static" if static else "continuous")
+        cache = PagedKVCache(num_layers=1, num_kv_heads=1, head_dim=4, num_blocks=blocks, block_size=bs,
+                             max_seqs=max_seqs, max_len=max_len, dtype=torch.float32, device="cpu",
+                             enable_prefix_caching=prefix)
+        sched = Scheduler(config, cache, eos_token_ids=(0, 1))
+
+        def make_seq(i, prompt, max_tokens, ignore_eos):
+            return Sequence(seq_id=i, prompt_token_ids=prompt,
+                            sampling=SamplingParams(max_tokens=max_tokens, ignore_eos=ignore_eos), arrival_time=0.0)
+
+        records = drive(sched, make_seq, cache, workload, steps)
+        traces.append({"name": name, "config": {"num_blocks": blocks, "block_size": bs, "max_num_seqs": max_seqs,
+                                                "max_num_batched_tokens": budget, "max_model_len": max_len,
+                                                "static": static, "enable_prefix_caching": prefix,
+                                                "eos_token_ids": [0, 1], "steps": steps},
+                       "workload": workload, "records": records})
+    (HERE / "scheduler_traces.json").write_text(json.dumps(traces))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True, help="path of a Ham12-3/mini-inference checkout")
-    ap.add_argument("--only", choices=["rope", "lm_head"], help="write only these fixtures")
+    ap.add_argument("--only", choices=["rope", "lm_head", "scheduler"], help="write only these fixtures")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     from engine.kv_cache import PagedKVCache  # noqa: E402  (the reference's own class)
     from engine.model import RotaryEmbedding, apply_rope  # noqa: E402
 
     torch.set_num_threads(4)
+    if args.only == "scheduler":
+        sys.path.insert(0, str(HERE))
+        from engine.scheduler import Scheduler  # noqa: E402
+        from engine.sequence import SamplingParams, Sequence  # noqa: E402
+        make_scheduler_traces(Scheduler, Sequence, SamplingParams, PagedKVCache)
+        print("scheduler traces written to", HERE)
+        return
     if args.only == "lm_head":
         import engine.model as engine_model  # noqa: E402
         import engine.sampler as engine_sampler  # noqa: E402  (it imports SamplingParams)
