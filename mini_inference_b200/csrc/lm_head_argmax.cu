@@ -12,7 +12,8 @@
 // rows:
 //   * one copy warp streams 64-wide K stages of the chunk's weight rows and of the hidden
 //     states (re-read from L2 per chunk; rows past the batch arrive as zeros) by TMA into
-//     a 4-stage ring; with PKV_LM_WEIGHT_READY the weight of the first stages is requested
+//     two rings, 4-5 stages of weight rows and 3 of hidden rows; with PKV_LM_WEIGHT_READY
+//     the weight of the first stages is requested
 //     before the wait for the previous kernel (programmatic dependent launch), the hidden
 //     states always after it;
 //   * one thread issues tcgen05.mma kind::f16 (A = hidden rows, M = 128 per tile; B = weight
@@ -37,7 +38,6 @@ namespace {
 
 constexpr int kUnit = 64;     // vocab rows per unit (one TMA box of the weight)
 constexpr int kKB = 64;       // K elements per stage: one 128-byte swizzled row
-constexpr int kRingBytes = 192 * 1024;  // shared-memory ring of K stages
 constexpr int kThreads = 192;  // copy warp, MMA warp, 4 epilogue warps
 constexpr int kMaxBatch = 256;
 
@@ -45,6 +45,8 @@ constexpr int kMaxBatch = 256;
 // (MT x 256 columns) fill the 512 TMEM columns twice over for one M tile, so the epilogue of
 // one chunk overlaps the MMAs of the next, and once for two (measured: faster than two
 // buffers of 128-row chunks, whose hidden rows, re-read per chunk, cost twice as much).
+// The weight and the hidden rows of a K stage travel in separate rings: the weight comes
+// from HBM and needs the deeper one (WS stages in flight), the hidden rows hit L2.
 template <int MT>
 struct LmShape {
   static constexpr int NCOLS = 512;
@@ -54,10 +56,11 @@ struct LmShape {
   static constexpr int NBUF = NCOLS / BUF_COLS;       // 2 for one M tile, 1 for two
   static constexpr int A_BYTES = MT * 128 * 128;      // hidden: MT tiles of 128 rows x 64 K
   static constexpr int B_BYTES = NC * 128;            // weight: NC rows x 64 K
-  static constexpr int STAGE = A_BYTES + B_BYTES;     // 48 KB (one M tile) or 64 KB (two)
-  static constexpr int STAGES = kRingBytes / STAGE;   // 4 or 3
-  static constexpr int NBARS = 2 * STAGES + 2 * NBUF + 1;
-  static constexpr int SMEM = 1024 + STAGES * STAGE + NBARS * 8 + 16;
+  static constexpr int WS = MT == 1 ? 5 : 4;          // weight stages (32 KB each)
+  static constexpr int HS = 3;                        // hidden stages
+  static constexpr int NBARS = 2 * WS + HS + 2 * NBUF + 1;
+  static constexpr int SMEM = 1024 + WS * B_BYTES + HS * A_BYTES + NBARS * 8 + 16;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 struct LmParams {
@@ -99,19 +102,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     lm_head_argmax_kernel(const __grid_constant__ CUtensorMap tmap_h, const __grid_constant__ CUtensorMap tmap_w,
                           const LmParams p) {
   using S = LmShape<MT>;
-  constexpr int kStages = S::STAGES, NBUF = S::NBUF;
+  constexpr int WS = S::WS, HS = S::HS, NBUF = S::NBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * S::STAGE);
-  uint64_t* full = bars;                  // [kStages] a stage's bytes landed
-  uint64_t* empty = full + kStages;       // [kStages] the MMAs reading a stage completed
-  uint64_t* acc_full = empty + kStages;   // [NBUF] a chunk's accumulators are final
+  uint8_t* ring_w = smem;                          // [WS][B_BYTES]
+  uint8_t* ring_h = smem + WS * S::B_BYTES;        // [HS][A_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring_h + HS * S::A_BYTES);
+  uint64_t* w_full = bars;                // [WS] a stage's weight rows landed
+  uint64_t* h_full = w_full + WS;         // [HS] a stage's hidden rows landed
+  uint64_t* done = h_full + HS;           // [WS] the MMAs of stage j completed (frees both of its slots)
+  uint64_t* acc_full = done + WS;         // [NBUF] a chunk's accumulators are final
   uint64_t* acc_empty = acc_full + NBUF;  // [NBUF] the epilogue warps read a chunk buffer
   uint64_t* mma_done = acc_empty + NBUF;  // every MMA of the CTA completed (before TMEM is freed)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + S::NBARS);
   int* s_last = reinterpret_cast<int*>(tslot + 1);
-  auto stage_a = [&](int s) { return smem + s * S::STAGE; };
-  auto stage_b = [&](int s) { return smem + s * S::STAGE + S::A_BYTES; };
+  auto stage_a = [&](int j) { return ring_h + (j % HS) * S::A_BYTES; };
+  auto stage_b = [&](int j) { return ring_w + (j % WS) * S::B_BYTES; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, g = blockIdx.x;
@@ -124,10 +130,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto chunk_units = [&](int c) { return min(S::CU, nu - c * S::CU); };
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+    for (int i = 0; i < WS; ++i) {
+      mbar_init(&w_full[i], 1);
+      mbar_init(&done[i], 1);
     }
+    for (int i = 0; i < HS; ++i) mbar_init(&h_full[i], 1);
     for (int i = 0; i < NBUF; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
@@ -151,31 +158,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tmap_w);
     }
     const uint64_t stream_once = policy_evict_first(), reused = policy_evict_last();
-    auto issue_w = [&](int j) {  // expect the whole stage, request its weight rows
-      const int c = j / kst, ks = j % kst, s = j % kStages, cu = chunk_units(c);
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], S::A_BYTES + cu * kUnit * 128);
+    auto issue_w = [&](int j) {  // stage j's weight rows into slot j % WS
+      const int c = j / kst, ks = j % kst, cu = chunk_units(c);
+      uint64_t* bar = &w_full[j % WS];
+      if (lane == 0) mbar_arrive_expect_tx(bar, cu * kUnit * 128);
       __syncwarp();
       if (lane < cu)
-        tma_load_2d(stage_b(s) + lane * kUnit * 128, &tmap_w, ks * kKB, (u0 + c * S::CU + lane) * kUnit, &full[s],
+        tma_load_2d(stage_b(j) + lane * kUnit * 128, &tmap_w, ks * kKB, (u0 + c * S::CU + lane) * kUnit, bar,
                     stream_once);
     };
-    auto issue_h = [&](int j) {
-      const int ks = j % kst, s = j % kStages;
-      if (lane < MT) tma_load_2d(stage_a(s) + lane * 128 * 128, &tmap_h, ks * kKB, lane * 128, &full[s], reused);
+    auto issue_h = [&](int j) {  // stage j's hidden rows into slot j % HS
+      const int ks = j % kst;
+      uint64_t* bar = &h_full[j % HS];
+      if (lane == 0) mbar_arrive_expect_tx(bar, S::A_BYTES);
+      __syncwarp();
+      if (lane < MT) tma_load_2d(stage_a(j) + lane * 128 * 128, &tmap_h, ks * kKB, lane * 128, bar, reused);
     };
-    const int pre = p.weight_ready ? min(total, kStages) : 0;
-    for (int j = 0; j < pre; ++j) issue_w(j);
+    // The first WS weight stages (before the wait for the previous kernel when the weight is
+    // known ready) and HS hidden stages; then, as the MMAs of stage c complete, the slots of
+    // stage c take stage c + HS's hidden rows and stage c + WS's weight rows.
+    const int pw = min(total, WS), ph = min(total, HS);
+    if (p.weight_ready)
+      for (int j = 0; j < pw; ++j) issue_w(j);
     grid_dep_wait();  // the hidden states are the previous kernel's output
+    if (!p.weight_ready)
+      for (int j = 0; j < pw; ++j) issue_w(j);
+    for (int j = 0; j < ph; ++j) issue_h(j);
     bool ok = true;
-    for (int j = 0; j < total && ok; ++j) {
-      if (j >= pre) {
-        if (lane == 0 && j >= kStages && !mbar_wait_until(&empty[j % kStages], ((j / kStages) - 1) & 1, deadline))
-          ok = false;
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        issue_w(j);
-      }
-      issue_h(j);
+    for (int c = 0; c + HS < total && ok; ++c) {
+      if (lane == 0 && !mbar_wait_until(&done[c % WS], (c / WS) & 1, deadline)) ok = false;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      issue_h(c + HS);
+      if (c + WS < total) issue_w(c + WS);
     }
     if (!ok && lane == 0) report(p.status, PKV_ERR_TIMEOUT);
   } else if (warp == 1) {
@@ -191,22 +206,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after_sync();
         const uint32_t d0 = tmem + (uint32_t)(b * S::BUF_COLS);
         for (int ks = 0; ks < kst && ok; ++ks, ++j) {
-          const int s = j % kStages;
-          if (!mbar_wait_until(&full[s], (j / kStages) & 1, deadline)) {
+          if (!mbar_wait_until(&w_full[j % WS], (j / WS) & 1, deadline) ||
+              !mbar_wait_until(&h_full[j % HS], (j / HS) & 1, deadline)) {
             ok = false;
             break;
           }
           tc_fence_after_sync();
 #pragma unroll
           for (int kk = 0; kk < kKB / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(smem_u32(stage_b(s) + kk * 32), 16, 1024);
+            const uint64_t bd = umma_desc_sw128(smem_u32(stage_b(j) + kk * 32), 16, 1024);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
-              const uint64_t ad = umma_desc_sw128(smem_u32(stage_a(s) + mt * 128 * 128 + kk * 32), 16, 1024);
+              const uint64_t ad = umma_desc_sw128(smem_u32(stage_a(j) + mt * 128 * 128 + kk * 32), 16, 1024);
               umma_f16_ss(d0 + mt * S::NC, ad, bd, idesc, ks > 0 || kk > 0);
             }
           }
-          umma_commit(&empty[s]);
+          umma_commit(&done[j % WS]);
         }
         if (ok) umma_commit(&acc_full[b]);
       }
