@@ -701,34 +701,60 @@ def run_e2e(args, dev, pool, tables, ctx, q_dev, kn_dev, vn_dev, world):
     CUDA graph, recorded once and replayed per step: the table, slot and length copies,
     then the layers' q / k_new / v_new in chunks of 1, 2, 4, 8, ... layers on a copy
     stream (each layer's call waits only for its chunk, so later chunks land while earlier
-    layers compute), the 24 ``pkv_decode_attention`` calls, and the outputs back in chunks
-    that shrink towards the last layer on a second copy stream, so only one layer's output
-    is copied after the last kernel. Every step copies all its inputs in and all its
-    outputs out inside the timed region and ends with the host waiting for its result.
-    (Measured on B200: 0.38 ms per step this way, 0.49 ms with one copy per layer and
-    tensor, 1.6 ms issuing the same calls eagerly from Python.)
+    layers compute; the step's inputs sit in one staging buffer, so a chunk is one copy), the
+    24 ``pkv_decode_attention`` calls, and the outputs back in chunks that shrink towards the
+    last layer on a second copy stream, so only one layer's output is copied after the last
+    kernel. Every step copies all its inputs in and all its outputs out inside the timed
+    region and ends with the host waiting for its result. (Measured on B200: 0.38 ms per step
+    with one copy per chunk and tensor, 0.49 ms with one copy per layer and tensor, 1.6 ms
+    issuing the same calls eagerly from Python.)
     """
     from mini_inference_b200 import ops
 
     LAYERS = args.layers
     cols = max(len(t) for t in tables)
-    tab_h = torch.full((BATCH, cols), 0, dtype=torch.int32)
+    # One pinned staging buffer per step, as an engine keeps one: the metadata (tables,
+    # slots, lengths) and then each layer's q | k_new | v_new back to back, so that a chunk of
+    # layers is one contiguous copy (a host-device copy costs ~8-10 us on its own here,
+    # measured, whatever its size up to ~150 KB), mirrored by one device buffer.
+    def up(n: int) -> int:
+        return (n + 255) // 256 * 256
+
+    tab_b, sm_b, cl_b = BATCH * cols * 4, BATCH * 8, BATCH * 4
+    q_b, kv_b = BATCH * HQ * D * ELT, BATCH * HKV * D * ELT
+    meta = up(tab_b) + up(sm_b) + up(cl_b)
+    layer_b = up(q_b + 2 * kv_b)
+    buf_h = torch.zeros(meta + LAYERS * layer_b, dtype=torch.uint8).pin_memory()
+    buf_d = torch.zeros_like(buf_h, device=dev)
+
+    def views(buf):
+        tab = buf[:tab_b].view(torch.int32).view(BATCH, cols)
+        sm = buf[up(tab_b):up(tab_b) + sm_b].view(torch.int64)
+        cl = buf[up(tab_b) + up(sm_b):up(tab_b) + up(sm_b) + cl_b].view(torch.int32)
+        per = []
+        for layer in range(LAYERS):
+            o = meta + layer * layer_b
+            per.append((buf[o:o + q_b].view(torch.float16).view(BATCH, HQ, D),
+                        buf[o + q_b:o + q_b + kv_b].view(torch.float16).view(BATCH, HKV, D),
+                        buf[o + q_b + kv_b:o + q_b + 2 * kv_b].view(torch.float16).view(BATCH, HKV, D)))
+        return tab, sm, cl, per
+
+    tab_h, sm_h, cl_h, per_h = views(buf_h)
     for i, t in enumerate(tables):
         tab_h[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
-    sm_h = torch.tensor([t[c // BS] * BS + c % BS for t, c in zip(tables, ctx)], dtype=torch.int64)
-    cl_h = torch.tensor([c + 1 for c in ctx], dtype=torch.int32)
-    q_h = q_dev.cpu().pin_memory()
-    kn_h, vn_h = kn_dev.cpu().pin_memory(), vn_dev.cpu().pin_memory()
-    tab_h, sm_h, cl_h = tab_h.pin_memory(), sm_h.pin_memory(), cl_h.pin_memory()
+    sm_h.copy_(torch.tensor([t[c // BS] * BS + c % BS for t, c in zip(tables, ctx)], dtype=torch.int64))
+    cl_h.copy_(torch.tensor([c + 1 for c in ctx], dtype=torch.int32))
+    for layer, (qh, kh, vh) in enumerate(per_h):
+        qh.copy_(q_dev[layer].cpu())
+        kh.copy_(kn_dev[layer].cpu())
+        vh.copy_(vn_dev[layer].cpu())
+    tab_d, sm_d, cl_d, per_d = views(buf_d)
     out_h = torch.empty(LAYERS, BATCH, HQ, D, dtype=torch.float16).pin_memory()
-    q_d, kn_d, vn_d = torch.empty_like(q_dev), torch.empty_like(kn_dev), torch.empty_like(vn_dev)
     out_d = torch.empty(LAYERS, BATCH, HQ, D, dtype=torch.float16, device=dev)
-    tab_d = torch.empty_like(tab_h, device=dev)
-    sm_d, cl_d = torch.empty_like(sm_h, device=dev), torch.empty_like(cl_h, device=dev)
     ws = torch.zeros(ops.decode_workspace_bytes(BATCH, HKV, cols, BS, D, HQ), dtype=torch.uint8, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     tabs = ops.make_tables(tab_d)
-    h2d = sum(t.numel() * t.element_size() for t in (q_h, kn_h, vn_h, tab_h, sm_h, cl_h))
+    h2d = buf_h.numel()
     d2h = out_h.numel() * out_h.element_size()
     h2d_stream, d2h_stream = torch.cuda.Stream(), torch.cuda.Stream()
 
@@ -746,17 +772,16 @@ def run_e2e(args, dev, pool, tables, ctx, q_dev, kn_dev, vn_dev, world):
         d2h_stream.wait_stream(main)
         landed = {}
         with torch.cuda.stream(h2d_stream):
-            for src, dst in ((tab_h, tab_d), (sm_h, sm_d), (cl_h, cl_d)):
-                dst.copy_(src, non_blocking=True)
-            for a, b in h2d_chunks:
-                for src, dst in ((q_h, q_d), (kn_h, kn_d), (vn_h, vn_d)):
-                    dst[a:b].copy_(src[a:b], non_blocking=True)
+            for a, b in h2d_chunks:  # one copy per chunk; the first one carries the metadata too
+                lo, hi = (0 if a == 0 else meta + a * layer_b), meta + b * layer_b
+                buf_d[lo:hi].copy_(buf_h[lo:hi], non_blocking=True)
                 landed[a] = torch.cuda.Event()
                 landed[a].record(h2d_stream)
         for layer in range(LAYERS):  # after the first layer the copied tables and lengths are complete
             if layer in landed:
                 main.wait_event(landed[layer])
-            ops.decode_attention(pool, layer, tabs, q_d[layer], cl_d, ws, k_new=kn_d[layer], v_new=vn_d[layer],
+            q_l, kn_l, vn_l = per_d[layer]
+            ops.decode_attention(pool, layer, tabs, q_l, cl_d, ws, k_new=kn_l, v_new=vn_l,
                                  slot_mapping=sm_d, out=out_d[layer], status=status, inputs_ready=layer > 0)
             if layer in d2h_after:
                 a, b = d2h_after[layer]
