@@ -29,7 +29,6 @@ import torch
 pytestmark = pytest.mark.gpu
 
 L, HQ, HKV, D, H, VOCAB, BS = 2, 14, 2, 64, 128, 97, 16
-W_QKV = (HQ + 2 * HKV) * D
 THETA, MAX_POS = 1e6, 512
 
 
@@ -83,34 +82,44 @@ class Seq:
         return self.status is SequenceStatus.FINISHED
 
 
-class Model:
-    """Random fp16 weights; the GPU forward uses the package's contexts."""
+SHAPES = {  # attention heads of the two model families, in their dtypes
+    "0.5b_fp16": (HQ, HKV, D, torch.float16),  # Qwen2.5-0.5B: 14 / 2 heads of 64
+    "7b_bf16": (28, 4, 128, torch.bfloat16),   # Qwen2.5-7B: 28 / 4 heads of 128
+}
 
-    def __init__(self, dev, seed=0):
+
+class Model:
+    """Random weights in the model dtype; the GPU forward uses the package's contexts."""
+
+    def __init__(self, dev, seed=0, shape=SHAPES["0.5b_fp16"]):
+        self.hq, self.hkv, self.d, self.dtype = shape
         g = torch.Generator(device="cpu").manual_seed(seed)
+        wqkv = (self.hq + 2 * self.hkv) * self.d
 
         def w(*shape, std):
-            return (torch.randn(*shape, generator=g) * std).half().to(dev)
+            return (torch.randn(*shape, generator=g) * std).to(self.dtype).to(dev)
 
         self.embed = w(VOCAB, H, std=1.0)
-        self.layers = [(w(H, W_QKV, std=0.08), w(W_QKV, std=0.1), w(HQ * D, H, std=0.03)) for _ in range(L)]
+        self.layers = [(w(H, wqkv, std=0.08), w(wqkv, std=0.1), w(self.hq * self.d, H, std=0.03 * (64 / self.d) ** 0.5))
+                       for _ in range(L)]
         self.lm = w(VOCAB, H, std=0.5)
         from mini_inference_b200 import ops
-        self.cos, self.sin = ops.rope_tables(D, MAX_POS, THETA, torch.float16, dev)
+        self.cos, self.sin = ops.rope_tables(self.d, MAX_POS, THETA, self.dtype, dev)
 
     def forward(self, ids, ctx):  # ids [B, T] -> hidden [B, T, H]
         b, t = ids.shape
         x = self.embed[ids]
         for layer, (wqkv, bqkv, wo) in enumerate(self.layers):
             qkv = x @ wqkv + bqkv
-            o = ctx.attend_qkv(layer, qkv, self.cos, self.sin, HQ)  # [B, Hq, T, d]
-            x = x + o.transpose(1, 2).reshape(b, t, HQ * D) @ wo
+            o = ctx.attend_qkv(layer, qkv, self.cos, self.sin, self.hq)  # [B, Hq, T, d]
+            x = x + o.transpose(1, 2).reshape(b, t, self.hq * self.d) @ wo
         return x
 
 
 def oracle_logits(model, tokens):
     """Dense float64 forward over one sequence: logits [len(tokens), vocab] (row p predicts token p + 1)."""
     f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    HQ, HKV, D = model.hq, model.hkv, model.d  # noqa: N806
     cos, sin = f(model.cos), f(model.sin)
     pos = np.arange(len(tokens))
     x = f(model.embed)[tokens]
@@ -145,8 +154,8 @@ def run_engine(dev, model, requests, num_blocks, max_seqs, budget, max_len):
     from mini_inference_b200.sampler import GreedyLMHead
     from mini_inference_b200.scheduler import Scheduler, SequenceStatus
 
-    cache = PagedKVCache(L, HKV, D, num_blocks=num_blocks, block_size=BS, max_seqs=max_seqs, max_len=max_len,
-                         dtype=torch.float16, device=dev, enable_prefix_caching=True)
+    cache = PagedKVCache(L, model.hkv, model.d, num_blocks=num_blocks, block_size=BS, max_seqs=max_seqs,
+                         max_len=max_len, dtype=model.dtype, device=dev, enable_prefix_caching=True)
     sched = Scheduler(SimpleNamespace(max_num_seqs=max_seqs, max_num_batched_tokens=budget, max_model_len=max_len,
                                       scheduling="continuous"), cache)
     head = GreedyLMHead(model.lm, max_batch=max_seqs)
@@ -179,14 +188,15 @@ def run_engine(dev, model, requests, num_blocks, max_seqs, budget, max_len):
     return seqs, sched.num_preemptions, cache.prefix_hit_tokens
 
 
-def test_engine_loop_tokens_match_the_dense_oracle(dev):
+@pytest.mark.parametrize("shape", list(SHAPES))
+def test_engine_loop_tokens_match_the_dense_oracle(dev, shape):
     rng = random.Random(5)
     prefixes = [[rng.randrange(VOCAB) for _ in range(n)] for n in (40, 23)]
     requests = []
     for i in range(14):
         prompt = (list(rng.choice(prefixes)) if i % 3 else []) + [rng.randrange(VOCAB) for _ in range(rng.randint(1, 30))]
         requests.append((prompt, rng.randint(4, 40)))
-    model = Model(dev)
+    model = Model(dev, shape=SHAPES[shape])
     # 12 blocks of 16 for up to 6 running sequences of up to 110 tokens: preemptions happen.
     seqs, preemptions, hits = run_engine(dev, model, requests, num_blocks=12, max_seqs=6, budget=512, max_len=160)
     assert preemptions > 0 and hits > 0
