@@ -48,5 +48,9 @@ class GreedyLMHead:
         if params is not None and not all(p.greedy for p in params):
             raise ValueError("sampled requests need the logits: use compute_logits and the reference Sampler")
         ids = self(hidden).tolist()
-        ops.raise_device_errors(self.status)
+        try:
+            ops.raise_device_errors(self.status)
+        except RuntimeError:
+            self.workspace.zero_()  # a call that gave up may have left maxima or its ticket behind
+            raise
         return ids
