@@ -24,7 +24,9 @@ class GreedyLMHead:
 
     ``weight`` is the LM head (the embedding matrix when the embeddings are tied,
     ``engine/model.py:300-323``). One instance per stream: the workspace is reused by
-    every call and left zeroed by each.
+    every call and left zeroed by each. Calls pass ``PKV_LM_WEIGHT_READY``: the weight (a
+    model parameter) must not be written by the kernel launched just before a call on the
+    same stream.
     """
 
     def __init__(self, weight: torch.Tensor, max_batch: int = 256) -> None:
