@@ -898,6 +898,8 @@ def main() -> None:
                     help="only the tcgen05 prefill leg (config 4's prefill), for ncu captures")
     ap.add_argument("--long-only", action="store_true",
                     help="only config 5's attention kernel (7B bf16, contexts 8k..32k), for ncu captures")
+    ap.add_argument("--qkv-only", action="store_true",
+                    help="only the qkv-post leg (RoPE fused with the KV append), for ncu captures")
     ap.add_argument("--lm-head-only", action="store_true",
                     help="only the greedy LM-head leg (0.5B embedding, batches 64 and 256), for ncu captures")
     ap.add_argument("--profile-case", action="store_true",
@@ -908,10 +910,11 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.prefill_only or args.long_only or args.lm_head_only:
+    if args.prefill_only or args.long_only or args.lm_head_only or args.qkv_only:
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         torch.cuda.set_device(dev)
-        run = run_prefill if args.prefill_only else run_long_context if args.long_only else run_lm_head
+        run = (run_prefill if args.prefill_only else run_long_context if args.long_only
+               else run_lm_head if args.lm_head_only else run_qkv_post)
         print(json.dumps(run(dev, seed=0, reps=args.steps)), flush=True)
         return
     rank, world, local = dist_setup(args.gpus)
