@@ -4,7 +4,7 @@
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N --steps K --warmup W
 
-Workload (the configuration the "paged-attn KV GB/s" half of
+Workload (configuration 2 of the task, the one the "paged-attn KV GB/s" half of
 the metric is quoted on): 64 sequences with context lengths uniform in
 128..2048, 14 query / 2 KV heads, head_dim 64, blocks of 16 tokens, fp16,
 K/V/Q ~ N(0, 1), block tables = consecutive slices of a seeded permutation of a
@@ -459,6 +459,17 @@ def bytes_per_layer_call(ctx: list[int]) -> int:
     return kv + qo + append + table
 
 
+def decode_config(world: int, layers: int) -> dict:
+    """The ``config`` of the config-2 line, the same in both arms."""
+    ctx, _ = workload(seed=0)
+    return {"workload": "config 2: paged decode attention micro-benchmark, fused one-token append",
+            "batch_per_gpu": BATCH, "context": f"U{{{CTX_LO}..{CTX_HI}}}", "q_heads": HQ, "kv_heads": HKV,
+            "head_dim": D, "block_size": BS, "pool_blocks": NUM_BLOCKS, "layers_per_step": layers,
+            "bytes_per_step_per_gpu": bytes_per_layer_call(ctx) * layers, "tokens_per_step_per_gpu": BATCH,
+            "l2": f"inputs above L2: {layers} layer pools of 134 MB, each read once per step",
+            "parallelism": f"replicas x{world} (requests sharded by rank, no collective)"}
+
+
 def measured_peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -529,12 +540,11 @@ def dist_setup(n_gpus: int):
 
         import torch.distributed as dist
 
-        timeout = datetime.timedelta(seconds=120)
+        # The replicas share nothing on the data path; the process group only carries the
+        # barriers around the timed regions and the max of the ranks' times, on the host (gloo).
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-            dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", local))
-        else:
-            dist.init_process_group("gloo", timeout=timeout)
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     return rank, world, local
 
 
@@ -544,8 +554,7 @@ def max_over_ranks(value: float, world: int) -> float:
         return value
     import torch.distributed as dist
 
-    dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
-    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    t = torch.tensor([value], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -649,6 +658,13 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     ms_job = max_over_ranks(ms_total, world)
     ms_attn_job = max_over_ranks(ms_attn, world)
     ms_e2e_job = max_over_ranks(ms_e2e, world)
+    del g_step, g_attn, k_pool, v_pool
+    serving = None
+    if not args.profile_case and not args.no_serving:  # every rank serves its share of config 3
+        with ClockSampler(local) as serve_clocks:
+            serving = run_serving(args, rank, world, local)
+        if serving is not None:
+            serving["clocks"] = serve_clocks.summary()
     if rank != 0:
         return None
     peaks, peak_kind = measured_peaks()
@@ -660,12 +676,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_job / args.steps, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded; config 2 shapes and distributions)",
-        "config": {"workload": "config 2: paged decode attention micro-benchmark, fused one-token append",
-                   "batch_per_gpu": BATCH, "context": f"U{{{CTX_LO}..{CTX_HI}}}", "q_heads": HQ, "kv_heads": HKV,
-                   "head_dim": D, "block_size": BS, "pool_blocks": NUM_BLOCKS, "layers_per_step": LAYERS,
-                   "bytes_per_step_per_gpu": step_bytes, "tokens_per_step_per_gpu": BATCH,
-                   "l2": "inputs above L2: 24 layer pools of 134 MB (3.2 GB), each read once per step",
-                   "parallelism": f"replicas x{world} (requests sharded by rank, no collective)"},
+        "config": decode_config(world, LAYERS),
         "decode_steps_per_s": round(world * args.steps / (ms_job * 1e-3), 1),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": f"{peak_kind} copy bandwidth",
@@ -689,6 +700,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         line["qkv_post"] = run_qkv_post(dev, seed=rank)
         line["lm_head"] = run_lm_head(dev, seed=rank)
         line["scheduler"] = run_scheduler(seed=rank)
+        line["serving"] = serving
     if world == 1 and not args.profile_case:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -822,6 +834,182 @@ def run_e2e(args, dev, pool, tables, ctx, q_dev, kn_dev, vn_dev, world):
     return start.elapsed_time(end), h2d, d2h, args.e2e_steps * LAYERS * DECODE_KERNELS
 
 
+# ---------------------------------------------------------------------------------------- serving (config 3)
+
+SERVE_REQUESTS, SERVE_MAX_SEQS, SERVE_MAX_LEN, SERVE_BUDGET = 200, 256, 2048, 4096
+SERVE_KV_TOKENS = SERVE_MAX_SEQS * SERVE_MAX_LEN  # 32768 blocks of 16: no sequence is ever preempted
+
+
+def serving_workload(seed: int = 0, vocab: int = 151936) -> list[tuple[list[int], int]]:
+    """Config 3's requests: prompt length round(exp(U(ln 16, ln 1024))), ids U{0..vocab-1}, outputs U{16..512}."""
+    g = torch.Generator().manual_seed(seed)
+    u = torch.rand(SERVE_REQUESTS, generator=g, dtype=torch.float64)
+    lens = torch.round(torch.exp(math.log(16) + u * (math.log(1024) - math.log(16)))).long().tolist()
+    outs = torch.randint(16, 513, (SERVE_REQUESTS,), generator=g).tolist()
+    return [(torch.randint(0, vocab, (n,), generator=g).tolist(), m) for n, m in zip(lens, outs)]
+
+
+def serving_config() -> dict:
+    return {"workload": "config 3: end-to-end serving, Qwen2.5-0.5B shape, fp16 random-init weights "
+                        "(N(0, 0.02), seed 0), 200 requests arriving at t=0, prompts log-uniform 16..1024 "
+                        "uniform token ids, outputs U{16..512} with EOS ignored, greedy",
+            "max_num_seqs": SERVE_MAX_SEQS, "max_model_len": SERVE_MAX_LEN,
+            "max_num_batched_tokens": SERVE_BUDGET, "kv_cache_tokens": SERVE_KV_TOKENS, "block_size": BS,
+            "sharding": "request i on rank i mod N (one engine replica and paged pool per GPU)"}
+
+
+def run_serving(args, rank: int, world: int, local: int) -> dict | None:
+    """Config 3 through ``LLMEngine`` on every rank; rank 0 returns the aggregate.
+
+    Each run adds this rank's share of the 200 requests at one common start (after a
+    barrier) and steps the engine until all finish. The run's time on a rank is device
+    time (CUDA events from the start to the last step's end; every step already waits
+    for its tokens); the job's time is the slowest rank's. TTFT and TPOT are the
+    reference's host-clock definitions (benchmarks/run_bench.py:201-221) over all 200
+    requests, gathered from the ranks.
+    """
+    from mini_inference_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from mini_inference_b200.model import Qwen2Config, Qwen2Model, init_random
+
+    dev = torch.device("cuda", local)
+    cfg = Qwen2Config.qwen2_0_5b()
+    model = Qwen2Model(cfg, init_random(cfg, seed=0, std=0.02, dtype=torch.float16, device=dev,
+                                        generator_device="cuda"))
+    requests = serving_workload(seed=0, vocab=cfg.vocab_size)
+    mine = [r for i, r in enumerate(requests) if i % world == rank]
+    t0 = time.perf_counter()
+    engine = LLMEngine(model, EngineConfig(max_num_seqs=SERVE_MAX_SEQS, max_model_len=SERVE_MAX_LEN,
+                                           max_num_batched_tokens=SERVE_BUDGET, kv_cache_tokens=SERVE_KV_TOKENS))
+    capture_s = time.perf_counter() - t0
+    engine.generate([p for p, _ in requests[:8]], SamplingParams(max_tokens=8, ignore_eos=True))  # warm-up
+    stream = torch.cuda.current_stream()
+    graphs = engine.runner.graphs
+    runs = []
+    for run in range(args.serving_warmup + args.serving_runs):
+        engine.step_stats.clear()
+        graphs.timing = []
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start = time.perf_counter()
+        ev0.record(stream)
+        ids = [engine.add_request(p, SamplingParams(max_tokens=m, ignore_eos=True), arrival_time=start)
+               for p, m in mine]
+        while engine.has_unfinished_requests():
+            engine.step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        seqs = [engine.sequences.pop(i) for i in ids]
+        decode_ms = sum(a.elapsed_time(b) for a, b in graphs.timing)
+        stats = engine.step_stats
+        runs.append({"device_ms": ev0.elapsed_time(ev1), "decode_ms": decode_ms,
+                     "records": [(s.arrival_time, s.first_token_time, s.finish_time, len(s.output_token_ids))
+                                 for s in seqs],
+                     "steps": len(stats), "decode_steps": sum(1 for st in stats if st.num_decodes),
+                     "decode_tokens": sum(st.num_decodes for st in stats),
+                     "decode_ctx_tokens": sum(st.decode_context_tokens for st in stats),
+                     "prefill_tokens": sum(st.num_prefill_tokens for st in stats),
+                     "graphed": graphs.replays})
+        if args.serving_check:
+            engine.check_device_errors()
+    engine.check_device_errors()
+    timed = runs[args.serving_warmup:]
+    # Slowest rank per run; latency records from every rank.
+    job_ms = [max_over_ranks(r["device_ms"], world) for r in timed]
+    dec_ms = [max_over_ranks(r["decode_ms"], world) for r in timed]
+    records = gather_to_rank0([r["records"] for r in timed], world)
+    if rank != 0:
+        return None
+    peaks, peak_kind = measured_peaks()
+    total_tokens = sum(m for _, m in requests)
+    w_bytes = model.weight_bytes()
+    kv_per_token = cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * 2
+    r0 = timed[0]
+    # Bytes a decode step must move: every weight once (the tied embedding is the LM head),
+    # the K/V of every context token in every layer, and the appended rows.
+    step_bytes = (r0["decode_steps"] * w_bytes + r0["decode_ctx_tokens"] * kv_per_token)
+    lat = []
+    for per_rank in records:  # per timed run: [rank][request] -> (arrival, first, finish, tokens)
+        flat = [x for rr in per_rank for x in rr]
+        ttft = np.array([f - a for a, f, _, _ in flat])
+        tpot = np.array([(e - f) / (n - 1) for _, f, e, n in flat if n > 1])
+        lat.append((np.percentile(ttft, 50), np.percentile(ttft, 95), np.percentile(tpot, 50),
+                    np.percentile(tpot, 95)))
+    lat = np.mean(np.array(lat), axis=0)
+    ms = statistics.mean(job_ms)
+    dms = statistics.mean(dec_ms)
+    achieved = step_bytes / (statistics.mean(r["decode_ms"] for r in timed) * 1e-3) / 1e9
+    out = {
+        "tok_s": round(total_tokens / (ms * 1e-3), 1), "unit": "output tok/s",
+        "decode_tok_s": round(world * r0["decode_tokens"] / (dms * 1e-3), 1),
+        "n_gpus": world, "output_tokens": total_tokens, "duration_ms": round(ms, 2),
+        "runs": len(timed), "warmup_runs": args.serving_warmup,
+        "ttft_p50_s": round(float(lat[0]), 4), "ttft_p95_s": round(float(lat[1]), 4),
+        "tpot_p50_ms": round(float(lat[2]) * 1e3, 3), "tpot_p95_ms": round(float(lat[3]) * 1e3, 3),
+        "rank0": {"requests": len(mine), "steps": r0["steps"], "decode_steps": r0["decode_steps"],
+                  "prefill_tokens": r0["prefill_tokens"], "decode_ms": round(statistics.mean(r["decode_ms"] for r in timed), 2),
+                  "decode_step_ms_avg": round(statistics.mean(r["decode_ms"] for r in timed) / max(1, r0["decode_steps"]), 4),
+                  "graphs_capture_s": round(capture_s, 2)},
+        "roofline": {"bound": "hbm", "scope": "rank 0's decode steps (device time, graph replays with their copies)",
+                     "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": f"{peak_kind} copy bandwidth",
+                     "bytes_per_decode_step_avg": int(step_bytes / max(1, r0["decode_steps"])),
+                     "weight_bytes": w_bytes, "kv_bytes_per_context_token": kv_per_token},
+        "config": serving_config(),
+        "timing": "device time (CUDA events) from the common start to the last step, max over ranks; "
+                  "TTFT / TPOT from host clocks as benchmarks/run_bench.py:201-221 defines them",
+    }
+    if world == 1 and not args.profile_case:
+        out["cpu_baseline"] = cpu_serving_sample(budget_s=args.serving_cpu_budget)
+    return out
+
+
+def gather_to_rank0(obj, world: int):
+    """Every rank's ``obj`` as a list on rank 0 (gloo, host objects); ``[obj]`` alone at world 1."""
+    if world == 1:
+        return [[o] for o in obj]
+    import torch.distributed as dist
+
+    got = [None] * world
+    dist.all_gather_object(got, obj)
+    return [[got[r][i] for r in range(world)] for i in range(len(obj))]
+
+
+def cpu_serving_sample(budget_s: float = 20.0, n_requests: int = 8, max_tokens: int = 32) -> dict:
+    """The reference's engine on the host cores (``oracle/engine_torch.py``, float32) on a bounded sample.
+
+    The sample is config 3's first ``n_requests`` requests with their outputs capped at
+    ``max_tokens`` (fewer requests if a timed single-request probe says they would not fit
+    ``budget_s``), run as the reference's LLMEngine loop; its output tokens per second is
+    the number, by the same definition as the GPU leg.
+    """
+    from mini_inference_b200.model import Qwen2Config, init_random
+    from oracle.engine_torch import TorchPagedCache, TorchQwen2, serve
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = Qwen2Config.qwen2_0_5b()
+    w = init_random(cfg, seed=0, std=0.02, dtype=torch.float32, device="cpu")
+    model = TorchQwen2(w, cfg.num_layers, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.rms_norm_eps,
+                       cfg.rope_theta, cfg.max_position_embeddings)
+    reqs = [(p, min(m, max_tokens)) for p, m in serving_workload(seed=0, vocab=cfg.vocab_size)[:n_requests]]
+
+    def run(rs):
+        cache = TorchPagedCache(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, len(rs) * (SERVE_MAX_LEN // BS), BS,
+                                len(rs), SERVE_MAX_LEN, torch.float32)
+        t0 = time.perf_counter()
+        seqs = serve(model, cache, rs, len(rs), SERVE_BUDGET, SERVE_MAX_LEN)
+        return time.perf_counter() - t0, sum(len(s.output_token_ids) for s in seqs)
+
+    probe_s, _ = run(reqs[:1])
+    n = max(1, min(n_requests, int(budget_s / max(probe_s, 1e-3))))
+    dt, tokens = run(reqs[:n])
+    return {"value": round(tokens / dt, 2), "unit": "output tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"config 3's first {n} requests (prompts {[len(p) for p, _ in reqs[:n]]} tokens), outputs "
+                      f"capped at {max_tokens} tokens, the reference's engine loop and PyTorch ops in float32 on the "
+                      f"host (oracle/engine_torch.py); {tokens} tokens in {dt:.2f} s",
+            "seconds": round(dt, 2)}
+
+
 # ---------------------------------------------------------------------------------------- CPU legs
 
 
@@ -878,12 +1066,14 @@ def run_reference(args) -> None:
         "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded; config 2 shapes and distributions)", "impl": "reference",
-        "config": {"workload": "config 2: paged decode attention micro-benchmark, fused one-token append",
-                   "batch_per_gpu": BATCH, "context": f"U{{{CTX_LO}..{CTX_HI}}}", "q_heads": HQ, "kv_heads": HKV,
-                   "head_dim": D, "block_size": BS, "pool_blocks": NUM_BLOCKS},
+        "config": decode_config(world, LAYERS),
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_serving:  # config 3 through the reference's engine loop on the host cores
+        sample = cpu_serving_sample(budget_s=args.serving_cpu_budget)
+        line["serving"] = {"tok_s": sample["value"], "unit": sample["unit"], "cpu_baseline": sample,
+                           "config": serving_config()}
     print(json.dumps(line), flush=True)
 
 
@@ -902,6 +1092,13 @@ def main() -> None:
                     help="only the qkv-post leg (RoPE fused with the KV append), for ncu captures")
     ap.add_argument("--lm-head-only", action="store_true",
                     help="only the greedy LM-head leg (0.5B embedding, batches 64 and 256), for ncu captures")
+    ap.add_argument("--serving-runs", type=int, default=2, help="timed runs of config 3's 200 requests")
+    ap.add_argument("--serving-warmup", type=int, default=1, help="untimed runs of config 3 before them")
+    ap.add_argument("--serving-cpu-budget", type=float, default=20.0, help="seconds for the CPU serving sample")
+    ap.add_argument("--serving-check", action="store_true", help="check device errors after every serving run")
+    ap.add_argument("--no-serving", action="store_true", help="skip the config-3 serving leg")
+    ap.add_argument("--serving-only", action="store_true",
+                    help="only the config-3 serving leg (under torchrun: every rank its share)")
     ap.add_argument("--profile-case", action="store_true",
                     help="small case for ncu captures: 4 layer pools (536 MB, still above L2), no e2e / CPU legs")
     args = ap.parse_args()
@@ -919,7 +1116,13 @@ def main() -> None:
         return
     rank, world, local = dist_setup(args.gpus)
     try:
-        line = run_ours(args, rank, world, local)
+        if args.serving_only:
+            with ClockSampler(local) as serve_clocks:
+                line = run_serving(args, rank, world, local)
+            if line is not None:
+                line["clocks"] = serve_clocks.summary()
+        else:
+            line = run_ours(args, rank, world, local)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -145,7 +145,18 @@ enum {
 PKV_API int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
                                    int32_t block_size, int32_t head_dim, int32_t num_q_heads);
 
-/* Size of the device array that pkv_decode_attention_static uses as its workspace. */
+/*
+ * Zero a decode workspace's ticket counters on `stream` (its first 4 KB). Every call leaves
+ * them at zero; after a call that reported an error (a timed-out wait, a refused unit) the
+ * caller resets them before reusing the workspace, so a stale ticket cannot make a later
+ * call merge the wrong chunks. No counterpart in the reference (it keeps no device state
+ * between steps).
+ */
+PKV_API int pkv_decode_reset_workspace(void* workspace, int64_t workspace_bytes, pkv_stream_t stream);
+
+/* Size of the device array that pkv_decode_attention_static uses as its workspace. On a
+ * 148-SM B200 it holds every supported shape except 8 KV heads with more than 8 query heads
+ * each at head_dim 128 (which needs 20 MB): see pkv_decode_attention_static. */
 #define PKV_DECODE_STATIC_SCRATCH_BYTES (16 * 1024 * 1024)
 
 /*
@@ -155,7 +166,11 @@ PKV_API int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, 
  * allocator owns, and so cannot get a workspace buffer mid-step.
  * Arguments, results and status words are those of pkv_decode_attention. Its workspace is
  * one file-scope device array of PKV_DECODE_STATIC_SCRATCH_BYTES per device:
- *   - a call that would need more returns PKV_ERR_WORKSPACE and launches nothing;
+ *   - what a launch needs depends on the model's shape (KV heads, query heads per KV head,
+ *     head_dim) and the GPU's SM count, not on the batch: 4 KB of tickets plus
+ *     2 * CTAs * kv_heads * (8 or 16 rows) * (head_dim + 4) floats. A shape that needs more
+ *     (on a 148-SM B200: 8 KV heads, group > 8, head_dim 128) returns PKV_ERR_WORKSPACE for
+ *     every call and launches nothing;
  *   - every call on a device shares it, so calls that overlap on the GPU (other streams,
  *     other host threads) race and must be serialised by the caller;
  *   - the first call on a device looks the array up and clears it on `stream` (the current
@@ -167,6 +182,15 @@ PKV_API int pkv_decode_attention_static(const pkv_pool* pool, int32_t layer, con
                                 const void* k_new, const void* v_new, int64_t kv_stride_b,
                                 int64_t kv_stride_h, const int64_t* slot_mapping, const int32_t* context_lens,
                                 float scale, int32_t flags, int32_t* status_dev, pkv_stream_t stream);
+
+/* Zero the current device's static decode scratch tickets on `stream` (set-up included, as
+ * on a first call): what pkv_decode_reset_workspace does for a caller workspace, for use
+ * after a pkv_decode_attention_static call that reported an error. */
+PKV_API int pkv_decode_static_reset(pkv_stream_t stream);
+/* Device address and size of the current device's static decode scratch (set-up included),
+ * for callers that inspect or clear it themselves; it is the array's real device address,
+ * found with cudaGetSymbolAddress. */
+PKV_API int pkv_decode_static_scratch(void** address, int64_t* bytes, pkv_stream_t stream);
 
 /*
  * Packed (varlen) prefill attention over the paged cache, prefix-cache hits included.

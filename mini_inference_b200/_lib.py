@@ -75,6 +75,9 @@ SIGNATURES: dict[str, tuple] = {
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                        c_void_p, c_float, c_int32, c_void_p, c_int64, c_void_p, c_void_p]),
     "pkv_decode_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
+    "pkv_decode_reset_workspace": (c_int32, [c_void_p, c_int64, c_void_p]),
+    "pkv_decode_static_reset": (c_int32, [c_void_p]),
+    "pkv_decode_static_scratch": (c_int32, [POINTER(c_void_p), P_I64, c_void_p]),
     "pkv_decode_attention_static": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64,
                                               c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
                                               c_int64, c_void_p, c_void_p, c_float, c_int32, c_void_p, c_void_p]),

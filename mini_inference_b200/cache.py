@@ -372,9 +372,20 @@ class PagedKVCache:
         return ws
 
     def raise_device_errors(self) -> None:
-        """Synchronise and raise any index error a kernel recorded for this cache."""
-        if self.on_gpu:
+        """Synchronise and raise any error a kernel recorded for this cache.
+
+        After an error the decode workspaces' ticket counters are zeroed before the
+        exception propagates: a call that gave up part-way must not leave a ticket that
+        makes a later call merge the wrong chunks.
+        """
+        if not self.on_gpu:
+            return
+        try:
             ops.raise_device_errors(self.status)
+        except (RuntimeError, IndexError):
+            for ws in self._workspaces.values():
+                ops.decode_reset_workspace(ws)
+            raise
 
     # ------------------------------------------------------------ contexts
     def _require_gpu(self) -> None:

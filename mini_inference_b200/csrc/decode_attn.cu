@@ -50,7 +50,8 @@ constexpr int kMinCap = 16;        // items of up to 16 blocks are never split
 constexpr int kLongUnit = 256;     // blocks per CTA above which the split cap is tightened
 constexpr int kIssueLanes = 4;     // producer lanes issuing copies together
 constexpr int kMergeBatch = 4;     // chunk states a merging thread loads at once
-constexpr int kMaxPending = 8;     // split units of one CTA whose tickets are taken at the end
+constexpr int kMaxPending = 32;    // split units of one CTA whose tickets are taken at the end
+constexpr int kTicketBatch = 8;    // tickets thread 0 keeps in flight at once
 constexpr float kLog2e = 1.4426950408889634f;
 
 // D: head_dim, NH: KV heads (all in one tile), RK: rows kept per head (8 or 16 >= group).
@@ -450,10 +451,13 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
         }
       }
       if (!whole && warp == 0 && lane == 0) {
+        // A CTA holds at most ceil(U / C) units, U <= batch + (split units <= max_slots); the
+        // launcher refuses launches where that bound exceeds kMaxPending, so every split unit
+        // gets its ticket below and every counter returns to zero.
         if (s_npend < kMaxPending) {
           s_pend[s_npend++] = make_int4(b, un.nch, sPS[b], 0);
         } else {
-          report(p.status, PKV_ERR_WORKSPACE);  // cannot happen: see kMaxPending
+          report(p.status, PKV_ERR_WORKSPACE);
         }
       }
       named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next unit
@@ -471,16 +475,18 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   // barrier below) orders the other chunks' partials before its threads' reads. One
   // acquire-release atomic per ticket measured faster than fence + atomic + fence.
   if (tid == 0) {
-    int ticket[kMaxPending];
+    for (int k0 = 0; k0 < npend; k0 += kTicketBatch) {
+      int ticket[kTicketBatch];
 #pragma unroll
-    for (int k = 0; k < kMaxPending; ++k)  // all in flight together
-      if (k < npend) ticket[k] = atom_add_acq_rel_gpu(p.counters + s_pend[k].x, 1);
+      for (int k = 0; k < kTicketBatch; ++k)  // a batch in flight together
+        if (k0 + k < npend) ticket[k] = atom_add_acq_rel_gpu(p.counters + s_pend[k0 + k].x, 1);
 #pragma unroll
-    for (int k = 0; k < kMaxPending; ++k) {
-      if (k >= npend) break;
-      const bool last = ticket[k] == s_pend[k].y - 1;
-      if (last) p.counters[s_pend[k].x] = 0;  // ready for the next call
-      s_last[k] = last;
+      for (int k = 0; k < kTicketBatch; ++k) {
+        if (k0 + k >= npend) break;
+        const bool last = ticket[k] == s_pend[k0 + k].y - 1;
+        if (last) p.counters[s_pend[k0 + k].x] = 0;  // ready for the next call
+        s_last[k0 + k] = last;
+      }
     }
   }
   __syncthreads();
@@ -573,6 +579,9 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   const int want = knobs().ctas_per_sm > 0 ? std::min(knobs().ctas_per_sm, per_sm) : per_sm;
   const int ctas = std::min(num_sms() * want, kMaxCtas);
   if (!workspace || workspace_bytes < ws_bytes(ctas, NH, RK, D)) return PKV_ERR_WORKSPACE;
+  // Units per CTA are at most ceil((batch + 2 * ctas) / ctas): whole items plus the split
+  // units' slots. Every split unit of a CTA must fit its pending list (148+ SMs: always).
+  if ((p0.batch + 2 * ctas + ctas - 1) / ctas > kMaxPending) return PKV_ERR_UNSUPPORTED;
   CUtensorMap tk, tv;
   if (!get_pool_maps(pool, &tk, &tv, NH)) return PKV_ERR_CUDA;
   DecodeParams p = p0;
@@ -615,6 +624,11 @@ int launch_heads(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t 
 }  // namespace pkv
 
 using namespace pkv;
+
+extern "C" int pkv_decode_reset_workspace(void* workspace, int64_t workspace_bytes, pkv_stream_t stream) {
+  if (!workspace || workspace_bytes < kPartialsOffset) return PKV_ERR_INVALID_ARGUMENT;
+  return cuda_status(cudaMemsetAsync(workspace, 0, kPartialsOffset, reinterpret_cast<cudaStream_t>(stream)));
+}
 
 extern "C" int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
                                               int32_t block_size, int32_t head_dim, int32_t num_q_heads) {

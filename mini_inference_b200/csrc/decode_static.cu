@@ -57,6 +57,21 @@ int device_scratch(void** out, cudaStream_t stream) {
 }  // namespace
 }  // namespace pkv
 
+extern "C" int pkv_decode_static_scratch(void** address, int64_t* bytes, pkv_stream_t stream) {
+  if (!address || !bytes) return PKV_ERR_INVALID_ARGUMENT;
+  const int st = pkv::device_scratch(address, reinterpret_cast<cudaStream_t>(stream));
+  *bytes = st == PKV_OK ? pkv::kScratchBytes : 0;
+  return st;
+}
+
+extern "C" int pkv_decode_static_reset(pkv_stream_t stream) {
+  void* scratch = nullptr;
+  const int st = pkv::device_scratch(&scratch, reinterpret_cast<cudaStream_t>(stream));
+  if (st != PKV_OK) return st;
+  // The ticket counters lead the array, laid out as in a caller workspace.
+  return pkv_decode_reset_workspace(scratch, pkv::kScratchBytes, stream);
+}
+
 extern "C" int pkv_decode_attention_static(const pkv_pool* pool, int32_t layer, const pkv_tables* tables,
                                            int32_t batch, int32_t num_q_heads, void* out, int64_t out_stride_b,
                                            int64_t out_stride_h, const void* q, int64_t q_stride_b,

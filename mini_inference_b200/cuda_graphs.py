@@ -66,14 +66,36 @@ class _GraphDecodeContext:
         self._attends += 1
         return out.transpose(1, 2)
 
+    def attend_qkv(self, layer_idx: int, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                   num_q_heads: int) -> torch.Tensor:
+        """RoPE fused with the append, then paged attention (as ``PagedDecodeContext.attend_qkv``)."""
+        batch = qkv.shape[0]
+        rows = qkv.reshape(batch, -1)
+        hkv, d = self.cache.num_kv_heads, self.cache.head_dim
+        k_store = torch.empty_like(rows)  # rotated keys with the v columns' row stride
+        k_rot = k_store[:, :hkv * d].view(batch, hkv, d)
+        q_rot, _ = ops.rope_append(self.cache.pool, layer_idx, rows, self.positions, cos, sin, num_q_heads,
+                                   k_out=k_rot, status=self.cache.status)
+        v_new = rows[:, (num_q_heads + hkv) * d:].view(batch, hkv, d)
+        ws = self.cache.workspace(self.cache.max_seqs, num_q_heads)
+        out = torch.empty(batch, 1, num_q_heads, d, dtype=qkv.dtype, device=qkv.device)
+        ops.decode_attention(self.cache.pool, layer_idx, self.tables, q_rot, self.context_lens, ws, k_new=k_rot,
+                             v_new=v_new, slot_mapping=self.slot_mapping, out=out[:, 0], status=self.cache.status,
+                             inputs_ready=self._attends > 0)
+        self._attends += 1
+        return out.transpose(1, 2)
+
 
 class GraphedDecoder:
     """Captures the decode step as CUDA graphs (one per batch bucket) and replays them."""
 
-    def __init__(self, model, cache: PagedKVCache, max_batch: int) -> None:
+    def __init__(self, model, cache: PagedKVCache, max_batch: int, head=None) -> None:
         if not isinstance(cache, PagedKVCache) or not cache.on_gpu:
             raise TypeError("GraphedDecoder needs a libpkv PagedKVCache on a CUDA device")
         self.model, self.cache = model, cache
+        # With a greedy head (sampler.GreedyLMHead) each graph ends in the fused LM head +
+        # argmax and yields token ids instead of float32 logits.
+        self.head = head
         self.paged = True
         self.device = cache.device
         self.batch_buckets = _batch_buckets(min(max_batch, cache.max_seqs))
@@ -85,6 +107,9 @@ class GraphedDecoder:
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, torch.Tensor, _GraphDecodeContext]] = {}
         self._pool = None
         self.replays = 0
+        # When a list, every decode() appends a (start, end) pair of CUDA events around its
+        # copies and replay, for device-side timing of the steps.
+        self.timing: list | None = None
 
     @torch.inference_mode()
     def capture(self) -> None:
@@ -99,6 +124,8 @@ class GraphedDecoder:
         def step() -> torch.Tensor:
             ctx.prepare()
             hidden = self.model(self.ids[:batch], ctx.positions.unsqueeze(1), ctx)
+            if self.head is not None:
+                return self.head(hidden[:, -1])
             return self.model.compute_logits(hidden[:, -1]).float()
 
         self.rows.fill_(-1)  # every row reads and writes the scratch block while recording
@@ -118,7 +145,11 @@ class GraphedDecoder:
 
     @torch.inference_mode()
     def decode(self, slots: Sequence[int], last_tokens: Sequence[int]) -> torch.Tensor | None:
-        """One decode step through a captured graph: logits ``[len(slots), vocab]``, or None."""
+        """One decode step through a captured graph: logits ``[len(slots), vocab]``, or None.
+
+        With a greedy head the result is the step's token ids (int64 ``[len(slots)]`` on the
+        device, valid until the next replay) instead of logits.
+        """
         n = len(slots)
         batch = next((b for b in self.batch_buckets if b >= n), None)
         if batch is None or batch not in self.graphs:
@@ -132,11 +163,17 @@ class GraphedDecoder:
         host[1, :] = -1
         host[1, :n] = slots_np
         host[2, :n] = positions
+        if self.timing is not None:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
         staged = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
         self.ids[:batch, 0].copy_(staged[0])
         self.rows[:batch].copy_(staged[1])
         self.lengths[:batch].copy_(staged[2])
         graph.replay()
+        if self.timing is not None:
+            end.record()
+            self.timing.append((start, end))
         self.replays += 1
         self.cache._bm.commit_decode(slots_np)
         return logits[:n]

@@ -183,6 +183,25 @@ def decode_attention(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tens
     return out
 
 
+def decode_reset_workspace(workspace: torch.Tensor) -> None:
+    """Zero a decode workspace's ticket counters (after a call that reported an error)."""
+    _require_cuda(workspace)
+    check(lib.pkv_decode_reset_workspace(workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                                         _stream()), "decode_reset_workspace")
+
+
+def decode_static_reset() -> None:
+    """Zero the current device's static decode scratch tickets (after a static call that reported an error)."""
+    check(lib.pkv_decode_static_reset(_stream()), "decode_static_reset")
+
+
+def decode_static_scratch() -> tuple[int, int]:
+    """Device address and size of the current device's static decode scratch."""
+    addr, nbytes = ctypes.c_void_p(), ctypes.c_int64()
+    check(lib.pkv_decode_static_scratch(ctypes.byref(addr), ctypes.byref(nbytes), _stream()), "decode_static_scratch")
+    return int(addr.value or 0), nbytes.value
+
+
 def decode_attention_static(pool: PkvPool, layer: int, tables: PkvTables, q: torch.Tensor,
                             context_lens: torch.Tensor, out: torch.Tensor, k_new: torch.Tensor | None = None,
                             v_new: torch.Tensor | None = None, slot_mapping: torch.Tensor | None = None,
@@ -193,7 +212,8 @@ def decode_attention_static(pool: PkvPool, layer: int, tables: PkvTables, q: tor
     The library's static per-device scratch replaces the workspace, and this
     wrapper allocates nothing either: ``out`` is required, and tensors whose last
     dimension is strided are refused rather than copied. Calls on one device must
-    not overlap on the GPU (they share the scratch).
+    not overlap on the GPU (they share the scratch). After a call whose status reports an
+    error, :func:`decode_static_reset` clears the scratch's tickets.
     """
     _require_cuda(q, context_lens, out, k_new, v_new, slot_mapping)
     batch, hq, d = q.shape

@@ -32,6 +32,17 @@ Ham12-3/mini-inference (pure Python + PyTorch, run on the CPU) and records:
 * ``scheduler_traces.json`` -- the reference's ``Scheduler`` over its ``PagedKVCache``
   (``engine/scheduler.py``) on seeded workloads from ``sched_driver.py``: every step's
   prefills, decodes, finishes, queues, preemptions and cache counters.
+* ``streams_<name>.npz`` -- greedy token streams of the reference's own model and engine:
+  ``Qwen2ForCausalLM`` (``engine/model.py:254-323``) with ``torch.manual_seed(seed)`` and
+  ``normal_(0, std)`` over ``named_parameters()`` (std 0.02 at the 0.5B shape), driven as ``LLMEngine.step`` does
+  (``ModelRunner.prefill_packed`` / ``decode`` on a ``PagedKVCache``, the ``Scheduler``,
+  ``pack_by_budget``, ``register_prefix`` and the greedy ``Sampler``,
+  ``engine/engine.py:99-123,281-312``) in float32 on the CPU, for prompts drawn as the task's
+  configuration 1 draws them: the generated tokens of every request and, for every sampled
+  row, its 32 largest logits (ids and values). ``0p5b`` is configuration 1 itself (the
+  Qwen2.5-0.5B shape); ``0p5b_unit_norms`` the same draws with the RMSNorm weights then set
+  to 1 (their own initial value), which makes the tokens depend on the context; ``small`` a
+  2-layer model for the CPU check of the oracle's engine.
 
 The reference does not travel with this repository, so the fixtures are
 committed and this script is only rerun by hand.
@@ -440,16 +451,109 @@ def make_scheduler_traces(Scheduler, Sequence, SamplingParams, PagedKVCache) -> 
     (HERE / "scheduler_traces.json").write_text(json.dumps(traces))
 
 
+# (name, layers, hidden, intermediate, vocab, heads, kv heads, head_dim, requests, prompt lengths, tokens,
+#  unit norms, std)
+STREAM_CASES = [
+    ("0p5b", 24, 896, 4864, 151936, 14, 2, 64, 8, (64, 256), 64, False, 0.02),
+    ("0p5b_unit_norms", 24, 896, 4864, 151936, 14, 2, 64, 8, (64, 256), 64, True, 0.02),
+    ("small", 2, 256, 512, 1000, 14, 2, 64, 4, (8, 40), 16, True, 0.1),
+]
+TOPK = 32
+
+
+def make_greedy_streams(engine_model, engine_engine, engine_scheduler, engine_sampler, engine_sequence,
+                        PagedKVCache, only: str | None = None) -> None:
+    """Greedy streams of the reference's model and engine loop (float32, CPU)."""
+    from types import SimpleNamespace
+
+    for name, layers, hidden, inter, vocab, hq, hkv, d, n_req, (lo, hi), n_tok, unit_norms, std in STREAM_CASES:
+        if only and name != only:
+            continue
+        cfg = engine_model.Qwen2Config(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter,
+                                       num_layers=layers, num_heads=hq, num_kv_heads=hkv, head_dim=d,
+                                       rms_norm_eps=1e-6, rope_theta=1e6, max_position_embeddings=32768,
+                                       tie_word_embeddings=True, attention_bias=True)
+        model = engine_model.Qwen2ForCausalLM(cfg)
+        torch.manual_seed(0)
+        with torch.no_grad():
+            for pname, prm in model.named_parameters():
+                prm.normal_(0, std)
+                if unit_norms and pname.endswith("norm.weight"):
+                    prm.fill_(1.0)
+        model = model.eval()
+        g = torch.Generator().manual_seed(0)
+        lens = torch.randint(lo, hi + 1, (n_req,), generator=g).tolist()
+        prompts = [torch.randint(0, vocab, (n,), generator=g).tolist() for n in lens]
+        max_len = hi + n_tok + 16
+        cache = PagedKVCache.for_model(cfg, num_blocks=n_req * (max_len // 16 + 1), block_size=16, max_seqs=n_req,
+                                       max_len=max_len, dtype=torch.float32, device="cpu")
+        runner = engine_engine.ModelRunner(model, cache)
+        conf = SimpleNamespace(max_num_seqs=n_req, max_num_batched_tokens=4096, max_model_len=max_len,
+                               scheduling="continuous")
+        sched = engine_scheduler.Scheduler(conf, cache)
+        sampler = engine_sampler.Sampler(0, "cpu")
+        seqs = [engine_sequence.Sequence(i, p, engine_sequence.SamplingParams(max_tokens=n_tok, ignore_eos=True), 0.0)
+                for i, p in enumerate(prompts)]
+        for s in seqs:
+            sched.add(s)
+        top_ids = np.zeros((n_req, n_tok, TOPK), np.int32)
+        top_vals = np.zeros((n_req, n_tok, TOPK), np.float32)
+
+        def record(batch_seqs, logits):
+            v, i = logits.topk(TOPK, dim=-1)
+            for s, vv, ii in zip(batch_seqs, v, i):
+                j = len(s.output_token_ids)
+                top_ids[s.seq_id, j], top_vals[s.seq_id, j] = ii.numpy(), vv.numpy()
+
+        with torch.inference_mode():
+            while sched.has_work():  # LLMEngine.step (engine/engine.py:281-312)
+                batch = sched.schedule()
+                new_of = {s.seq_id: s.token_ids[cache.lengths[s.slot]:] for s in batch.prefills}
+                for group in engine_engine.pack_by_budget([len(new_of[s.seq_id]) for s in batch.prefills], 4096):
+                    gs = [batch.prefills[i] for i in group]
+                    logits = runner.prefill_packed([s.slot for s in gs], [new_of[s.seq_id] for s in gs])
+                    for s in gs:
+                        cache.register_prefix(s.slot, s.token_ids)
+                    record(gs, logits)
+                    for s, t in zip(gs, sampler(logits, [s.sampling for s in gs])):
+                        sched.append_token(s, t, 0.0)
+                if batch.decodes:
+                    logits = runner.decode([s.slot for s in batch.decodes], [s.last_token for s in batch.decodes])
+                    record(batch.decodes, logits)
+                    for s, t in zip(batch.decodes, sampler(logits, [s.sampling for s in batch.decodes])):
+                        sched.append_token(s, t, 0.0)
+        flat = [t for p in prompts for t in p]
+        np.savez_compressed(
+            HERE / f"streams_{name}.npz",
+            config=np.array([layers, hidden, inter, vocab, hq, hkv, d], np.int64), unit_norms=np.array(unit_norms),
+            std=np.array(std), seed=np.array(0), max_model_len=np.array(max_len),
+            prompt_lens=np.array(lens, np.int64), prompt_ids=np.array(flat, np.int64),
+            tokens=np.array([s.output_token_ids for s in seqs], np.int64), top_ids=top_ids, top_vals=top_vals,
+            threads=np.array(torch.get_num_threads()))
+        print(name, "distinct tokens per stream:", [len(set(s.output_token_ids)) for s in seqs])
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reference", required=True, help="path of a Ham12-3/mini-inference checkout")
-    ap.add_argument("--only", choices=["rope", "lm_head", "scheduler"], help="write only these fixtures")
+    ap.add_argument("--only", choices=["rope", "lm_head", "scheduler", "streams"], help="write only these fixtures")
+    ap.add_argument("--stream-case", help="with --only streams: just this case")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     from engine.kv_cache import PagedKVCache  # noqa: E402  (the reference's own class)
     from engine.model import RotaryEmbedding, apply_rope  # noqa: E402
 
     torch.set_num_threads(4)
+    if args.only == "streams":
+        import engine.engine as engine_engine  # noqa: E402
+        import engine.model as engine_model  # noqa: E402
+        import engine.sampler as engine_sampler  # noqa: E402
+        import engine.scheduler as engine_scheduler  # noqa: E402
+        import engine.sequence as engine_sequence  # noqa: E402
+        make_greedy_streams(engine_model, engine_engine, engine_scheduler, engine_sampler, engine_sequence,
+                            PagedKVCache, args.stream_case)
+        print("stream fixtures written to", HERE)
+        return
     if args.only == "scheduler":
         sys.path.insert(0, str(HERE))
         from engine.scheduler import Scheduler  # noqa: E402

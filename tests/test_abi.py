@@ -97,3 +97,18 @@ def test_lm_head_argmax_validates_on_the_host():
     assert call(hidden_stride=900) == _lib.PKV_ERR_INVALID_ARGUMENT  # rows not 16-byte aligned
     assert call(ws=16) == _lib.PKV_ERR_WORKSPACE
     assert call(batch=0) == _lib.PKV_OK
+
+
+def test_static_scratch_size_matches_the_header():
+    from mini_inference_b200 import _lib
+
+    m = re.search(r"#define\s+PKV_DECODE_STATIC_SCRATCH_BYTES\s+\(([^)]*)\)", HEADER.read_text())
+    assert m, "PKV_DECODE_STATIC_SCRATCH_BYTES is not defined in pkv.h"
+    assert eval(m.group(1), {"__builtins__": {}}) == _lib.PKV_DECODE_STATIC_SCRATCH_BYTES
+
+
+def test_workspace_reset_validates_before_any_cuda_call():
+    from mini_inference_b200 import _lib
+
+    assert _lib.lib.pkv_decode_reset_workspace(None, 1 << 20, None) == _lib.PKV_ERR_INVALID_ARGUMENT
+    assert _lib.lib.pkv_decode_static_scratch(None, None, None) == _lib.PKV_ERR_INVALID_ARGUMENT

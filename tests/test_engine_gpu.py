@@ -232,8 +232,8 @@ def test_preemption_does_not_change_the_tokens(dev):
 
 def test_greedy_streams_identical_over_64_tokens(dev):
     """The first 64 greedy tokens of every request equal the dense oracle's own greedy stream
-    (float64, recomputed from scratch at every step). A stream may part from the oracle's only
-    at a near-tie of the dense logits; with this model's logit spread none is expected."""
+    (float64, recomputed from scratch at every step), all of them: this model's logits are
+    spread far wider than float16 rounding, so no near-tie may excuse a difference."""
     rng = random.Random(13)
     prefix = [rng.randrange(VOCAB) for _ in range(33)]
     requests = [((prefix if i % 2 else []) + [rng.randrange(VOCAB) for _ in range(rng.randint(3, 40))], 64)
@@ -241,18 +241,12 @@ def test_greedy_streams_identical_over_64_tokens(dev):
     model = Model(dev, seed=2)
     seqs, _, hits = run_engine(dev, model, requests, num_blocks=40, max_seqs=8, budget=1024, max_len=160)
     assert hits > 0
-    identical = 0
     for s in seqs:
         toks = list(s.prompt_token_ids)
         for j in range(64):
             row = oracle_logits(model, toks)[-1]
             want = int(row.argmax())
             got = s.output_token_ids[j]
-            if got != want:
-                tol = 0.02 * max(1.0, abs(row.max()))
-                assert row[got] >= row.max() - tol, (s.seq_id, j, got, want)
-                break
+            assert got == want, (f"stream {s.seq_id} parts from the oracle at token {j}: {got} vs {want} "
+                                 f"(dense logits {row[got]:.5f} vs {row[want]:.5f})")
             toks.append(want)
-        else:
-            identical += 1
-    assert identical >= len(seqs) - 1, f"only {identical} of {len(seqs)} streams identical over 64 tokens"

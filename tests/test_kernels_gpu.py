@@ -220,7 +220,7 @@ def test_prefill_scores_growing_along_the_keys(dev, dtype, d):
 
 def micro_bench_case(dev, seed=0, batch=64, lo=128, hi=2048, num_blocks=16384, layers=2, dtype=torch.float16,
                      hq=14, hkv=2, d=64):
-    """64 sequences, context U{128..2048}, tables from a seeded permutation of the pool."""
+    """The task's configuration 2: 64 sequences, context U{128..2048}, tables from a seeded permutation of the pool."""
     g = torch.Generator().manual_seed(seed)
     ctx = torch.randint(lo, hi + 1, (batch,), generator=g)
     perm = torch.randperm(num_blocks, generator=g)

@@ -94,3 +94,56 @@ def test_static_entry_point_refuses_copies(dev):
     with pytest.raises(ValueError, match="copies nothing"):
         ops.decode_attention_static(ops.make_pool(k_pool, v_pool), 0, ops.make_tables(tab), q_strided, ctx_lens,
                                     out)
+
+
+class _DeviceArray:
+    """A raw device address as a torch tensor, through the CUDA array interface (no copy)."""
+
+    def __init__(self, address: int, n: int, typestr: str) -> None:
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (address, False), "version": 2}
+
+
+def test_static_reset_clears_stale_tickets(dev):
+    """Tickets left in the static scratch (written here from the host) are cleared by the reset,
+    after which the static entry point again matches the workspace entry point bit for bit."""
+    from mini_inference_b200 import ops
+
+    tab, slots, ctx_lens, k_pool, v_pool, qs, news = _case(dev, 11, 64, 14, 2, 64, torch.float16, 16384)
+    out = torch.empty(64, 14, 64, dtype=torch.float16, device=dev)
+    pool = ops.make_pool(k_pool, v_pool)
+    tables = ops.make_tables(tab)
+    ops.decode_attention_static(pool, 0, tables, qs[0], ctx_lens, out)  # set-up on this device
+    torch.cuda.synchronize()
+    addr, nbytes = ops.decode_static_scratch()
+    assert addr and nbytes == 16 * 1024 * 1024
+    tickets = torch.as_tensor(_DeviceArray(addr, 1024, "<i4"), device=dev)
+    tickets[:64] = 3  # a stale ticket for every sequence of the batch
+    ops.decode_static_reset()
+    torch.cuda.synchronize()
+    assert int(tickets.abs().sum()) == 0
+    ws = torch.zeros(ops.decode_workspace_bytes(64, 2, tab.shape[1], 16, 64, 14), dtype=torch.uint8, device=dev)
+    status = torch.zeros(2, dtype=torch.int32, device=dev)
+    got = ops.decode_attention_static(pool, 0, tables, qs[1], ctx_lens, out, status=status[0:1])
+    want = ops.decode_attention(pool, 0, tables, qs[1], ctx_lens, ws, status=status[1:2])
+    ops.raise_device_errors(status)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+def test_static_entry_point_refuses_a_shape_beyond_the_scratch(dev):
+    """8 KV heads of 16 query heads at head_dim 128 need ~20 MB of scratch on a 148-SM B200: the
+    call is refused with PKV_ERR_WORKSPACE before anything runs, leaving out and status as they were."""
+    from mini_inference_b200 import ops
+    from mini_inference_b200._lib import PKV_ERR_WORKSPACE, PkvError
+
+    if torch.cuda.get_device_properties(dev).multi_processor_count < 148:
+        pytest.skip("the scratch need depends on the SM count; sized here for a 148-SM B200")
+    tab, slots, ctx_lens, k_pool, v_pool, qs, _ = _case(dev, 5, 2, 128, 8, 128, torch.bfloat16, 512)
+    out = torch.full((2, 128, 128), 7.0, dtype=torch.bfloat16, device=dev)
+    status = torch.full((1,), 0, dtype=torch.int32, device=dev)
+    before = out.clone()
+    with pytest.raises(PkvError) as err:
+        ops.decode_attention_static(ops.make_pool(k_pool, v_pool), 0, ops.make_tables(tab), qs[0], ctx_lens, out,
+                                    status=status)
+    assert err.value.status == PKV_ERR_WORKSPACE
+    torch.cuda.synchronize()
+    assert torch.equal(out, before) and int(status.item()) == 0
