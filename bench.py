@@ -660,9 +660,11 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     ms_e2e_job = max_over_ranks(ms_e2e, world)
     del g_step, g_attn, k_pool, v_pool
     serving = None
-    if not args.profile_case and not args.no_serving:  # every rank serves its share of config 3
+    prefix_serving = None
+    if not args.profile_case and not args.no_serving:  # every rank serves its share of configs 3 and 4
         with ClockSampler(local) as serve_clocks:
-            serving = run_serving(args, rank, world, local)
+            serving, model = run_serving(args, rank, world, local)
+            prefix_serving = run_prefix_serving(args, rank, world, local, model)
         if serving is not None:
             serving["clocks"] = serve_clocks.summary()
     if rank != 0:
@@ -701,6 +703,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         line["lm_head"] = run_lm_head(dev, seed=rank)
         line["scheduler"] = run_scheduler(seed=rank)
         line["serving"] = serving
+        line["prefix_serving"] = prefix_serving
     if world == 1 and not args.profile_case:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
@@ -919,7 +922,7 @@ def run_serving(args, rank: int, world: int, local: int) -> dict | None:
     dec_ms = [max_over_ranks(r["decode_ms"], world) for r in timed]
     records = gather_to_rank0([r["records"] for r in timed], world)
     if rank != 0:
-        return None
+        return None, model
     peaks, peak_kind = measured_peaks()
     total_tokens = sum(m for _, m in requests)
     w_bytes = model.weight_bytes()
@@ -961,7 +964,91 @@ def run_serving(args, rank: int, world: int, local: int) -> dict | None:
     }
     if world == 1 and not args.profile_case:
         out["cpu_baseline"] = cpu_serving_sample(budget_s=args.serving_cpu_budget)
-    return out
+    return out, model
+
+
+PREFIX_REQUESTS, PREFIX_LEN, PREFIX_OUT = 256, 1024, 128
+
+
+def prefix_workload(seed: int = 4, vocab: int = 151936) -> list[tuple[list[int], int]]:
+    """Config 4's requests: one seeded 1024-token common prefix + U{64..256} own ids, 128 outputs each."""
+    g = torch.Generator().manual_seed(seed)
+    shared = torch.randint(0, vocab, (PREFIX_LEN,), generator=g).tolist()
+    lens = torch.randint(64, 257, (PREFIX_REQUESTS,), generator=g).tolist()
+    return [(shared + torch.randint(0, vocab, (n,), generator=g).tolist(), PREFIX_OUT) for n in lens]
+
+
+def run_prefix_serving(args, rank: int, world: int, local: int, model=None) -> dict | None:
+    """Config 4 through ``LLMEngine`` with prefix caching; rank i mod N serves request i.
+
+    Every run uses a fresh engine (an empty prefix cache), so each run sees the same
+    admissions and hits: the requests admitted in the first step miss (their prefix is
+    registered only after their prefill, engine/engine.py:297-298) and every later one finds
+    the 64 prefix blocks cached.
+    """
+    from mini_inference_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from mini_inference_b200.model import Qwen2Config, Qwen2Model, init_random
+
+    dev = torch.device("cuda", local)
+    cfg = Qwen2Config.qwen2_0_5b()
+    if model is None:
+        model = Qwen2Model(cfg, init_random(cfg, seed=0, std=0.02, dtype=torch.float16, device=dev,
+                                            generator_device="cuda"))
+    requests = prefix_workload(vocab=cfg.vocab_size)
+    mine = [r for i, r in enumerate(requests) if i % world == rank]
+    stream = torch.cuda.current_stream()
+    runs = []
+    for run in range(1 + args.serving_runs):  # one untimed run first
+        engine = LLMEngine(model, EngineConfig(max_num_seqs=SERVE_MAX_SEQS, max_model_len=SERVE_MAX_LEN,
+                                               max_num_batched_tokens=SERVE_BUDGET, kv_cache_tokens=SERVE_KV_TOKENS,
+                                               enable_prefix_caching=True))
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start = time.perf_counter()
+        ev0.record(stream)
+        seqs = [engine.sequences[engine.add_request(p, SamplingParams(max_tokens=m, ignore_eos=True),
+                                                    arrival_time=start)] for p, m in mine]
+        while engine.has_unfinished_requests():
+            engine.step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        engine.check_device_errors()
+        runs.append({"device_ms": ev0.elapsed_time(ev1), "hits": engine.cache.prefix_hit_tokens,
+                     "prompt_tokens": sum(len(p) for p, _ in mine),
+                     "misses": sum(1 for s in seqs if s.num_cached_tokens == 0),
+                     "records": [(s.arrival_time, s.first_token_time, s.finish_time, len(s.output_token_ids))
+                                 for s in seqs]})
+        del engine
+    timed = runs[1:]
+    job_ms = [max_over_ranks(r["device_ms"], world) for r in timed]
+    hits = [sum_over_ranks(r["hits"], world) for r in timed]
+    misses = sum_over_ranks(timed[0]["misses"], world)
+    records = gather_to_rank0([r["records"] for r in timed], world)
+    if rank != 0:
+        return None
+    ms = statistics.mean(job_ms)
+    flat = [x for rr in records[0] for x in rr]
+    ttft = np.array([f - a for a, f, _, _ in flat])
+    prompt_tokens = sum(len(p) for p, _ in requests)
+    return {"workload": "config 4: 256 requests sharing one seeded 1024-token prefix + U{64..256} own tokens, "
+                        "128 greedy outputs each, prefix caching on, max_num_batched_tokens 4096",
+            "tok_s": round(PREFIX_REQUESTS * PREFIX_OUT / (ms * 1e-3), 1), "unit": "output tok/s", "n_gpus": world,
+            "duration_ms": round(ms, 2), "runs": len(timed), "prefix_hit_tokens": hits[0],
+            "prefix_hit_tokens_every_run_equal": len(set(hits)) == 1, "prompt_tokens": prompt_tokens,
+            "hit_rate": round(hits[0] / prompt_tokens, 4), "requests_without_hit": misses,
+            "ttft_p50_s": round(float(np.percentile(ttft, 50)), 4),
+            "ttft_p95_s": round(float(np.percentile(ttft, 95)), 4)}
+
+
+def sum_over_ranks(value: int, world: int) -> int:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.int64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return int(t.item())
 
 
 def gather_to_rank0(obj, world: int):
@@ -975,7 +1062,7 @@ def gather_to_rank0(obj, world: int):
     return [[got[r][i] for r in range(world)] for i in range(len(obj))]
 
 
-def cpu_serving_sample(budget_s: float = 20.0, n_requests: int = 8, max_tokens: int = 32) -> dict:
+def cpu_serving_sample(budget_s: float = 20.0, n_requests: int = 32, max_tokens: int = 32) -> dict:
     """The reference's engine on the host cores (``oracle/engine_torch.py``, float32) on a bounded sample.
 
     The sample is config 3's first ``n_requests`` requests with their outputs capped at
@@ -1118,9 +1205,11 @@ def main() -> None:
     try:
         if args.serving_only:
             with ClockSampler(local) as serve_clocks:
-                line = run_serving(args, rank, world, local)
+                line, model = run_serving(args, rank, world, local)
+                prefix = run_prefix_serving(args, rank, world, local, model)
             if line is not None:
                 line["clocks"] = serve_clocks.summary()
+                line["prefix_serving"] = prefix
         else:
             line = run_ours(args, rank, world, local)
         if line is not None:

@@ -334,6 +334,21 @@ PKV_API int pkv_bm_free(pkv_block_manager* bm, int32_t slot);
  * PKV_ERR_UNKNOWN_SLOT a slot without a table.
  */
 PKV_API int pkv_bm_decode_positions(const pkv_block_manager* bm, const int32_t* slots, int32_t n, int32_t* out);
+/*
+ * Copy-on-write of shared blocks; no counterpart in the reference, which shares only full
+ * blocks no sequence writes again (engine/kv_cache.py:499-501, 536-537), so neither call
+ * changes anything on its allocator traces.
+ * pkv_bm_fork: a new slot whose table shares every block of src_slot, a partially filled
+ * last one included (refcounts + 1; same length). PKV_ERR_NO_BLOCKS without a free slot.
+ * pkv_bm_prepare_write: before tokens first_pos .. first_pos + n_tokens - 1 of `slot` are
+ * written, each block of that range that another sequence also holds is replaced in this
+ * slot's table by a fresh block; (old, fresh) pairs go to `pairs` (2 ints each, at most
+ * cap_pairs, else PKV_ERR_WORKSPACE) for pkv_copy_blocks to copy before the write.
+ * PKV_ERR_NO_BLOCKS, with nothing changed, when the pool cannot supply them.
+ */
+PKV_API int pkv_bm_fork(pkv_block_manager* bm, int32_t src_slot, int32_t* out_slot);
+PKV_API int pkv_bm_prepare_write(pkv_block_manager* bm, int32_t slot, int64_t first_pos, int64_t n_tokens,
+                                 int32_t* pairs, int32_t cap_pairs, int32_t* n_pairs);
 /* lengths[slots[i]] += 1 for each i: PagedDecodeContext.commit (engine/kv_cache.py:622-624). */
 PKV_API int pkv_bm_commit_decode(pkv_block_manager* bm, const int32_t* slots, int32_t n);
 /* lengths[slot] read / write (the reference's public `lengths` dict, engine/kv_cache.py:431) */
@@ -385,6 +400,8 @@ typedef struct pkv_sched_step {
   int32_t* decode_slots;
   int64_t* preempted_ids;          /* preempted while making room, in order (now waiting) */
   int32_t n_prefills, n_decodes, n_preempted;
+  int64_t* prefill_new_tokens;     /* tokens each prefill processes this step (NULL: not written); the
+                                    * rest of the sequence unless chunked prefill splits it */
 } pkv_sched_step;
 
 /* static_batching: the reference's scheduling == "static" (nobody joins a running batch) */
@@ -397,6 +414,16 @@ PKV_API int pkv_sched_add(pkv_scheduler* s, int64_t seq_id, const int64_t* promp
                   int32_t max_tokens, int32_t ignore_eos);
 /* Scheduler.schedule (engine/scheduler.py:68-111); PKV_ERR_WORKSPACE if capacity is too small */
 PKV_API int pkv_sched_schedule(pkv_scheduler* s, pkv_sched_step* out);
+/*
+ * Chunked prefill, off by default (the reference has none: README.md:470-473,
+ * engine/kv_cache.py:243-249). When on, a prompt is prefilled across steps: each step runs
+ * every decode first, then the running sequences still prefilling (oldest first), then
+ * admissions from the queue's front, each given what is left of max_num_batched_tokens
+ * (prefill_new_tokens says how many); a sequence whose last prompt token is still
+ * unwritten decodes it and samples its first token. Admission, allocation and preemption
+ * stay the reference's.
+ */
+PKV_API int pkv_sched_set_chunked_prefill(pkv_scheduler* s, int32_t enable);
 /* Scheduler.append_token for n (seq_id, token) pairs in order (engine/scheduler.py:143-159):
  * finish_reasons[i] = PKV_FINISH_*; finished sequences leave running and free their slot. */
 PKV_API int pkv_sched_append_tokens(pkv_scheduler* s, const int64_t* seq_ids, const int64_t* tokens, int32_t n,

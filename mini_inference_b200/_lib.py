@@ -50,7 +50,7 @@ class PkvSchedStep(ctypes.Structure):
     _fields_ = [("capacity", c_int32), ("prefill_ids", c_void_p), ("prefill_slots", c_void_p),
                 ("prefill_cached_tokens", c_void_p), ("decode_ids", c_void_p), ("decode_slots", c_void_p),
                 ("preempted_ids", c_void_p), ("n_prefills", c_int32), ("n_decodes", c_int32),
-                ("n_preempted", c_int32)]
+                ("n_preempted", c_int32), ("prefill_new_tokens", c_void_p)]
 
 
 P_POOL = POINTER(PkvPool)
@@ -96,6 +96,7 @@ SIGNATURES: dict[str, tuple] = {
     "pkv_sched_destroy": (None, [c_void_p]),
     "pkv_sched_add": (c_int32, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32]),
     "pkv_sched_schedule": (c_int32, [c_void_p, POINTER(PkvSchedStep)]),
+    "pkv_sched_set_chunked_prefill": (c_int32, [c_void_p, c_int32]),
     "pkv_sched_append_tokens": (c_int32, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p]),
     "pkv_sched_abort": (c_int32, [c_void_p, c_int64, P_I32]),
     "pkv_sched_counts": (c_int32, [c_void_p, P_I32, P_I32, P_I64]),
@@ -107,6 +108,8 @@ SIGNATURES: dict[str, tuple] = {
     "pkv_bm_register_prefix": (c_int32, [c_void_p, c_int32, c_void_p, c_int64]),
     "pkv_bm_ensure_capacity": (c_int32, [c_void_p, c_int32, c_int64, P_I32]),
     "pkv_bm_free": (c_int32, [c_void_p, c_int32]),
+    "pkv_bm_fork": (c_int32, [c_void_p, c_int32, P_I32]),
+    "pkv_bm_prepare_write": (c_int32, [c_void_p, c_int32, c_int64, c_int64, c_void_p, c_int32, P_I32]),
     "pkv_bm_decode_positions": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p]),
     "pkv_bm_commit_decode": (c_int32, [c_void_p, c_void_p, c_int32]),
     "pkv_bm_get_length": (c_int32, [c_void_p, c_int32, P_I64]),

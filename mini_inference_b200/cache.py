@@ -146,6 +146,27 @@ class NativeBlockManager:
         check(st, "decode positions")
         return out
 
+    def fork(self, slot: int) -> int:
+        st = lib.pkv_bm_fork(self._h, slot, ctypes.byref(self._i32))
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError(slot)
+        if st == PKV_ERR_NO_BLOCKS:
+            raise RuntimeError("no free slot to fork into")
+        check(st, "fork")
+        return self._i32.value
+
+    def prepare_write(self, slot: int, first_pos: int, n_tokens: int) -> list[tuple[int, int]]:
+        """(old, fresh) block pairs to copy before tokens first_pos.. of slot are written (shared blocks only)."""
+        cap = self.blocks_for(n_tokens) + 1
+        buf = (ctypes.c_int32 * (2 * cap))()
+        st = lib.pkv_bm_prepare_write(self._h, slot, first_pos, n_tokens, buf, cap, ctypes.byref(self._i32))
+        if st == PKV_ERR_NO_BLOCKS:
+            raise RuntimeError("not enough free KV cache blocks")
+        if st == PKV_ERR_UNKNOWN_SLOT:
+            raise KeyError(slot)
+        check(st, "prepare_write")
+        return [(buf[2 * i], buf[2 * i + 1]) for i in range(self._i32.value)]
+
     def commit_decode(self, slots: np.ndarray) -> None:
         check(lib.pkv_bm_commit_decode(self._h, slots.ctypes.data, len(slots)), "commit")
 
@@ -260,7 +281,7 @@ class PagedKVCache:
 
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, num_blocks: int, block_size: int,
                  max_seqs: int, max_len: int, dtype: torch.dtype, device: torch.device | str,
-                 enable_prefix_caching: bool = False) -> None:
+                 enable_prefix_caching: bool = False, enable_copy_on_write: bool = False) -> None:
         shape = (num_layers, num_blocks + 1, num_kv_heads, block_size, head_dim)
         self.k = torch.zeros(shape, dtype=dtype, device=device)
         self.v = torch.zeros(shape, dtype=dtype, device=device)
@@ -273,6 +294,10 @@ class PagedKVCache:
         self.max_seqs = max_seqs
         self.max_len = max_len
         self.enable_prefix_caching = enable_prefix_caching
+        # Copy-on-write of shared partially filled blocks (fork). Off by default: the
+        # reference never writes a shared block, and with it off every allocator decision
+        # is the reference's.
+        self.enable_copy_on_write = enable_copy_on_write
         self._bm = NativeBlockManager(num_blocks, block_size, max_seqs, max_len, enable_prefix_caching)
         self.lengths = _LengthsView(self._bm)
         self.block_tables = _TablesView(self._bm)
@@ -326,6 +351,32 @@ class PagedKVCache:
 
     def free(self, slot: int) -> None:
         self._bm.free(slot)
+
+    def fork(self, slot: int) -> int:
+        """A new sequence sharing all of ``slot``'s blocks and length (copy-on-write on its first write).
+
+        No counterpart in the reference. Needs ``enable_copy_on_write``: whichever of the two
+        sequences first writes into a block they share (the partially filled last block, on
+        the next token) gets a private copy of it, made on the device before the write.
+        """
+        if not self.enable_copy_on_write:
+            raise RuntimeError("fork needs a cache built with enable_copy_on_write=True")
+        return self._bm.fork(slot)
+
+    def copy_on_write(self, writes: Sequence[tuple[int, int, int]]) -> int:
+        """Give every (slot, first position, tokens) about to be written its own copy of any shared block.
+
+        Launches one ``pkv_copy_blocks`` (every layer, K and V) for all the copies, on the
+        current stream, ahead of the writes; the table mirror is updated by the next
+        :meth:`sync_tables`. Returns the number of blocks copied.
+        """
+        if not self.enable_copy_on_write:
+            return 0
+        pairs = [pr for slot, a, n in writes for pr in self._bm.prepare_write(slot, a, n)]
+        if pairs and self.on_gpu:
+            dev = torch.from_numpy(np.asarray(pairs, np.int32).T.copy()).pin_memory().to(self.device, non_blocking=True)
+            ops.copy_blocks(self.pool, dev[0], dev[1], self.status)
+        return len(pairs)
 
     def write_index(self, slots: Sequence[int], starts: Sequence[int], counts: Sequence[int]
                     ) -> tuple[torch.Tensor, torch.Tensor]:
@@ -413,6 +464,8 @@ class PagedDecodeContext:
         self.slots = list(slots)
         self._slots_np = np.asarray(self.slots, dtype=np.int32)
         pos = cache._bm.decode_positions(self._slots_np)  # raises the reference's ValueError
+        if cache.enable_copy_on_write:
+            cache.copy_on_write([(s, int(p), 1) for s, p in zip(self.slots, pos)])
         cache.sync_tables()
         batch = len(self.slots)
         dev = cache.device
@@ -499,6 +552,7 @@ class PackedPrefillContext:
         for s, start, n in zip(self.slots, self.starts, self.lengths):
             if not cache.ensure_capacity(s, start + n):
                 raise ValueError(f"no room in the KV cache for {start + n} tokens")
+        cache.copy_on_write(list(zip(self.slots, self.starts, self.lengths)))
         cache.sync_tables()
         dev = cache.device
         cu = np.zeros(len(self.slots) + 1, np.int32)

@@ -297,6 +297,51 @@ int pkv_bm_free(pkv_block_manager* bm, int32_t slot) {
   return PKV_OK;
 }
 
+int pkv_bm_fork(pkv_block_manager* bm, int32_t src_slot, int32_t* out_slot) {
+  if (!bm || !out_slot) return PKV_ERR_INVALID_ARGUMENT;
+  if (!bm->valid_slot(src_slot)) return PKV_ERR_UNKNOWN_SLOT;
+  if (bm->slot_stack.empty()) return PKV_ERR_NO_BLOCKS;
+  const int32_t slot = bm->slot_stack.back();
+  bm->slot_stack.pop_back();
+  std::vector<int32_t>& table = bm->tables[slot];
+  table = bm->tables[src_slot];  // every block shared, a partially filled last one included
+  for (size_t i = 0; i < table.size(); ++i) {
+    bm->add_ref(table[i]);
+    bm->record(slot, static_cast<int32_t>(i), table[i]);
+  }
+  bm->live[slot] = 1;
+  bm->lengths[slot] = bm->lengths[src_slot];
+  *out_slot = slot;
+  return PKV_OK;
+}
+
+int pkv_bm_prepare_write(pkv_block_manager* bm, int32_t slot, int64_t first_pos, int64_t n_tokens, int32_t* pairs,
+                         int32_t cap_pairs, int32_t* n_pairs) {
+  if (!bm || !n_pairs || n_tokens < 0 || first_pos < 0 || (cap_pairs > 0 && !pairs)) return PKV_ERR_INVALID_ARGUMENT;
+  *n_pairs = 0;
+  if (!bm->valid_slot(slot)) return PKV_ERR_UNKNOWN_SLOT;
+  if (n_tokens == 0) return PKV_OK;
+  std::vector<int32_t>& table = bm->tables[slot];
+  const int64_t b0 = first_pos / bm->block_size, b1 = (first_pos + n_tokens - 1) / bm->block_size;
+  if (b1 >= static_cast<int64_t>(table.size())) return PKV_ERR_OUT_OF_RANGE;
+  int32_t shared = 0;
+  for (int64_t i = b0; i <= b1; ++i) shared += bm->refs[table[i]] > 1;
+  if (shared > cap_pairs) return PKV_ERR_WORKSPACE;
+  if (shared > bm->pool_size) return PKV_ERR_NO_BLOCKS;  // nothing changed
+  for (int64_t i = b0; i <= b1; ++i) {
+    const int32_t old = table[i];
+    if (bm->refs[old] <= 1) continue;
+    const int32_t fresh = bm->take_fresh();
+    table[i] = fresh;
+    bm->drop_ref(old);  // still held by the sequences it is shared with
+    bm->record(slot, static_cast<int32_t>(i), fresh);
+    pairs[2 * *n_pairs] = old;
+    pairs[2 * *n_pairs + 1] = fresh;
+    ++*n_pairs;
+  }
+  return PKV_OK;
+}
+
 int pkv_bm_decode_positions(const pkv_block_manager* bm, const int32_t* slots, int32_t n, int32_t* out) {
   if (!bm || n < 0 || (n > 0 && (!slots || !out))) return PKV_ERR_INVALID_ARGUMENT;
   for (int32_t i = 0; i < n; ++i) {

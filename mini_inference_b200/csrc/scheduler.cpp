@@ -40,6 +40,7 @@ struct pkv_scheduler {
   int64_t max_num_batched_tokens = 0;
   int64_t max_model_len = 0;
   bool static_batching = false;
+  bool chunked_prefill = false;  // split prompts across steps under the token budget (opt-in)
   std::unordered_set<int64_t> eos;
   std::unordered_map<int64_t, Request> reqs;  // unfinished requests
   std::deque<int64_t> waiting;
@@ -128,9 +129,91 @@ int pkv_sched_add(pkv_scheduler* s, int64_t seq_id, const int64_t* prompt_ids, i
   return PKV_OK;
 }
 
+namespace {
+
+// Chunked prefill (opt-in; the reference has none, README.md:470-473). A running sequence
+// whose cache holds all its tokens but the last sampled one decodes; one that holds fewer
+// is still prefilling and continues with as many of its remaining tokens as the budget
+// leaves. Each step: decodes first (one token each), then the running prefills oldest
+// first, then admissions from the front of the queue while the budget lasts, each taking
+// what is left of it (at least one token). Preemption and the cache checks are the
+// reference's (whole-sequence allocation at admission).
+int schedule_chunked(pkv_scheduler* s, pkv_sched_step* out) {
+  std::vector<int64_t> preempted;
+  int rc = s->make_room_for_decodes(preempted);
+  if (rc != PKV_OK) return rc;
+  const int32_t cap = out->capacity;
+  if (static_cast<int64_t>(preempted.size()) > cap) return PKV_ERR_WORKSPACE;
+  for (int64_t id : preempted) out->preempted_ids[out->n_preempted++] = id;
+  auto emit_prefill = [&](int64_t id, const Request& r, int64_t cached, int64_t n_new) {
+    if (out->n_prefills >= cap) return PKV_ERR_WORKSPACE;
+    out->prefill_slots[out->n_prefills] = r.slot;
+    out->prefill_cached_tokens[out->n_prefills] = cached;
+    if (out->prefill_new_tokens) out->prefill_new_tokens[out->n_prefills] = n_new;
+    out->prefill_ids[out->n_prefills++] = id;
+    return PKV_OK;
+  };
+  int64_t budget = s->max_num_batched_tokens;
+  std::vector<std::pair<int64_t, int64_t>> partial;  // (id, tokens still to prefill)
+  for (int64_t id : s->running) {
+    const Request& r = s->req(id);
+    int64_t held = 0;
+    rc = pkv_bm_get_length(s->bm, r.slot, &held);
+    if (rc != PKV_OK) return rc;
+    const int64_t remaining = static_cast<int64_t>(r.tokens.size()) - held;
+    if (remaining > 1) { partial.emplace_back(id, remaining); continue; }
+    if (out->n_decodes >= cap) return PKV_ERR_WORKSPACE;
+    out->decode_slots[out->n_decodes] = r.slot;
+    out->decode_ids[out->n_decodes++] = id;
+    budget -= 1;
+  }
+  for (const auto& [id, remaining] : partial) {
+    const int64_t chunk = std::min(remaining, budget);
+    if (chunk <= 0) break;
+    int64_t held = 0;
+    pkv_bm_get_length(s->bm, s->req(id).slot, &held);
+    if ((rc = emit_prefill(id, s->req(id), held, chunk)) != PKV_OK) return rc;
+    budget -= chunk;
+  }
+  if (s->static_batching && !s->running.empty()) return PKV_OK;
+  while (budget > 0 && !s->waiting.empty() && static_cast<int32_t>(s->running.size()) < s->max_num_seqs) {
+    const int64_t id = s->waiting.front();
+    Request& r = s->req(id);
+    const int64_t num_tokens = static_cast<int64_t>(r.tokens.size());
+    int32_t fits = 0;
+    rc = pkv_bm_can_allocate(s->bm, num_tokens + 1, &fits);
+    if (rc != PKV_OK) return rc;
+    if (!fits) break;
+    if (out->n_prefills >= cap) return PKV_ERR_WORKSPACE;
+    s->waiting.pop_front();
+    int32_t slot = -1;
+    rc = pkv_bm_allocate(s->bm, num_tokens, r.tokens.data(), num_tokens, &slot);
+    if (rc != PKV_OK) return rc;
+    int64_t cached = 0;
+    pkv_bm_get_length(s->bm, slot, &cached);
+    r.slot = slot;
+    r.num_cached_tokens = cached;
+    r.status = PKV_SEQ_RUNNING;
+    s->running.push_back(id);
+    const int64_t chunk = std::min(num_tokens - cached, budget);
+    if ((rc = emit_prefill(id, r, cached, chunk)) != PKV_OK) return rc;
+    budget -= chunk;
+  }
+  return PKV_OK;
+}
+
+}  // namespace
+
+int pkv_sched_set_chunked_prefill(pkv_scheduler* s, int32_t enable) {
+  if (!s) return PKV_ERR_INVALID_ARGUMENT;
+  s->chunked_prefill = enable != 0;
+  return PKV_OK;
+}
+
 int pkv_sched_schedule(pkv_scheduler* s, pkv_sched_step* out) {  // engine/scheduler.py:68-111
   if (!s || !out) return PKV_ERR_INVALID_ARGUMENT;
   out->n_prefills = out->n_decodes = out->n_preempted = 0;
+  if (s->chunked_prefill) return schedule_chunked(s, out);
   std::vector<int64_t> preempted;
   int rc = s->make_room_for_decodes(preempted);
   if (rc != PKV_OK) return rc;
@@ -166,6 +249,7 @@ int pkv_sched_schedule(pkv_scheduler* s, pkv_sched_step* out) {  // engine/sched
     s->running.push_back(id);
     out->prefill_slots[out->n_prefills] = slot;
     out->prefill_cached_tokens[out->n_prefills] = cached;
+    if (out->prefill_new_tokens) out->prefill_new_tokens[out->n_prefills] = num_tokens - cached;
     out->prefill_ids[out->n_prefills++] = id;
     budget -= num_tokens - cached;
   }

@@ -157,6 +157,8 @@ class GraphedDecoder:
         graph, logits, _ = self.graphs[batch]
         slots_np = np.asarray(list(slots), dtype=np.int32)
         positions = self.cache._bm.decode_positions(slots_np)  # raises the reference's ValueError
+        if self.cache.enable_copy_on_write:
+            self.cache.copy_on_write([(s, int(p), 1) for s, p in zip(slots_np.tolist(), positions.tolist())])
         self.cache.sync_tables()
         host = np.zeros((3, batch), dtype=np.int64)
         host[0, :n] = np.asarray(list(last_tokens), dtype=np.int64)

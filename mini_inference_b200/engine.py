@@ -110,6 +110,9 @@ class EngineConfig:
     batched_prefill: bool = True
     cuda_graphs: bool = True
     cuda_graph_max_batch: int | None = None
+    # Prefill long prompts across steps under the token budget (opt-in; the reference has
+    # none, README.md:470-473). With it a prompt may be longer than the budget.
+    chunked_prefill: bool = False
 
     def __post_init__(self) -> None:
         if self.max_num_seqs < 1:
@@ -122,8 +125,10 @@ class EngineConfig:
             self.kv_cache_tokens = self.max_num_seqs * self.max_model_len
         if self.kv_cache_tokens < self.max_model_len:
             raise ValueError("kv_cache_tokens must be >= max_model_len")
-        if self.max_num_batched_tokens < self.max_model_len:
+        if self.max_num_batched_tokens < self.max_model_len and not self.chunked_prefill:
             raise ValueError("max_num_batched_tokens must be >= max_model_len")
+        if self.max_num_batched_tokens < 1:
+            raise ValueError("max_num_batched_tokens must be at least 1")
         if self.cuda_graph_max_batch is None:
             self.cuda_graph_max_batch = self.max_num_seqs
 
@@ -258,20 +263,28 @@ class LLMEngine:
         batch = self.scheduler.schedule()
         new_tokens: list[tuple[int, int]] = []
         budget = self.config.max_num_batched_tokens if self.config.batched_prefill else 0
-        news = [s.token_ids[self.cache.lengths[s.slot]:] for s in batch.prefills]
-        n_prefill_tokens = sum(len(n) for n in news)
-        for group in pack_by_budget([len(n) for n in news], budget):
+        # Each prefill processes its next `count` tokens: all it has not cached, unless
+        # chunked prefill gave it only part of this step's budget. Only a sequence whose
+        # prefill reaches its last token samples one.
+        starts = [self.cache.lengths[s.slot] for s in batch.prefills]
+        counts = batch.prefill_tokens
+        news = [s.token_ids[a:a + n] for s, a, n in zip(batch.prefills, starts, counts)]
+        n_prefill_tokens = sum(counts)
+        for group in pack_by_budget(counts, budget):
             seqs = [batch.prefills[i] for i in group]
             tokens = self.runner.prefill_tokens([s.slot for s in seqs], [news[i] for i in group])
             for s in seqs:
                 self.cache.register_prefix(s.slot, s.token_ids)
-            self.scheduler.append_tokens(seqs, tokens, time.perf_counter())
-            new_tokens.extend((s.seq_id, t) for s, t in zip(seqs, tokens))
+            done = [(s, t) for i, s, t in zip(group, seqs, tokens) if starts[i] + counts[i] == s.num_tokens]
+            self.scheduler.append_tokens([s for s, _ in done], [t for _, t in done], time.perf_counter())
+            new_tokens.extend((s.seq_id, t) for s, t in done)
         ctx_tokens = 0
         if batch.decodes:
             ctx_tokens = sum(s.num_tokens for s in batch.decodes)
+            # The token at the sequence's last position: its last output, or (chunked prefill)
+            # the last prompt token when the final chunk left exactly that one.
             tokens = self.runner.decode_tokens([s.slot for s in batch.decodes],
-                                               [s.last_token for s in batch.decodes])
+                                               [s.token_ids[-1] for s in batch.decodes])
             self.scheduler.append_tokens(batch.decodes, tokens, time.perf_counter())
             new_tokens.extend((s.seq_id, t) for s, t in zip(batch.decodes, tokens))
         self.step_stats.append(StepStats(

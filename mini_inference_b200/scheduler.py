@@ -49,6 +49,9 @@ class SchedulerOutput:
 
     prefills: list = field(default_factory=list)
     decodes: list = field(default_factory=list)
+    # Tokens each prefill processes this step, parallel to ``prefills``: all the sequence's
+    # uncached tokens, or with chunked prefill the part the step's budget allows.
+    prefill_tokens: list = field(default_factory=list)
 
     @property
     def is_empty(self) -> bool:
@@ -94,9 +97,14 @@ class Scheduler:
         self._dec_ids = np.zeros(cap, np.int64)
         self._dec_slots = np.zeros(cap, np.int32)
         self._preempted = np.zeros(cap, np.int64)
+        self._pre_new = np.zeros(cap, np.int64)
         self._step = PkvSchedStep(cap, self._pre_ids.ctypes.data, self._pre_slots.ctypes.data,
                                   self._pre_cached.ctypes.data, self._dec_ids.ctypes.data,
-                                  self._dec_slots.ctypes.data, self._preempted.ctypes.data, 0, 0, 0)
+                                  self._dec_slots.ctypes.data, self._preempted.ctypes.data, 0, 0, 0,
+                                  self._pre_new.ctypes.data)
+        self.chunked_prefill = bool(getattr(config, "chunked_prefill", False))
+        if self.chunked_prefill:
+            _check(lib.pkv_sched_set_chunked_prefill(self._h, 1), "chunked prefill")
         self._seqs: dict[int, object] = {}  # unfinished sequences by id
         self._i32a, self._i32b, self._i64 = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int64()
 
@@ -161,12 +169,14 @@ class Scheduler:
             seq.num_preemptions += 1
         out = SchedulerOutput(decodes=[self._seqs[i] for i in self._dec_ids[:st.n_decodes].tolist()])
         running = self._status.RUNNING
+        out.prefill_tokens = self._pre_new[:st.n_prefills].tolist()
         for i, slot, cached in zip(self._pre_ids[:st.n_prefills].tolist(), self._pre_slots[:st.n_prefills].tolist(),
                                    self._pre_cached[:st.n_prefills].tolist()):
             seq = self._seqs[i]
-            seq.slot = slot
-            seq.num_cached_tokens = cached
-            seq.status = running
+            if seq.status is not running:  # admitted now (a chunked prefill already running keeps its own)
+                seq.slot = slot
+                seq.num_cached_tokens = cached
+                seq.status = running
             out.prefills.append(seq)
         return out
 

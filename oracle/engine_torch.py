@@ -233,3 +233,38 @@ def serve(model: TorchQwen2, cache: TorchPagedCache, requests: Sequence[tuple[Se
                     record(s, row)
                 sched.append_token(s, int(row.argmax()), now)
     return seqs
+
+
+def serve_bookkeeping(cache: OracleBlockManager, requests: Sequence[tuple[Sequence[int], int]], max_num_seqs: int,
+                      max_num_batched_tokens: int, max_model_len: int, token: int = 0) -> list[OracleSequence]:
+    """The allocator side of :func:`serve` alone, every sampled token being ``token``.
+
+    With EOS ignored and no preemption the scheduler's decisions, the block tables and
+    ``prefix_hit_tokens`` do not depend on the tokens (prefix keys come from the prompts),
+    so this gives the reference's exact admissions and prefix hits for a workload without
+    running a model.
+    """
+    sched = OracleScheduler(max_num_seqs, max_num_batched_tokens, max_model_len, cache)
+    seqs = [OracleSequence(i, list(p), OracleSampling(max_tokens=m, ignore_eos=True)) for i, (p, m) in enumerate(requests)]
+    for s in seqs:
+        sched.add(s)
+    while sched.has_work():
+        step = sched.schedule()
+        news = {s.seq_id: s.token_ids[cache.lengths[s.slot]:] for s in step.prefills}
+        for group in pack_by_budget([len(news[s.seq_id]) for s in step.prefills], max_num_batched_tokens):
+            group_seqs = [step.prefills[i] for i in group]
+            starts = [cache.lengths[s.slot] for s in group_seqs]
+            for s, a in zip(group_seqs, starts):  # PackedPrefillContext: room, then commit
+                if not cache.ensure_capacity(s.slot, a + len(news[s.seq_id])):
+                    raise ValueError("no room in the KV cache")
+            for s, a in zip(group_seqs, starts):
+                cache.lengths[s.slot] = a + len(news[s.seq_id])
+            for s in group_seqs:
+                cache.register_prefix(s.slot, s.token_ids)
+            for s in group_seqs:
+                sched.append_token(s, token, 0.0)
+        for s in step.decodes:  # PagedDecodeContext.commit
+            cache.lengths[s.slot] += 1
+        for s in step.decodes:
+            sched.append_token(s, token, 0.0)
+    return seqs

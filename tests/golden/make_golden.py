@@ -41,8 +41,10 @@ Ham12-3/mini-inference (pure Python + PyTorch, run on the CPU) and records:
   configuration 1 draws them: the generated tokens of every request and, for every sampled
   row, its 32 largest logits (ids and values). ``0p5b`` is configuration 1 itself (the
   Qwen2.5-0.5B shape); ``0p5b_unit_norms`` the same draws with the RMSNorm weights then set
-  to 1 (their own initial value), which makes the tokens depend on the context; ``small`` a
-  2-layer model for the CPU check of the oracle's engine.
+  to 1 (their own initial value), which makes the tokens depend on the context;
+  ``0p5b_prefix`` the latter with prefix caching on 12 prompts that share a 96-token prefix
+  under a 256-token step budget (it records the cache's ``prefix_hit_tokens`` and each
+  request's cached tokens); ``small`` a 2-layer model for the CPU check of the oracle's engine.
 
 The reference does not travel with this repository, so the fixtures are
 committed and this script is only rerun by hand.
@@ -451,13 +453,19 @@ def make_scheduler_traces(Scheduler, Sequence, SamplingParams, PagedKVCache) -> 
     (HERE / "scheduler_traces.json").write_text(json.dumps(traces))
 
 
-# (name, layers, hidden, intermediate, vocab, heads, kv heads, head_dim, requests, prompt lengths, tokens,
-#  unit norms, std)
-STREAM_CASES = [
-    ("0p5b", 24, 896, 4864, 151936, 14, 2, 64, 8, (64, 256), 64, False, 0.02),
-    ("0p5b_unit_norms", 24, 896, 4864, 151936, 14, 2, 64, 8, (64, 256), 64, True, 0.02),
-    ("small", 2, 256, 512, 1000, 14, 2, 64, 4, (8, 40), 16, True, 0.1),
-]
+# Shapes: (layers, hidden, intermediate, vocab, heads, kv heads, head_dim).
+_0P5B = (24, 896, 4864, 151936, 14, 2, 64)
+STREAM_CASES = {
+    # configuration 1: 8 prompts of U{64..256} ids, 64 greedy tokens
+    "0p5b": dict(shape=_0P5B, requests=8, lengths=(64, 256), tokens=64, unit_norms=False, std=0.02),
+    "0p5b_unit_norms": dict(shape=_0P5B, requests=8, lengths=(64, 256), tokens=64, unit_norms=True, std=0.02),
+    # prefix caching: 12 prompts = one shared 96-token prefix + U{8..40} own ids, a 256-token
+    # budget so that admissions spread over steps (the first ones miss, later ones hit)
+    "0p5b_prefix": dict(shape=_0P5B, requests=12, lengths=(8, 40), tokens=32, unit_norms=True, std=0.02,
+                        prefix=96, caching=True, budget=256),
+    "small": dict(shape=(2, 256, 512, 1000, 14, 2, 64), requests=4, lengths=(8, 40), tokens=16, unit_norms=True,
+                  std=0.1),
+}
 TOPK = 32
 
 
@@ -466,9 +474,13 @@ def make_greedy_streams(engine_model, engine_engine, engine_scheduler, engine_sa
     """Greedy streams of the reference's model and engine loop (float32, CPU)."""
     from types import SimpleNamespace
 
-    for name, layers, hidden, inter, vocab, hq, hkv, d, n_req, (lo, hi), n_tok, unit_norms, std in STREAM_CASES:
+    for name, case in STREAM_CASES.items():
         if only and name != only:
             continue
+        layers, hidden, inter, vocab, hq, hkv, d = case["shape"]
+        n_req, (lo, hi), n_tok = case["requests"], case["lengths"], case["tokens"]
+        unit_norms, std, prefix_len = case["unit_norms"], case["std"], case.get("prefix", 0)
+        caching, budget = case.get("caching", False), case.get("budget", 4096)
         cfg = engine_model.Qwen2Config(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter,
                                        num_layers=layers, num_heads=hq, num_kv_heads=hkv, head_dim=d,
                                        rms_norm_eps=1e-6, rope_theta=1e6, max_position_embeddings=32768,
@@ -482,13 +494,16 @@ def make_greedy_streams(engine_model, engine_engine, engine_scheduler, engine_sa
                     prm.fill_(1.0)
         model = model.eval()
         g = torch.Generator().manual_seed(0)
+        shared = torch.randint(0, vocab, (prefix_len,), generator=g).tolist()
         lens = torch.randint(lo, hi + 1, (n_req,), generator=g).tolist()
-        prompts = [torch.randint(0, vocab, (n,), generator=g).tolist() for n in lens]
-        max_len = hi + n_tok + 16
+        prompts = [shared + torch.randint(0, vocab, (n,), generator=g).tolist() for n in lens]
+        lens = [len(p) for p in prompts]
+        max_len = prefix_len + hi + n_tok + 16
         cache = PagedKVCache.for_model(cfg, num_blocks=n_req * (max_len // 16 + 1), block_size=16, max_seqs=n_req,
-                                       max_len=max_len, dtype=torch.float32, device="cpu")
+                                       max_len=max_len, dtype=torch.float32, device="cpu",
+                                       enable_prefix_caching=caching)
         runner = engine_engine.ModelRunner(model, cache)
-        conf = SimpleNamespace(max_num_seqs=n_req, max_num_batched_tokens=4096, max_model_len=max_len,
+        conf = SimpleNamespace(max_num_seqs=n_req, max_num_batched_tokens=budget, max_model_len=max_len,
                                scheduling="continuous")
         sched = engine_scheduler.Scheduler(conf, cache)
         sampler = engine_sampler.Sampler(0, "cpu")
@@ -509,7 +524,7 @@ def make_greedy_streams(engine_model, engine_engine, engine_scheduler, engine_sa
             while sched.has_work():  # LLMEngine.step (engine/engine.py:281-312)
                 batch = sched.schedule()
                 new_of = {s.seq_id: s.token_ids[cache.lengths[s.slot]:] for s in batch.prefills}
-                for group in engine_engine.pack_by_budget([len(new_of[s.seq_id]) for s in batch.prefills], 4096):
+                for group in engine_engine.pack_by_budget([len(new_of[s.seq_id]) for s in batch.prefills], budget):
                     gs = [batch.prefills[i] for i in group]
                     logits = runner.prefill_packed([s.slot for s in gs], [new_of[s.seq_id] for s in gs])
                     for s in gs:
@@ -529,8 +544,11 @@ def make_greedy_streams(engine_model, engine_engine, engine_scheduler, engine_sa
             std=np.array(std), seed=np.array(0), max_model_len=np.array(max_len),
             prompt_lens=np.array(lens, np.int64), prompt_ids=np.array(flat, np.int64),
             tokens=np.array([s.output_token_ids for s in seqs], np.int64), top_ids=top_ids, top_vals=top_vals,
-            threads=np.array(torch.get_num_threads()))
-        print(name, "distinct tokens per stream:", [len(set(s.output_token_ids)) for s in seqs])
+            threads=np.array(torch.get_num_threads()), prefix_caching=np.array(caching), budget=np.array(budget),
+            prefix_hit_tokens=np.array(cache.prefix_hit_tokens),
+            cached_tokens=np.array([s.num_cached_tokens for s in seqs], np.int64))
+        print(name, "distinct tokens per stream:", [len(set(s.output_token_ids)) for s in seqs],
+              "prefix hit tokens:", cache.prefix_hit_tokens)
 
 
 def main() -> None:

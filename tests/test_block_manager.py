@@ -241,3 +241,58 @@ def test_journal_records_table_edits_for_the_device_mirror():
     assert m.ensure_capacity(a, 16) and m.ensure_capacity(b, 8)  # one new block each
     n, ovf = m.drain_edits(small)
     assert n == 1 and ovf
+
+
+def test_fork_shares_every_block_and_copy_on_write_unshares_only_what_is_written():
+    """No reference counterpart (it never writes a shared block); host-side rules of fork + prepare_write."""
+    from mini_inference_b200.cache import NativeBlockManager
+
+    bm = NativeBlockManager(num_blocks=8, block_size=4, max_seqs=4, max_len=32)
+    a = bm.allocate(10)  # 3 blocks, the last holding 2 tokens
+    bm.set_length(a, 10)
+    b = bm.fork(a)
+    assert bm.table(b) == bm.table(a) and bm.get_length(b) == 10
+    refs = bm.ref_counts()
+    assert all(refs[x] == 2 for x in bm.table(a))
+    free_before = bm.num_free_blocks
+    # Writing tokens 10..13 of b touches blocks 2 and 3 of its table; only block 2 exists and is shared.
+    assert bm.ensure_capacity(b, 14)
+    pairs = bm.prepare_write(b, 10, 4)
+    old_a = bm.table(a)
+    assert len(pairs) == 1 and pairs[0][0] == old_a[2] and pairs[0][1] not in old_a
+    assert bm.table(b)[:2] == old_a[:2] and bm.table(b)[2] == pairs[0][1]
+    assert bm.ref_counts()[old_a[2]] == 1  # now a's alone
+    assert bm.num_free_blocks == free_before - 2  # one block for position 12+, one copy
+    assert bm.prepare_write(a, 10, 1) == []  # a's block 2 is no longer shared
+    bm.free(b)
+    assert all(bm.ref_counts()[x] == 1 for x in old_a)
+    bm.free(a)
+    assert bm.num_free_blocks == 8
+
+
+def test_copy_on_write_without_room_changes_nothing():
+    from mini_inference_b200.cache import NativeBlockManager
+
+    bm = NativeBlockManager(num_blocks=2, block_size=4, max_seqs=3, max_len=16)
+    a = bm.allocate(6)  # both blocks
+    bm.set_length(a, 6)
+    b = bm.fork(a)
+    with pytest.raises(RuntimeError, match="not enough free KV cache blocks"):
+        bm.prepare_write(b, 6, 1)
+    assert bm.table(b) == bm.table(a) and bm.ref_counts() == [2, 2]
+
+
+def test_fork_needs_the_copy_on_write_cache():
+    import torch
+
+    from mini_inference_b200 import PagedKVCache
+
+    cache = PagedKVCache(1, 1, 4, num_blocks=4, block_size=4, max_seqs=2, max_len=16, dtype=torch.float16,
+                         device="cpu")
+    s = cache.allocate(3)
+    with pytest.raises(RuntimeError, match="enable_copy_on_write"):
+        cache.fork(s)
+    cow = PagedKVCache(1, 1, 4, num_blocks=4, block_size=4, max_seqs=2, max_len=16, dtype=torch.float16,
+                       device="cpu", enable_copy_on_write=True)
+    s = cow.allocate(3)
+    assert cow.block_tables[cow.fork(s)] == cow.block_tables[s]

@@ -39,7 +39,8 @@ def test_reset_workspace_then_decode_matches_a_fresh_workspace(dev):
     status = torch.zeros(2, dtype=torch.int32, device=dev)
     got = ops.decode_attention(pool, 1, tables, qs[0], ctx_lens, stale, status=status[0:1])
     want = ops.decode_attention(pool, 1, tables, qs[0], ctx_lens, fresh, status=status[1:2])
-    ops.raise_device_errors(status)
+    ops.raise_device_errors(status[0:1])
+    ops.raise_device_errors(status[1:2])
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 

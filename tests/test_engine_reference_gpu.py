@@ -6,6 +6,11 @@ Qwen2.5-0.5B shape, seeded as the task's configuration 1 (``manual_seed(0)``, th
 ``Scheduler`` and greedy ``Sampler`` in float32 on the CPU: 8 prompts of 64..256 uniform
 token ids, 64 greedy tokens each, and the 32 largest logits of every sampled row.
 
+``0p5b_prefix`` is the same model (RMSNorm weights set to 1) serving 12 prompts that share a
+96-token prefix with prefix caching on, under a 256-token step budget: some requests miss
+and some hit, and the reference's ``prefix_hit_tokens`` and per-request cached tokens are
+recorded; they must be equal here exactly.
+
 Here the same weights (drawn the same way, cast to float16) run through ``LLMEngine``:
 the native scheduler, the paged cache with RoPE fused into the append, tcgen05 prefill,
 split-K paged decode replayed as CUDA graphs, and the LM head fused with argmax. Every
@@ -53,8 +58,11 @@ def last_logits(model, tokens, dev):
     return out
 
 
-@pytest.mark.parametrize("case", ["0p5b", "0p5b_unit_norms"])
-def test_greedy_streams_equal_the_reference_model(dev, golden_dir, case):
+@pytest.mark.parametrize("case,chunk", [("0p5b", 0), ("0p5b_unit_norms", 0), ("0p5b_prefix", 0),
+                                        ("0p5b_unit_norms", 48)])
+def test_greedy_streams_equal_the_reference_model(dev, golden_dir, case, chunk):
+    """``chunk`` > 0: the same requests with chunked prefill under a budget of that many tokens
+    (every prompt is longer), which the reference does not have: same tokens, same tie rule."""
     from mini_inference_b200.engine import EngineConfig, LLMEngine, SamplingParams
     from mini_inference_b200.model import Qwen2Config, Qwen2Model, init_random
 
@@ -65,10 +73,19 @@ def test_greedy_streams_equal_the_reference_model(dev, golden_dir, case):
                                         unit_norms=bool(z["unit_norms"])))
     n_tok = z["tokens"].shape[1]
     max_len = int(z["max_model_len"])
+    caching = bool(z["prefix_caching"])
     engine = LLMEngine(model, EngineConfig(max_num_seqs=len(prompts), max_model_len=max_len,
-                                           max_num_batched_tokens=4096, kv_cache_tokens=len(prompts) * (max_len + 16)))
+                                           max_num_batched_tokens=chunk or int(z["budget"]),
+                                           kv_cache_tokens=len(prompts) * (max_len + 16),
+                                           enable_prefix_caching=caching, chunked_prefill=chunk > 0))
     seqs = engine.generate(prompts, SamplingParams(max_tokens=n_tok, ignore_eos=True))
     ref = z["tokens"]
+    if chunk:
+        assert any(st.num_prefill_tokens and st.num_prefill_tokens <= chunk for st in engine.step_stats)
+        assert sum(1 for st in engine.step_stats if st.num_prefills) > len(prompts) * 64 // chunk // 2
+    else:  # the same admissions, the same prefix hits (exact), whatever the tokens
+        assert engine.cache.prefix_hit_tokens == int(z["prefix_hit_tokens"])
+        assert [s.num_cached_tokens for s in seqs] == z["cached_tokens"].tolist()
 
     def noise_at(b, t, ours):
         """max |reference - ours| over the reference's recorded top logits of stream b, step t."""

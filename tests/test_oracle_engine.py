@@ -57,3 +57,18 @@ def test_oracle_engine_reproduces_the_reference_streams(golden_dir):
         for j in range(n_tok):
             row = seen[(b, j)]
             np.testing.assert_allclose(row[z["top_ids"][b, j]].numpy(), z["top_vals"][b, j], rtol=1e-5, atol=1e-6)
+
+
+def test_bookkeeping_replay_gives_the_reference_prefix_hits(golden_dir):
+    """Scheduling and prefix hits without a model: the reference's recorded hits, request by request."""
+    from oracle.block_manager import OracleBlockManager
+    from oracle.engine_torch import serve_bookkeeping
+
+    z, _, prompts = stream_case(golden_dir, "0p5b_prefix")
+    max_len = int(z["max_model_len"])
+    cache = OracleBlockManager(len(prompts) * (max_len // 16 + 1), 16, len(prompts), max_len,
+                               enable_prefix_caching=True)
+    seqs = serve_bookkeeping(cache, [(p, z["tokens"].shape[1]) for p in prompts], len(prompts), int(z["budget"]),
+                             max_len)
+    assert cache.prefix_hit_tokens == int(z["prefix_hit_tokens"]) > 0
+    assert [s.num_cached_tokens for s in seqs] == z["cached_tokens"].tolist()

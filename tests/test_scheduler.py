@@ -157,3 +157,58 @@ def test_needs_the_native_cache():
     with pytest.raises(TypeError):
         Scheduler(SimpleNamespace(max_num_seqs=4, max_num_batched_tokens=64, max_model_len=32,
                                   scheduling="continuous"), OracleBlockManager(8, 4, 4, 32))
+
+
+def _chunked_engine_loop(prompts, budget, max_seqs=4, blocks=64, max_tokens=3):
+    """The engine's side of chunked prefill on the allocator alone: returns per step
+    (prefills as (id, start, count, final), decode ids)."""
+    from mini_inference_b200 import PagedKVCache
+    from mini_inference_b200.scheduler import Scheduler, SequenceStatus
+
+    cache = PagedKVCache(num_layers=1, num_kv_heads=1, head_dim=4, num_blocks=blocks, block_size=16,
+                         max_seqs=max_seqs, max_len=512, dtype=torch.float32, device="cpu")
+    sched = Scheduler(SimpleNamespace(max_num_seqs=max_seqs, max_num_batched_tokens=budget, max_model_len=512,
+                                      scheduling="continuous", chunked_prefill=True), cache)
+    seqs = [Seq(i, list(p), Sampling(max_tokens, True), status=SequenceStatus.WAITING) for i, p in enumerate(prompts)]
+    for s in seqs:
+        sched.add(s)
+    log = []
+    while sched.has_work():
+        out = sched.schedule()
+        step = []
+        done = []
+        for s, n in zip(out.prefills, out.prefill_tokens):
+            a = cache.lengths[s.slot]
+            cache.lengths[s.slot] = a + n
+            final = a + n == s.num_tokens
+            step.append((s.seq_id, a, n, final))
+            if final:
+                done.append(s)
+        sched.append_tokens(done, [7] * len(done), 0.0)
+        for s in out.decodes:
+            cache.lengths[s.slot] += 1
+        sched.append_tokens(out.decodes, [7] * len(out.decodes), 0.0)
+        log.append((step, [s.seq_id for s in out.decodes]))
+        assert len(log) < 100
+    return log, seqs
+
+
+def test_chunked_prefill_splits_prompts_under_the_budget():
+    log, seqs = _chunked_engine_loop([list(range(150)), list(range(1000, 1030))], budget=64)
+    assert log[0] == ([(0, 0, 64, False)], [])  # the long prompt takes the whole budget
+    assert log[1] == ([(0, 64, 64, False)], [])
+    assert log[2] == ([(0, 128, 22, True), (1, 0, 30, True)], [])  # its rest, then the next admission
+    assert log[3] == ([], [0, 1])  # both decode from here on
+    assert all(len(s.output_token_ids) == 3 for s in seqs)
+
+
+def test_chunked_prefill_runs_decodes_first_and_finishes_a_one_token_tail_by_decode():
+    # Budget 33 with one decode running: the new 40-token prompt gets 32, then 8 minus the decode's share.
+    log, seqs = _chunked_engine_loop([list(range(20)), list(range(500, 540))], budget=33, max_tokens=4)
+    assert log[0][0] == [(0, 0, 20, True), (1, 0, 13, False)]
+    assert log[1] == ([(1, 13, 27, True)], [0])
+    for step, decodes in log:
+        assert sum(n for _, _, n, _ in step) + len(decodes) <= 33
+    # A 33-token prompt under a 32-token budget leaves one token, which the next step decodes.
+    log, _ = _chunked_engine_loop([list(range(33))], budget=32, max_tokens=2)
+    assert log[0] == ([(0, 0, 32, False)], []) and log[1] == ([], [0])

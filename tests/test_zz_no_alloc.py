@@ -125,7 +125,8 @@ def test_static_reset_clears_stale_tickets(dev):
     status = torch.zeros(2, dtype=torch.int32, device=dev)
     got = ops.decode_attention_static(pool, 0, tables, qs[1], ctx_lens, out, status=status[0:1])
     want = ops.decode_attention(pool, 0, tables, qs[1], ctx_lens, ws, status=status[1:2])
-    ops.raise_device_errors(status)
+    ops.raise_device_errors(status[0:1])
+    ops.raise_device_errors(status[1:2])
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 
