@@ -661,7 +661,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     del g_step, g_attn, k_pool, v_pool
     serving = None
     prefix_serving = None
-    if not args.profile_case and not args.no_serving:  # every rank serves its share of configs 3 and 4
+    if not args.profile_case and not args.no_serving and not args.decode_only:  # every rank: configs 3 and 4
         with ClockSampler(local) as serve_clocks:
             serving, model = run_serving(args, rank, world, local)
             prefix_serving = run_prefix_serving(args, rank, world, local, model)
@@ -696,6 +696,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     }
     if args.profile_case:  # no end-to-end leg in the capture case
         line["e2e"] = None
+    elif args.decode_only:
+        pass
     else:
         line["prefill"] = run_prefill(dev, seed=rank)
         line["long_context"] = run_long_context(dev, seed=rank)
@@ -704,7 +706,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         line["scheduler"] = run_scheduler(seed=rank)
         line["serving"] = serving
         line["prefix_serving"] = prefix_serving
-    if world == 1 and not args.profile_case:
+    if world == 1 and not args.profile_case and not args.decode_only:
         line["cpu_baseline"] = cpu_baseline(args)
     return line
 
@@ -1184,6 +1186,8 @@ def main() -> None:
     ap.add_argument("--serving-cpu-budget", type=float, default=20.0, help="seconds for the CPU serving sample")
     ap.add_argument("--serving-check", action="store_true", help="check device errors after every serving run")
     ap.add_argument("--no-serving", action="store_true", help="skip the config-3 serving leg")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the config-2 decode step and its e2e leg (no other legs, no CPU baseline)")
     ap.add_argument("--serving-only", action="store_true",
                     help="only the config-3 serving leg (under torchrun: every rank its share)")
     ap.add_argument("--profile-case", action="store_true",

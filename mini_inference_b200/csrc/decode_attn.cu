@@ -6,33 +6,40 @@
 // (engine/model.py:126-147). Here nothing is gathered: K/V blocks are read in
 // place through the block table, each exactly once, straight into shared memory.
 //
-// Work split. An "item" is one sequence: its K/V blocks (all KV heads) and its
-// query heads. A CTA takes one unit of work, an item or a chunk of one, and
-// streams its blocks once. Items longer than
-//   cap = max(kMinCap, ceil(T / max(C - I, C / 4)))
-// blocks (T: the batch's blocks, C: CTAs, I: items) are cut into ceil(n / cap)
-// balanced chunks of consecutive blocks, so that, when the items allow it, all units
-// fit one wave of CTAs and no unit is much longer than the mean. Every CTA derives
-// the same split from context_lens in its prologue; with more units than CTAs, CTA
-// g takes units g, g + C, ... The CTA that finishes the last chunk of an item (an
-// atomic ticket per item; no CTA waits for another) merges the chunks' partial
-// softmax states in chunk order, so the result does not depend on which CTA came
-// last.
+// Work split. A CTA streams an ordered list of segments, each a run of consecutive
+// blocks of one sequence. Every CTA derives the split from context_lens in its prologue
+// (which, with PKV_DECODE_INPUTS_READY, runs before it waits for the previous kernel),
+// by one of two rules:
+//  * long ranges (at least kFlatMin blocks per CTA on average): the batch's blocks are
+//    laid end to end and cut into equal ranges of ceil(T / C) blocks, one per CTA (T
+//    blocks, C CTAs). Every CTA streams the same bytes whatever the mix of lengths; its
+//    range covers the tail of one sequence, whole sequences and the head of another, and
+//    holds at most two cut pieces (its first and its last).
+//  * short ranges: sequences longer than cap = max(kMinCap, ceil(T / max(C - I, C / 4)))
+//    blocks (I: sequences) are cut into ceil(n / cap) balanced chunks so that all units
+//    fit one wave when the batch allows, and CTA g takes units g, g + C, ... Units then
+//    differ in length, and the CTAs that finish early make room for the next launch's
+//    CTAs, which fill their rings while this launch ends; with equal ranges every CTA
+//    would end at once and nothing of the next launch could start early (measured slower
+//    at 64 sequences of 128..2048 tokens, faster at 8..32 K tokens).
+// A sequence cut into several segments leaves one partial softmax state per segment; the
+// CTA that takes the sequence's last ticket merges them in segment order, so the result
+// does not depend on which CTA came last.
 //
-// Inside a CTA one producer warp resolves block ids through the block table (32
-// at a time, one lookup per lane, the next 32 already in flight) and keeps a ring
-// of stages full with TMA copies of a block's K and V for all KV heads at once
-// (adjacent in the pool: 4 KB per tensor at 2 heads x d 64; 128B swizzle, L2
-// evict-first). kIssueLanes lanes issue the copies of consecutive blocks with one
-// instruction. The 8 consumer warps split the KV heads (8 / Hkv warps per head);
-// block j goes, for every head, to warp j % (8 / Hkv) of that head through stage
-// j % S (S a multiple of 8 / Hkv), so each warp waits on every phase of its stages
-// in turn (an mbarrier parity wait cannot tell a phase from the one two later).
-// Each consumer runs the 16-key flash step on mma.sync m16n8k16 with the M = 16
-// rows being its head's GQA group of query heads (the reference regroups head h to
-// (h / group, h % group) the same way), so a tile read from HBM serves the whole
-// group (attn_tile.cuh). At the end of a unit the warps of a head merge their
-// softmax states through shared memory.
+// Inside a CTA one producer warp resolves block ids through the block table (32 at a
+// time, one lookup per lane, the next 32 in flight) and keeps a ring of stages full
+// with TMA copies of a block's K and V for all KV heads at once (adjacent in the pool;
+// 128B swizzle, L2 evict-first); kIssueLanes lanes issue the copies of consecutive
+// blocks with one instruction. The 8 consumer warps split the KV heads
+// (8 / Hkv warps per head); the CTA's j-th block goes, for every head, to warp
+// j % (8 / Hkv) of that head through stage j % S (S a multiple of 8 / Hkv), so each warp
+// waits on every phase of its stages in turn (an mbarrier parity wait cannot tell a
+// phase from the one two later). Each consumer runs the 16-key flash step on mma.sync
+// m16n8k16 with the M = 16 rows being its head's GQA group of query heads (the reference
+// regroups head h to (h / group, h % group) the same way), so a tile read from HBM serves
+// the whole group (attn_tile.cuh). At the end of a segment the warps of a head merge
+// their softmax states through shared memory and write the output (a whole sequence) or
+// the segment's partial state.
 #include <algorithm>
 #include <cstdlib>
 
@@ -46,11 +53,12 @@ constexpr int kBS = 16;  // tokens per block handled by this kernel
 constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
 constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared memory
-constexpr int kMinCap = 16;        // items of up to 16 blocks are never split
-constexpr int kLongUnit = 256;     // blocks per CTA above which the split cap is tightened
+constexpr int kMinCap = 16;        // chunks: sequences of up to 16 blocks are never cut
+constexpr int kFlatMin = 128;      // blocks per CTA from which the ranges are equal
+constexpr int kMinQuota = 4;       // equal ranges: never fewer blocks per CTA than this
 constexpr int kIssueLanes = 4;     // producer lanes issuing copies together
-constexpr int kMergeBatch = 4;     // chunk states a merging thread loads at once
-constexpr int kMaxPending = 32;    // split units of one CTA whose tickets are taken at the end
+constexpr int kMergeBatch = 4;     // segment states a merging thread loads at once
+constexpr int kMaxPending = 32;    // cut segments of one CTA whose tickets are taken at the end
 constexpr int kTicketBatch = 8;    // tickets thread 0 keeps in flight at once
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -62,7 +70,7 @@ template <int D, int NH, int RK> struct DecodeShape {
   static constexpr int DP = D + 4;                     // padded combine row (no bank conflicts)
   static constexpr int WARP_STATE = 2 * RK + RK * DP;  // floats: m[RK], l[RK], O[RK][DP]
   static constexpr int COMB = kNC * WARP_STATE * 4;
-  static constexpr int TABLES = 4 * (kMaxBatch + 1) * 4;  // context lengths, table rows, unit and split prefixes
+  static constexpr int TABLES = 4 * (kMaxBatch + 1) * 4;  // lengths, table rows, two prefix sums
   static constexpr int FIXED = 1024 + COMB + TABLES + 256;
   // Two CTAs per SM when each consumer warp keeps 2+ stages in half the shared memory,
   // else one CTA with up to 4 stages per warp.
@@ -72,7 +80,7 @@ template <int D, int NH, int RK> struct DecodeShape {
   static constexpr int PW = TWO ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > 4 ? 4 : PW_FULL);
   static constexpr int S = WPH * PW;
   static constexpr int RING = 2 * S * STAGE;
-  static constexpr int SMEM = 1024 + RING + COMB + 2 * S * 8 + TABLES;
+  static constexpr int SMEM = 1024 + RING + COMB + TABLES + 2 * S * 8;
   static constexpr int MIN_BLOCKS = TWO ? 2 : 1;
   static_assert(PW >= 1, "ring too shallow");
 };
@@ -89,11 +97,12 @@ struct DecodeParams {
   const int32_t* seq_rows;
   const int32_t* context_lens;
   int32_t* status;
-  int32_t* counters;  // [kMaxBatch] chunks of each item finished so far
-  float* partials;    // [max_slots][NH][RK][D + 4]: (m, l, pad, pad, O) per row of a chunk
+  int32_t* counters;  // [kMaxBatch] segments of each sequence finished so far
+  float* partials;    // [max_slots][NH][RK][D + 4]: (m, l, pad, pad, O) per row of a segment
   int64_t out_sb, out_sh, q_sb, q_sh, kv_sb, kv_sh, table_stride;
   int32_t table_rows, table_cols;
   int32_t batch, group, kv_heads, layer, nbt, inputs_ready, max_slots, cap_override;
+  int32_t flat_min, min_quota;
   float scale_log2;
 };
 
@@ -117,34 +126,92 @@ __device__ inline int warp_scan(int v, int lane) {
   return v;
 }
 
-struct Unit {
-  int b, c, nch, i0, i1;
-};
-
-// Smallest cap in [max(kMinCap, ceil(T / C)), cap] whose units (ceil(n / cap) per item of
-// n blocks) fit C CTAs, by binary search; `cap` itself if even it does not fit. Run by one
-// warp over the clamped context lengths.
-__device__ __noinline__ int tightest_cap(const int* sCtx, int B, int C, int cap, int lane) {
-  auto units_at = [&](int c) {
-    int u = 0;
-    for (int i = lane; i < B; i += 32) {
-      const int n = (sCtx[i] + kBS - 1) / kBS;
-      u += n == 0 ? 0 : (n <= c ? 1 : (n + c - 1) / c);
-    }
-    return warp_sum(u);
-  };
-  if (units_at(cap) > C) return cap;
-  int tiles = 0;
-  for (int i = lane; i < B; i += 32) tiles += (sCtx[i] + kBS - 1) / kBS;
-  int lo = max(kMinCap, (warp_sum(tiles) + C - 1) / C);
-  while (lo < cap) {
-    const int mid = (lo + cap) / 2;
-    if (units_at(mid) <= C) cap = mid; else lo = mid + 1;
+// Largest b in [lo, hi] with cum[b] <= k.
+__device__ inline int seq_of(const int* cum, int k, int lo, int hi) {
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cum[mid] <= k) lo = mid; else hi = mid - 1;
   }
-  return cap;
+  return lo;
 }
 
-template <typename T, int D, int NH, int RK>
+// One run of consecutive blocks [i0, i1) of sequence b. A cut one (parts > 1) is part
+// `part` of its sequence and keeps its partial state in `slot`.
+struct Seg {
+  int b, i0, i1, part, parts, slot;
+};
+
+// The CTA's segments in order, under either split (see the top of this file). sA holds
+// per-sequence prefix sums: of blocks (equal ranges) or of units (chunks); sB the prefix
+// sums of cut units (chunks only).
+template <bool FLAT_OK>
+struct SegIter {
+  const int* sA;
+  const int* sB;
+  const int* sCtx;
+  int B, C, g, flat, q, k0, k1, cur;  // cur: the last unit (chunks) or sequence (ranges) handed out
+  __device__ int blocks(int b) const { return (sCtx[b] + kBS - 1) / kBS; }
+  __device__ void start() {
+    if (FLAT_OK && flat) cur = k1 > k0 ? seq_of(sA, k0, 0, B - 1) - 1 : B;  // the sequence holding block k0, minus one
+    else cur = g - C;
+  }
+  __device__ bool next(Seg& s) {
+    if (FLAT_OK && flat) {
+      int b = cur + 1;
+      for (; b < B; ++b) {
+        if (sA[b] >= k1) return false;
+        if (sA[b + 1] > sA[b]) break;
+      }
+      if (b >= B) return false;
+      cur = b;
+      const int first = sA[b], last = sA[b + 1];
+      s.b = b;
+      s.i0 = max(first, k0) - first;
+      s.i1 = min(last, k1) - first;
+      const int f = first / q;
+      s.parts = (last - 1) / q - f + 1;
+      s.part = g - f;
+      // A CTA keeps its first segment's state in slot 2g and its last one's in 2g + 1.
+      s.slot = 2 * g + (first < k0 || (first == k0 && s.i1 == last - first) ? 0 : 1);
+      return true;
+    }
+    const int u = cur + C;
+    if (u >= sA[B]) return false;
+    cur = u;
+    const int b = seq_of(sA, u, 0, B - 1);  // the (non-empty) sequence owning unit u
+    const int nch = sA[b + 1] - sA[b], c = u - sA[b], n = blocks(b);
+    const int cs = (n + nch - 1) / nch;
+    s.b = b;
+    s.i0 = c * cs;
+    s.i1 = min(n, s.i0 + cs);
+    s.parts = nch;
+    s.part = c;
+    s.slot = sB[b] + c;
+    return true;
+  }
+  // Slot of part c of sequence b (for the merge).
+  __device__ int slot_of(int b, int c) const {
+    if (!FLAT_OK || !flat) return sB[b] + c;
+    const int first = sA[b], f = first / q;
+    return c == 0 ? 2 * f + (first == f * q ? 0 : 1) : 2 * (f + c);
+  }
+};
+
+template <typename T, int D>
+__device__ inline void load_q(uint32_t (&qa)[D / 16][4], const T* qb, int64_t q_sh, int G, int g_lane, int t4) {
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int c0 = kk * 16 + 2 * t4;
+    qa[kk][0] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * q_sh + c0) : 0u;
+    qa[kk][1] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * q_sh + c0) : 0u;
+    qa[kk][2] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * q_sh + c0 + 8) : 0u;
+    qa[kk][3] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * q_sh + c0 + 8) : 0u;
+  }
+}
+
+// FLAT_OK: the launch may take equal ranges (the host's bound on the batch's blocks
+// reaches the threshold); without it the chunk rule is compiled alone.
+template <typename T, int D, int NH, int RK, bool FLAT_OK>
 __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                   const DecodeParams p) {
@@ -152,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   constexpr int TILE = S::TILE, STAGE = S::STAGE, NS = S::S, WPH = S::WPH, DP = S::DP, WS = S::WARP_STATE;
   constexpr int LANES = kIssueLanes < NS ? kIssueLanes : NS;  // the copies of one issue use distinct stages
   constexpr int ROW = D + 4;            // partial row: m, l, 2 pad floats, O[D] (O 16-byte aligned)
-  constexpr int SLOT = NH * RK * ROW;   // floats of one chunk's partial state (all heads)
+  constexpr int SLOT = NH * RK * ROW;   // floats of one segment's partial state (all heads)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring_k = smem;
@@ -162,10 +229,10 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   uint64_t* empty = full + NS;
   int* sCtx = reinterpret_cast<int*>(empty + NS);  // [batch] clamped context lengths
   int* sRow = sCtx + kMaxBatch + 1;                // [batch] block-table row of each sequence
-  int* sPU = sRow + kMaxBatch + 1;                 // [batch + 1] units (per KV head) before sequence b
-  int* sPS = sPU + kMaxBatch + 1;                  // [batch + 1] split units (per KV head) before b
-  __shared__ int s_bad, s_npend;
-  __shared__ int4 s_pend[kMaxPending];  // (sequence, chunks, first slot, -) of split units
+  int* sA = sRow + kMaxBatch + 1;                  // [batch + 1] blocks (ranges) or units (chunks) before b
+  int* sB = sA + kMaxBatch + 1;                    // [batch + 1] cut units before b (chunks)
+  __shared__ int s_bad, s_npend, s_flat, s_q, s_total;
+  __shared__ int2 s_pend[kMaxPending];  // (sequence, parts) of cut segments
   __shared__ int s_last[kMaxPending];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -208,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     s_npend = 0;
   }
   __syncthreads();
-  if (warp == 0) {  // the split: cap, then per-sequence unit counts and their prefix sums
+  if (warp == 0) {  // the split: which rule, then its per-sequence prefix sums
     int tiles = 0, items = 0;
     for (int i = lane; i < B; i += 32) {
       const int n = (sCtx[i] + kBS - 1) / kBS;
@@ -217,65 +284,55 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     }
     tiles = warp_sum(tiles);
     items = warp_sum(items);
+    const int flat = FLAT_OK && p.cap_override <= 0 && tiles >= p.flat_min * C;
     const int free_ctas = max(C - items, max(C / 4, 1));
-    int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
-    // The cap above budgets a whole extra chunk per item, which can leave CTAs without a
-    // unit. When units are long (more than kLongUnit blocks per CTA on average) the merges
-    // are cheap next to the streaming, so the smallest cap whose units still fit one wave
-    // is taken instead: every SM streams. (For short units the extra merges cost more than
-    // the shorter longest unit saves, measured; the search stays out of line for them.)
-    if (p.cap_override <= 0 && tiles > kLongUnit * C) cap = tightest_cap(sCtx, B, C, cap, lane);
-    int carry_u = 0, carry_s = 0;
+    const int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
+    int carry_a = 0, carry_b = 0;
     for (int base = 0; base < B; base += 32) {
       const int i = base + lane;
       const int n = i < B ? (sCtx[i] + kBS - 1) / kBS : 0;
       const int nch = n == 0 ? 0 : (n <= cap ? 1 : (n + cap - 1) / cap);
-      const int pu = warp_scan(nch, lane), ps = warp_scan(nch > 1 ? nch : 0, lane);
+      const int pa = warp_scan(flat ? n : nch, lane), pb = warp_scan(nch > 1 ? nch : 0, lane);
       if (i < B) {
-        sPU[i + 1] = carry_u + pu;
-        sPS[i + 1] = carry_s + ps;
+        sA[i + 1] = carry_a + pa;
+        sB[i + 1] = carry_b + pb;
       }
-      carry_u += __shfl_sync(0xffffffffu, pu, 31);
-      carry_s += __shfl_sync(0xffffffffu, ps, 31);
+      carry_a += __shfl_sync(0xffffffffu, pa, 31);
+      carry_b += __shfl_sync(0xffffffffu, pb, 31);
     }
-    if (lane == 0) sPU[0] = sPS[0] = 0;
+    if (lane == 0) {
+      sA[0] = sB[0] = 0;
+      s_flat = flat;
+      s_total = carry_a;
+      s_q = max(p.min_quota, (tiles + C - 1) / C);
+    }
   }
   __syncthreads();
-  const int U = sPU[B];
-  // Split units never exceed 2 * max(C - I, C / 4) <= 2 * C, the slots the host provides
-  // (with the built-in cap; an overriding cap may ask for more).
-  if (sPS[B] > p.max_slots) {
+  const int flat = s_flat, q = s_q;
+  // Cut units never exceed 2 * max(C - I, C / 4) <= 2 * C and cut ranges 2 * C, the slots
+  // the host provides (an overriding cap may ask for more).
+  if (!flat && sB[B] > p.max_slots) {
     if (tid == 0) report(p.status, PKV_ERR_WORKSPACE);
     return;
   }
-  auto unit_of = [&](int u) {
-    Unit r;
-    int lo = 0, hi = B - 1;  // largest b with sPU[b] <= u (a sequence with units)
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (sPU[mid] <= u) lo = mid; else hi = mid - 1;
-    }
-    r.b = lo;
-    r.nch = sPU[lo + 1] - sPU[lo];
-    r.c = u - sPU[lo];
-    const int n = (sCtx[lo] + kBS - 1) / kBS;
-    const int cs = (n + r.nch - 1) / r.nch;
-    r.i0 = r.c * cs;
-    r.i1 = min(n, r.i0 + cs);
-    return r;
-  };
+  SegIter<FLAT_OK> segs{sA, sB, sCtx, B, C, g, flat, q, 0, 0, 0};
+  if (flat) {
+    segs.k0 = min(s_total, g * q);
+    segs.k1 = min(s_total, segs.k0 + q);
+  }
 
   if (warp == kNC) {
     // ---------------------------------------------------------------- producer
+    Seg sg;
     const uint64_t pol = policy_evict_first();
     bool ok = true, waited = false;
     uint64_t deadline = 0;
-    int j = 0;  // tiles of this CTA issued so far
-    for (int u = g; u < U && ok; u += C) {
-      const Unit un = unit_of(u);
-      const int row = sRow[un.b];
-      auto lookup = [&](int i) -> int {  // block id of block i of the unit's sequence
-        if (i >= un.i1) return 0;
+    int j = 0;  // blocks of this CTA issued so far
+    segs.start();
+    while (ok && segs.next(sg)) {
+      const int row = sRow[sg.b];
+      auto lookup = [&](int i) -> int {  // block id of block i of the segment's sequence
+        if (i >= sg.i1) return 0;
         int blk = row >= 0 ? p.tables[row * p.table_stride + i] : p.nbt - 1;  // padding rows: scratch block
         if (blk < 0 || blk >= p.nbt) {
           report(p.status, PKV_ERR_OUT_OF_RANGE);
@@ -283,11 +340,11 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
         }
         return blk;
       };
-      int blk_next = lookup(un.i0 + lane);
-      for (int base = un.i0; base < un.i1 && ok; base += 32) {
+      int blk_next = lookup(sg.i0 + lane);
+      for (int base = sg.i0; base < sg.i1 && ok; base += 32) {
         const int blk_cur = blk_next;
         blk_next = lookup(base + 32 + lane);  // in flight while this batch is issued
-        const int cnt = min(32, un.i1 - base);
+        const int cnt = min(32, sg.i1 - base);
         for (int k0 = 0; k0 < cnt && ok; k0 += LANES) {
           const int blk = __shfl_sync(0xffffffffu, blk_cur, (k0 + lane) & 31);
           if (!waited && j + k0 + LANES > NS) {
@@ -333,24 +390,16 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     float* head_comb = comb + h * WPH * WS;
     float* cw_state = head_comb + w * WS;
     bool ok = true;
-    int j = 0;  // tiles of this CTA consumed so far (by all warps)
-    for (int u = g; u < U; u += C) {
-      const Unit un = unit_of(u);
-      const int b = un.b;
-      const int ctx = sCtx[b];
+    int j = 0;  // blocks of this CTA consumed so far (by all warps)
+    Seg sg;
+    segs.start();
+    while (segs.next(sg)) {
       // Q fragments of this head's query group (A operand, rows = query heads).
       uint32_t qa[D / 16][4];
-      {
-        const T* qb = reinterpret_cast<const T*>(p.q) + b * p.q_sb + (int64_t)h * G * p.q_sh;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int c0 = kk * 16 + 2 * t4;
-          qa[kk][0] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0) : 0u;
-          qa[kk][1] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0) : 0u;
-          qa[kk][2] = g_lane < G ? *reinterpret_cast<const uint32_t*>(qb + g_lane * p.q_sh + c0 + 8) : 0u;
-          qa[kk][3] = g_lane + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g_lane + 8) * p.q_sh + c0 + 8) : 0u;
-        }
-      }
+      load_q<T, D>(qa, reinterpret_cast<const T*>(p.q) + sg.b * p.q_sb + (int64_t)h * G * p.q_sh, p.q_sh, G, g_lane,
+                   t4);
+      const int b = sg.b;
+      const int ctx = sCtx[b];
       const int append_blk = p.k_new ? (ctx - 1) / kBS : -1;
       float m_r[2] = {-INFINITY, -INFINITY};
       float l_r[2] = {0.f, 0.f};
@@ -358,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
 #pragma unroll
       for (int jj = 0; jj < D / 8; ++jj) o[jj][0] = o[jj][1] = o[jj][2] = o[jj][3] = 0.f;
 
-      const int n_i = un.i1 - un.i0;
+      const int n_i = sg.i1 - sg.i0;
       for (int k = ((w - j) % WPH + WPH) % WPH; k < n_i; k += WPH) {
         const int jj = j + k, st = jj % NS;
         if (ok && !mbar_wait_until(&full[st], (jj / NS) & 1, deadline)) {
@@ -368,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
         if (ok) {
           uint8_t* kt = ring_k + st * STAGE + h * TILE;
           uint8_t* vt = ring_v + st * STAGE + h * TILE;
-          const int i = un.i0 + k;  // block index within the sequence
+          const int i = sg.i0 + k;  // block index within the sequence
           if (i == append_blk) {
             // Put the new row into the staged tiles and write it to the pool at slot_mapping[b].
             const int off = (ctx - 1) % kBS;
@@ -423,9 +472,8 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
         if (RK > 8) *reinterpret_cast<float2*>(&co[(g_lane + 8) * DP + col]) = make_float2(o[jj][2], o[jj][3]);
       }
       named_bar(1 + h, WPH * 32);
-      const bool whole = un.nch == 1;
-      const int slot = sPS[b] + un.c;  // of a chunk of a split item
-      float* part = p.partials + (int64_t)slot * SLOT + h * RK * ROW;
+      const bool whole = sg.parts == 1;
+      float* part = p.partials + (int64_t)sg.slot * SLOT + h * RK * ROW;
       T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)h * G * p.out_sh;
       for (int it = w * 32 + lane; it < G * (D / 2); it += WPH * 32) {
         const int r = it / (D / 2), col = 2 * (it % (D / 2));
@@ -451,16 +499,11 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
         }
       }
       if (!whole && warp == 0 && lane == 0) {
-        // A CTA holds at most ceil(U / C) units, U <= batch + (split units <= max_slots); the
-        // launcher refuses launches where that bound exceeds kMaxPending, so every split unit
-        // gets its ticket below and every counter returns to zero.
-        if (s_npend < kMaxPending) {
-          s_pend[s_npend++] = make_int4(b, un.nch, sPS[b], 0);
-        } else {
-          report(p.status, PKV_ERR_WORKSPACE);
-        }
+        // The launcher refuses launches where a CTA could hold more cut segments than this.
+        if (s_npend < kMaxPending) s_pend[s_npend++] = make_int2(b, sg.parts);
+        else report(p.status, PKV_ERR_WORKSPACE);
       }
-      named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next unit
+      named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next segment
       j += n_i;
     }
     if (!ok) s_bad = 1;
@@ -469,11 +512,11 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   const int npend = s_npend;
   if (npend == 0) return;
 
-  // Tickets for this CTA's chunks; the CTA holding the last ticket of an item merges it.
-  // The barrier orders every consumer's partial writes before thread 0's tickets, whose
-  // release publishes them; for the last holder the same atomic's acquire (then the
-  // barrier below) orders the other chunks' partials before its threads' reads. One
-  // acquire-release atomic per ticket measured faster than fence + atomic + fence.
+  // Tickets for this CTA's cut segments; the CTA holding the last ticket of a sequence
+  // merges it. The barrier orders every consumer's partial writes before thread 0's
+  // tickets, whose release publishes them; for the last holder the same atomic's acquire
+  // (then the barrier below) orders the other segments' partials before its threads'
+  // reads. One acquire-release atomic per ticket measured faster than fence + atomic + fence.
   if (tid == 0) {
     for (int k0 = 0; k0 < npend; k0 += kTicketBatch) {
       int ticket[kTicketBatch];
@@ -493,36 +536,35 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   if (warp == kNC || s_bad) return;
   for (int k = 0; k < npend; ++k) {
     if (!s_last[k]) continue;
-    const int4 pe = s_pend[k];
-    const int b = pe.x, nch = pe.y, slot0 = pe.z;
+    const int b = s_pend[k].x, parts = s_pend[k].y;
     for (int it = tid; it < NH * G * (D / 4); it += kNC * 32) {
       const int c = (it % (D / 4)) * 4;
       const int hr = it / (D / 4), h = hr / G, r = hr - h * G;
       float mx = -INFINITY, l = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      for (int q0 = 0; q0 < nch; q0 += kMergeBatch) {
-        const int cnt = min(kMergeBatch, nch - q0);
+      for (int q0 = 0; q0 < parts; q0 += kMergeBatch) {
+        const int cnt = min(kMergeBatch, parts - q0);
         float2 ml[kMergeBatch];
         float4 ov[kMergeBatch];
 #pragma unroll
-        for (int q = 0; q < kMergeBatch; ++q) {
-          if (q < cnt) {
-            const float* row = p.partials + (int64_t)(slot0 + q0 + q) * SLOT + (h * RK + r) * ROW;
-            ml[q] = __ldcg(reinterpret_cast<const float2*>(row));
-            ov[q] = __ldcg(reinterpret_cast<const float4*>(row + 4 + c));
+        for (int x = 0; x < kMergeBatch; ++x) {
+          if (x < cnt) {
+            const float* row = p.partials + (int64_t)segs.slot_of(b, q0 + x) * SLOT + (h * RK + r) * ROW;
+            ml[x] = __ldcg(reinterpret_cast<const float2*>(row));
+            ov[x] = __ldcg(reinterpret_cast<const float4*>(row + 4 + c));
           }
         }
         float mn = mx;
 #pragma unroll
-        for (int q = 0; q < kMergeBatch; ++q)
-          if (q < cnt) mn = fmaxf(mn, ml[q].x);
+        for (int x = 0; x < kMergeBatch; ++x)
+          if (x < cnt) mn = fmaxf(mn, ml[x].x);
         const float fo = mx == -INFINITY ? 0.f : ex2(mx - mn);
         l *= fo, a0 *= fo, a1 *= fo, a2 *= fo, a3 *= fo;
 #pragma unroll
-        for (int q = 0; q < kMergeBatch; ++q) {
-          if (q < cnt) {
-            const float f = ex2(ml[q].x - mn);
-            l += ml[q].y * f;
-            a0 += ov[q].x * f, a1 += ov[q].y * f, a2 += ov[q].z * f, a3 += ov[q].w * f;
+        for (int x = 0; x < kMergeBatch; ++x) {
+          if (x < cnt) {
+            const float f = ex2(ml[x].x - mn);
+            l += ml[x].y * f;
+            a0 += ov[x].x * f, a1 += ov[x].y * f, a2 += ov[x].z * f, a3 += ov[x].w * f;
           }
         }
         mx = mn;
@@ -544,9 +586,10 @@ int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (in
 // Tuning knobs, read once from the environment (0 / unset = built-in choice):
 //   PKV_DECODE_CTAS_PER_SM  CTAs per SM (at most what the shared memory allows)
 //   PKV_DECODE_PDL          0 = launch without programmatic stream serialization
-//   PKV_DECODE_CAP          blocks per unit above which an item is split
+//   PKV_DECODE_CAP          chunks of at most this many blocks (no equal ranges)
+//   PKV_DECODE_FLAT_MIN     blocks per CTA from which the ranges are equal
 struct DecodeKnobs {
-  int ctas_per_sm = 0, pdl = 1, cap = 0;
+  int ctas_per_sm = 0, pdl = 1, cap = 0, flat_min = 0;
   DecodeKnobs() {
     auto env = [](const char* k, int dflt) {
       const char* v = getenv(k);
@@ -555,6 +598,7 @@ struct DecodeKnobs {
     ctas_per_sm = env("PKV_DECODE_CTAS_PER_SM", 0);
     pdl = env("PKV_DECODE_PDL", 1);
     cap = env("PKV_DECODE_CAP", 0);
+    flat_min = env("PKV_DECODE_FLAT_MIN", 0);
   }
 };
 const DecodeKnobs& knobs() {
@@ -562,25 +606,25 @@ const DecodeKnobs& knobs() {
   return k;
 }
 
-template <typename T, int D, int NH, int RK>
+template <typename T, int D, int NH, int RK, bool FLAT_OK>
 int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace, int64_t workspace_bytes,
                   cudaStream_t stream) {
   using S = DecodeShape<D, NH, RK>;
   static int per_sm = 0;
   if (per_sm == 0) {
     cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<T, D, NH, RK>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        cudaFuncSetAttribute(decode_kernel<T, D, NH, RK, FLAT_OK>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK>, kThreads, S::SMEM);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK, FLAT_OK>, kThreads, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     per_sm = std::max(1, occ);
   }
   const int want = knobs().ctas_per_sm > 0 ? std::min(knobs().ctas_per_sm, per_sm) : per_sm;
   const int ctas = std::min(num_sms() * want, kMaxCtas);
   if (!workspace || workspace_bytes < ws_bytes(ctas, NH, RK, D)) return PKV_ERR_WORKSPACE;
-  // Units per CTA are at most ceil((batch + 2 * ctas) / ctas): whole items plus the split
-  // units' slots. Every split unit of a CTA must fit its pending list (148+ SMs: always).
+  // With chunks a CTA holds at most ceil((batch + 2 * ctas) / ctas) units (whole sequences
+  // plus the cut units' slots), so every cut unit's ticket fits its list (148+ SMs: always).
   if ((p0.batch + 2 * ctas + ctas - 1) / ctas > kMaxPending) return PKV_ERR_UNSUPPORTED;
   CUtensorMap tk, tv;
   if (!get_pool_maps(pool, &tk, &tv, NH)) return PKV_ERR_CUDA;
@@ -590,6 +634,8 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   p.partials = reinterpret_cast<float*>(wsb + kPartialsOffset);
   p.max_slots = 2 * ctas;
   p.cap_override = knobs().cap;
+  p.flat_min = knobs().flat_min > 0 ? knobs().flat_min : kFlatMin;
+  p.min_quota = kMinQuota;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(kThreads);
@@ -600,13 +646,24 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = knobs().pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK>, tk, tv, p));
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, FLAT_OK>, tk, tv, p));
+}
+
+template <typename T, int D, int NH, int RK>
+int launch_split(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
+  // The batch holds at most batch * table_cols blocks: below the equal-range threshold
+  // for every CTA count this GPU launches, the chunk rule alone is compiled in.
+  const int64_t bound = (int64_t)p.batch * p.table_cols;
+  const int flat_min = knobs().flat_min > 0 ? knobs().flat_min : kFlatMin;
+  const bool may_flat = knobs().cap <= 0 && bound >= (int64_t)flat_min * num_sms();
+  return may_flat ? launch_decode<T, D, NH, RK, true>(pool, p, ws, wsb, st)
+                  : launch_decode<T, D, NH, RK, false>(pool, p, ws, wsb, st);
 }
 
 template <typename T, int D, int NH>
 int launch_rows(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
-  return p.group <= 8 ? launch_decode<T, D, NH, 8>(pool, p, ws, wsb, st)
-                      : launch_decode<T, D, NH, 16>(pool, p, ws, wsb, st);
+  return p.group <= 8 ? launch_split<T, D, NH, 8>(pool, p, ws, wsb, st)
+                      : launch_split<T, D, NH, 16>(pool, p, ws, wsb, st);
 }
 
 template <typename T, int D>

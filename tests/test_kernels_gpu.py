@@ -585,3 +585,45 @@ def test_prefill_more_sequences_than_one_launch_holds(dev):
                                 qq.astype(np.float64), knq.astype(np.float64), vnq.astype(np.float64))
     assert np.isfinite(got).all()
     assert excess(got, round_to(ref, "float16"), "float16") <= 0
+
+
+def test_decode_many_short_sequences_beside_long_ones_twice(dev):
+    """1000 sequences: most of one block, ten long ones spread through the batch, so CTA ranges
+    cover dozens of whole sequences next to cut ones. Two calls on one workspace give the
+    same bits (every cut sequence's tickets came back to zero) and match the oracle."""
+    from mini_inference_b200 import ops
+
+    bs, hq, hkv, d = 16, 14, 2, 64
+    g = torch.Generator().manual_seed(17)
+    batch = 1000
+    ctx = torch.randint(1, 16, (batch,), generator=g).tolist()
+    for i in range(10):
+        ctx[37 + 96 * i] = int(torch.randint(1500, 2001, (1,), generator=g))
+    nb = sum((c + 1 + bs - 1) // bs for c in ctx) + 3
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, at = [], 0
+    for c in ctx:
+        n = (c + 1 + bs - 1) // bs
+        tables.append(perm[at: at + n])
+        at += n
+    shape = (1, nb + 1, hkv, bs, d)
+    k_pool = torch.randn(shape, generator=g).half().to(dev)
+    v_pool = torch.randn(shape, generator=g).half().to(dev)
+    q = torch.randn(batch, hq, d, generator=g).half().to(dev)
+    kn = torch.randn(batch, hkv, d, generator=g).half().to(dev)
+    vn = torch.randn(batch, hkv, d, generator=g).half().to(dev)
+    meta = decode_metadata(tables, ctx, bs, max(len(t) for t in tables), pad_block=0)
+    tab = torch.from_numpy(meta["block_tables"].astype(np.int32)).to(dev)
+    pool = ops.make_pool(k_pool, v_pool)
+    ws = torch.zeros(ops.decode_workspace_bytes(batch, hkv, tab.shape[1], bs, d, hq), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    kp, vp = to_np(k_pool[0]), to_np(v_pool[0])
+    args = (pool, 0, ops.make_tables(tab), q, torch.from_numpy(meta["context_lens"].astype(np.int32)).to(dev), ws)
+    kw = dict(k_new=kn, v_new=vn, slot_mapping=torch.from_numpy(meta["slot_mapping"]).to(dev), status=status)
+    out = ops.decode_attention(*args, **kw)
+    out2 = ops.decode_attention(*args, **kw)
+    ops.raise_device_errors(status)
+    assert torch.equal(out, out2)
+    assert int(ws[:4096].view(torch.int32).abs().sum()) == 0
+    ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
+    assert excess(to_np(out), round_to(ref, "float16"), "float16") <= 0
