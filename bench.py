@@ -646,9 +646,43 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         barrier(world)
         return start.elapsed_time(end)
 
+    # The decode step as the model runs it, from each layer's qkv_proj rows: RoPE in its own
+    # kernel then the fused append + attention (two launches a layer), or rotated inside the
+    # decode kernel (one launch a layer, pkv_decode_attention_rope).
+    qkv = torch.randn(LAYERS, BATCH, (HQ + 2 * HKV) * D, generator=g, device=dev, dtype=torch.float16)
+    cos, sin = ops.rope_tables(D, CTX_HI + 16, 1e6, torch.float16, dev)
+    q_rot = torch.empty(BATCH, HQ, D, device=dev, dtype=torch.float16)
+    k_rot = torch.empty(BATCH, HKV, D, device=dev, dtype=torch.float16)
+
+    def rope_split_step():
+        ops.build_decode_metadata(tabs, lengths, BS, NUM_BLOCKS, positions, slot_mapping, context_lens, status)
+        for layer in range(LAYERS):
+            ops.rope_append(pool, layer, qkv[layer], positions, cos, sin, HQ, q_out=q_rot, k_out=k_rot, status=status)
+            ops.decode_attention(pool, layer, tabs, q_rot, context_lens, ws, k_new=k_rot,
+                                 v_new=qkv[layer][:, (HQ + HKV) * D:].view(BATCH, HKV, D), slot_mapping=slot_mapping,
+                                 out=out[layer], status=status, inputs_ready=True)
+
+    def rope_fused_step():
+        ops.build_decode_metadata(tabs, lengths, BS, NUM_BLOCKS, positions, slot_mapping, context_lens, status)
+        for layer in range(LAYERS):
+            ops.decode_attention_rope(pool, layer, tabs, qkv[layer], cos, sin, context_lens, ws, slot_mapping,
+                                      out=out[layer], status=status, inputs_ready=layer > 0)
+
+    g_rope = {}
+    for name, fn in (("split", rope_split_step), ("fused", rope_fused_step)):
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g_rope[name] = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_rope[name]):
+            fn()
+
     with ClockSampler(local) as clocks:
         ms_total = timed(g_step, args.steps)
         ms_attn = timed(g_attn, args.steps)
+        rope_steps = max(1, args.steps // 2)
+        ms_rope = {name: timed(gr, rope_steps) for name, gr in g_rope.items()}
         if args.profile_case:
             ms_e2e, h2d, d2h, e2e_launches = ms_total, 0, 0, 0
         else:
@@ -658,7 +692,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     ms_job = max_over_ranks(ms_total, world)
     ms_attn_job = max_over_ranks(ms_attn, world)
     ms_e2e_job = max_over_ranks(ms_e2e, world)
-    del g_step, g_attn, k_pool, v_pool
+    ms_rope_job = {name: max_over_ranks(v, world) for name, v in ms_rope.items()}
+    del g_step, g_attn, g_rope, k_pool, v_pool
     serving = None
     prefix_serving = None
     if not args.profile_case and not args.no_serving and not args.decode_only:  # every rank: configs 3 and 4
@@ -691,7 +726,16 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
                 "path": "C ABI (pkv_decode_attention via ctypes) on pinned host buffers, the step recorded as "
                         "one CUDA graph (as engine/cuda_graphs.py runs decode) with chunked copies overlapping "
                         "the kernels"},
-        "gpu_launches": args.steps * (1 + LAYERS * DECODE_KERNELS) + args.steps * LAYERS * DECODE_KERNELS + e2e_launches,
+        "decode_with_rope": {
+            "workload": "the config-2 step from each layer's qkv_proj rows: metadata, then per layer RoPE + "
+                        "append + attention",
+            "ms_per_step_rope_then_decode": round(ms_rope_job["split"] / rope_steps, 5),
+            "ms_per_step_fused": round(ms_rope_job["fused"] / rope_steps, 5),
+            "launches_per_layer": {"rope_then_decode": 2, "fused": 1},
+            "kv_gbs_fused": round(world * step_bytes * rope_steps / (ms_rope_job["fused"] * 1e-3) / 1e9, 2),
+            "kernel": "pkv_decode_attention_rope (q and the new k rotated in the decode kernel)"},
+        "gpu_launches": (args.steps * (1 + LAYERS * DECODE_KERNELS) + args.steps * LAYERS * DECODE_KERNELS + e2e_launches
+                         + rope_steps * (1 + 2 * LAYERS) + rope_steps * (1 + LAYERS)),
         "clocks": clocks.summary(),
     }
     if args.profile_case:  # no end-to-end leg in the capture case

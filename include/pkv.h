@@ -131,6 +131,25 @@ PKV_API int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_
                          int32_t flags, void* workspace, int64_t workspace_bytes, int32_t* status_dev,
                          pkv_stream_t stream);
 
+/*
+ * pkv_decode_attention with the rotary position embedding fused in: q, the new k and the new
+ * v come straight from the qkv_proj output, and q and k are rotated inside the kernel at
+ * position context_lens[b] - 1, bit-identical to the reference's apply_rope on the same
+ * tables (r(r(x * cos) + r(rotate_half(x) * sin)) per element). Replaces, for a decode step,
+ * pkv_rope_append (rotation) followed by pkv_decode_attention (append + attention): one
+ * launch per layer instead of two (engine/model.py:241-250 + engine/kv_cache.py:611-620).
+ *   qkv   : row b [q (Hq*d) | k (Hkv*d) | v (Hkv*d)] at qkv + b*qkv_stride (elements)
+ *   cos_table, sin_table : [max_positions, d] in the storage dtype (as pkv_rope_append)
+ *   slot_mapping : required (the rotated k and v are appended there)
+ * Everything else is pkv_decode_attention's; a position past the tables is reported in status.
+ */
+PKV_API int pkv_decode_attention_rope(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
+                              int32_t num_q_heads, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                              const void* qkv, int64_t qkv_stride, const void* cos_table, const void* sin_table,
+                              int64_t max_positions, const int64_t* slot_mapping, const int32_t* context_lens,
+                              float scale, int32_t flags, void* workspace, int64_t workspace_bytes,
+                              int32_t* status_dev, pkv_stream_t stream);
+
 /* pkv_decode_attention flags */
 enum {
   /* context_lens, the block tables / seq_rows and every cached K/V row the call reads were

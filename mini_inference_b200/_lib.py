@@ -74,6 +74,9 @@ SIGNATURES: dict[str, tuple] = {
     "pkv_decode_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64, c_int64,
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                        c_void_p, c_float, c_int32, c_void_p, c_int64, c_void_p, c_void_p]),
+    "pkv_decode_attention_rope": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64, c_int64,
+                                            c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float,
+                                            c_int32, c_void_p, c_int64, c_void_p, c_void_p]),
     "pkv_decode_workspace_bytes": (c_int64, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32]),
     "pkv_decode_reset_workspace": (c_int32, [c_void_p, c_int64, c_void_p]),
     "pkv_decode_static_reset": (c_int32, [c_void_p]),

@@ -509,25 +509,18 @@ class PagedDecodeContext:
         """The ``qkv_proj`` output ``[B, 1, (Hq + 2 Hkv) d]`` -> ``[B, Hq, 1, d]``, RoPE included.
 
         Replaces the split, head views and ``apply_rope`` of Attention.forward
-        (engine/model.py:241-250) plus :meth:`attend`: ``pkv_rope_append`` rotates q and k
-        (bit-identical to the reference's) on the full ``cos`` / ``sin`` tables of
-        ``ops.rope_tables``, then the fused append + paged attention kernel runs on them.
+        (engine/model.py:241-250) plus :meth:`attend` with one kernel
+        (``pkv_decode_attention_rope``): q and k are rotated (bit-identical to the
+        reference's) on the full ``cos`` / ``sin`` tables of ``ops.rope_tables`` while the
+        step's append and paged attention run.
         """
         batch = qkv.shape[0]
         rows = qkv.reshape(batch, -1)
-        hkv, d = self.cache.num_kv_heads, self.cache.head_dim
-        # The rotated keys get the v columns' row stride, so the decode kernel reads both
-        # through one (row, head) stride pair and nothing is copied.
-        k_store = torch.empty_like(rows)
-        k_rot = k_store[:, :hkv * d].view(batch, hkv, d)
-        q_rot, _ = ops.rope_append(self.cache.pool, layer_idx, rows, self.positions, cos, sin, num_q_heads,
-                                   k_out=k_rot, status=self.cache.status)
-        v_new = rows[:, (num_q_heads + hkv) * d:].view(batch, hkv, d)
         ws = self.cache.workspace(self.cache.max_seqs, num_q_heads)
-        out = torch.empty(batch, 1, num_q_heads, d, dtype=qkv.dtype, device=qkv.device)
-        ops.decode_attention(self.cache.pool, layer_idx, self.tables, q_rot, self.context_lens, ws, k_new=k_rot,
-                             v_new=v_new, slot_mapping=self.slot_mapping, out=out[:, 0], status=self.cache.status,
-                             inputs_ready=self._attends > 0)  # the rotation writes only q and k_new, read later
+        out = torch.empty(batch, 1, num_q_heads, self.cache.head_dim, dtype=qkv.dtype, device=qkv.device)
+        ops.decode_attention_rope(self.cache.pool, layer_idx, self.tables, rows, cos, sin, self.context_lens, ws,
+                                  self.slot_mapping, out=out[:, 0], status=self.cache.status,
+                                  inputs_ready=self._attends > 0)
         self._attends += 1
         return out.transpose(1, 2)
 

@@ -104,6 +104,11 @@ struct DecodeParams {
   int32_t batch, group, kv_heads, layer, nbt, inputs_ready, max_slots, cap_override;
   int32_t flat_min, min_quota;
   float scale_log2;
+  // RoPE fused in (pkv_decode_attention_rope): q and the new k are the raw qkv_proj rows,
+  // rotated here at position context_lens[b] - 1 with these [max_positions, D] tables.
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_max_pos;
 };
 
 __device__ inline void named_bar(int id, int threads) {
@@ -211,6 +216,39 @@ __device__ inline void load_q(uint32_t (&qa)[D / 16][4], const T* qb, int64_t q_
 
 // FLAT_OK: the launch may take equal ranges (the host's bound on the batch's blocks
 // reaches the threshold); without it the chunk rule is compiled alone.
+// r(r(x * c) + r(y * s)) for a packed pair, each product and the sum in float32 and each
+// rounded to T: the reference's apply_rope (engine/model.py:214-224) on eager fp16 / bf16
+// tensors, so the rotated values are bit-identical to it on the same tables.
+template <typename T>
+__device__ inline uint32_t rope_pair(uint32_t x, uint32_t c, uint32_t y, uint32_t s) {
+  const float2 xf = Dt<T>::unpack(x), cf = Dt<T>::unpack(c), yf = Dt<T>::unpack(y), sf = Dt<T>::unpack(s);
+  const float2 a = Dt<T>::unpack(Dt<T>::pack(xf.x * cf.x, xf.y * cf.y));
+  const float2 b = Dt<T>::unpack(Dt<T>::pack(yf.x * sf.x, yf.y * sf.y));
+  return Dt<T>::pack(a.x + b.x, a.y + b.y);
+}
+
+// -x of both halves (exact).
+__device__ inline uint32_t neg_pair(uint32_t x) { return x ^ 0x80008000u; }
+
+// Rotate the Q fragments (qa[kk][i]: columns kk * 16 + 2 t4 + {0, 1} (+ 8 for i >= 2)) at
+// the cos / sin rows of one position: column c < D / 2 pairs with -x[c + D / 2], column
+// c + D / 2 with x[c]; a thread holds both (fragments kk and kk + D / 32).
+template <typename T, int D>
+__device__ inline void rope_q(uint32_t (&qa)[D / 16][4], const T* crow, const T* srow, int t4) {
+#pragma unroll
+  for (int kk = 0; kk < D / 32; ++kk) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = kk * 16 + 2 * t4 + (i >= 2 ? 8 : 0), c2 = c + D / 2;
+      const uint32_t x1 = qa[kk][i], x2 = qa[kk + D / 32][i];
+      const uint32_t c1 = *reinterpret_cast<const uint32_t*>(crow + c), s1 = *reinterpret_cast<const uint32_t*>(srow + c);
+      const uint32_t cc2 = *reinterpret_cast<const uint32_t*>(crow + c2), s2 = *reinterpret_cast<const uint32_t*>(srow + c2);
+      qa[kk][i] = rope_pair<T>(x1, c1, neg_pair(x2), s1);
+      qa[kk + D / 32][i] = rope_pair<T>(x2, cc2, x1, s2);
+    }
+  }
+}
+
 template <typename T, int D, int NH, int RK, bool FLAT_OK>
 __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -398,6 +436,18 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
       uint32_t qa[D / 16][4];
       load_q<T, D>(qa, reinterpret_cast<const T*>(p.q) + sg.b * p.q_sb + (int64_t)h * G * p.q_sh, p.q_sh, G, g_lane,
                    t4);
+      const T* rope_c = nullptr;
+      const T* rope_s = nullptr;
+      if (p.rope_cos) {  // rows at the new token's position (rows >= G are zero and stay zero)
+        int64_t pos = sCtx[sg.b] - 1;
+        if (pos >= p.rope_max_pos) {
+          if (lane == 0) report(p.status, PKV_ERR_OUT_OF_RANGE);
+          pos = 0;
+        }
+        rope_c = reinterpret_cast<const T*>(p.rope_cos) + pos * D;
+        rope_s = reinterpret_cast<const T*>(p.rope_sin) + pos * D;
+        rope_q<T, D>(qa, rope_c, rope_s, t4);
+      }
       const int b = sg.b;
       const int ctx = sCtx[b];
       const int append_blk = p.k_new ? (ctx - 1) / kBS : -1;
@@ -431,8 +481,13 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
 #pragma unroll
             for (int wd = lane; wd < D / 2; wd += 32) {
               const int d0 = 2 * wd;
-              const uint32_t kw = *reinterpret_cast<const uint32_t*>(kn + d0);
+              uint32_t kw = *reinterpret_cast<const uint32_t*>(kn + d0);
               const uint32_t vw = *reinterpret_cast<const uint32_t*>(vn + d0);
+              if (rope_c) {  // the new key rotated as q: its partner is D / 2 away
+                const uint32_t kp = *reinterpret_cast<const uint32_t*>(kn + (d0 ^ (D / 2)));
+                kw = rope_pair<T>(kw, *reinterpret_cast<const uint32_t*>(rope_c + d0), d0 < D / 2 ? neg_pair(kp) : kp,
+                                  *reinterpret_cast<const uint32_t*>(rope_s + d0));
+              }
               const uint32_t r = (d0 / 64) * kBS + off;
               *reinterpret_cast<uint32_t*>(kt + swz128(r, d0 % 64)) = kw;
               *reinterpret_cast<uint32_t*>(vt + swz128(r, d0 % 64)) = vw;
@@ -681,6 +736,7 @@ int launch_heads(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t 
 }  // namespace pkv
 
 using namespace pkv;
+using T16 = uint16_t;  // a 16-bit element of the pool's storage type
 
 extern "C" int pkv_decode_reset_workspace(void* workspace, int64_t workspace_bytes, pkv_stream_t stream) {
   if (!workspace || workspace_bytes < kPartialsOffset) return PKV_ERR_INVALID_ARGUMENT;
@@ -698,14 +754,14 @@ extern "C" int64_t pkv_decode_workspace_bytes(int32_t batch, int32_t num_kv_head
   return ws_bytes(kMaxCtas, num_kv_heads, group <= 8 ? 8 : 16, head_dim);
 }
 
-extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
-                                    int32_t num_q_heads, void* out, int64_t out_stride_b, int64_t out_stride_h,
-                                    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_new,
-                                    const void* v_new, int64_t kv_stride_b, int64_t kv_stride_h,
-                                    const int64_t* slot_mapping, const int32_t* context_lens, float scale,
-                                    int32_t flags, void* workspace, int64_t workspace_bytes,
-                                    int32_t* status_dev, pkv_stream_t stream) {
-  if (!pool || !tables || !out || !q || !context_lens || !tables->block_tables) return PKV_ERR_INVALID_ARGUMENT;
+namespace {
+
+// Checks shared by the entry points and the launch; q, k_new, v_new and their strides are set.
+int decode_launch(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch, int32_t num_q_heads,
+                  void* out, int64_t out_stride_b, int64_t out_stride_h, const int64_t* slot_mapping,
+                  const int32_t* context_lens, float scale, int32_t flags, void* workspace, int64_t workspace_bytes,
+                  int32_t* status_dev, pkv_stream_t stream, DecodeParams& p) {
+  if (!pool || !tables || !out || !p.q || !context_lens || !tables->block_tables) return PKV_ERR_INVALID_ARGUMENT;
   if (batch < 0 || layer < 0 || layer >= pool->num_layers) return PKV_ERR_INVALID_ARGUMENT;
   if (batch == 0) return PKV_OK;
   if (batch > kMaxBatch) return PKV_ERR_UNSUPPORTED;
@@ -715,22 +771,19 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   if (hkv != 1 && hkv != 2 && hkv != 4 && hkv != 8) return PKV_ERR_UNSUPPORTED;
   const int group = num_q_heads / hkv;
   if (group > 16) return PKV_ERR_UNSUPPORTED;
-  if ((k_new == nullptr) != (v_new == nullptr)) return PKV_ERR_INVALID_ARGUMENT;
-  if (k_new && !slot_mapping) return PKV_ERR_INVALID_ARGUMENT;
+  if ((p.k_new == nullptr) != (p.v_new == nullptr)) return PKV_ERR_INVALID_ARGUMENT;
+  if (p.k_new && !slot_mapping) return PKV_ERR_INVALID_ARGUMENT;
   // 32-bit accesses to q, out and the new rows: even strides, 4-byte aligned bases.
   auto aligned4 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3) == 0; };
-  if (!aligned4(q) || !aligned4(out) || (k_new && (!aligned4(k_new) || !aligned4(v_new)))) return PKV_ERR_INVALID_ARGUMENT;
-  if ((q_stride_b | q_stride_h | out_stride_b | out_stride_h) & 1) return PKV_ERR_INVALID_ARGUMENT;
-  if (k_new && ((kv_stride_b | kv_stride_h) & 1)) return PKV_ERR_INVALID_ARGUMENT;
+  if (!aligned4(p.q) || !aligned4(out) || (p.k_new && (!aligned4(p.k_new) || !aligned4(p.v_new))))
+    return PKV_ERR_INVALID_ARGUMENT;
+  if ((p.q_sb | p.q_sh | out_stride_b | out_stride_h) & 1) return PKV_ERR_INVALID_ARGUMENT;
+  if (p.k_new && ((p.kv_sb | p.kv_sh) & 1)) return PKV_ERR_INVALID_ARGUMENT;
   if (tables->cols <= 0 || tables->rows <= 0) return PKV_ERR_INVALID_ARGUMENT;
   if (!tables->seq_rows && tables->rows < batch) return PKV_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return PKV_ERR_INVALID_ARGUMENT;
 
-  DecodeParams p{};
   p.out = out;
-  p.q = q;
-  p.k_new = k_new;
-  p.v_new = v_new;
   p.k_pool = pool->k;
   p.v_pool = pool->v;
   p.slot_mapping = slot_mapping;
@@ -740,10 +793,6 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
   p.status = status_dev;
   p.out_sb = out_stride_b;
   p.out_sh = out_stride_h;
-  p.q_sb = q_stride_b;
-  p.q_sh = q_stride_h;
-  p.kv_sb = kv_stride_b;
-  p.kv_sh = kv_stride_h;
   p.table_stride = tables->stride;
   p.table_rows = tables->rows;
   p.table_cols = tables->cols;
@@ -765,4 +814,51 @@ extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const p
                    : launch_heads<__nv_bfloat16, 128>(*pool, p, workspace, workspace_bytes, st);
   }
   return PKV_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" int pkv_decode_attention(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
+                                    int32_t num_q_heads, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                                    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* k_new,
+                                    const void* v_new, int64_t kv_stride_b, int64_t kv_stride_h,
+                                    const int64_t* slot_mapping, const int32_t* context_lens, float scale,
+                                    int32_t flags, void* workspace, int64_t workspace_bytes,
+                                    int32_t* status_dev, pkv_stream_t stream) {
+  DecodeParams p{};
+  p.q = q;
+  p.q_sb = q_stride_b;
+  p.q_sh = q_stride_h;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.kv_sb = kv_stride_b;
+  p.kv_sh = kv_stride_h;
+  return decode_launch(pool, layer, tables, batch, num_q_heads, out, out_stride_b, out_stride_h, slot_mapping,
+                       context_lens, scale, flags, workspace, workspace_bytes, status_dev, stream, p);
+}
+
+extern "C" int pkv_decode_attention_rope(const pkv_pool* pool, int32_t layer, const pkv_tables* tables, int32_t batch,
+                                         int32_t num_q_heads, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                                         const void* qkv, int64_t qkv_stride, const void* cos_table,
+                                         const void* sin_table, int64_t max_positions, const int64_t* slot_mapping,
+                                         const int32_t* context_lens, float scale, int32_t flags, void* workspace,
+                                         int64_t workspace_bytes, int32_t* status_dev, pkv_stream_t stream) {
+  if (!pool || !qkv || !cos_table || !sin_table || !slot_mapping || max_positions <= 0) return PKV_ERR_INVALID_ARGUMENT;
+  auto aligned4 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 3) == 0; };
+  if (!aligned4(cos_table) || !aligned4(sin_table)) return PKV_ERR_INVALID_ARGUMENT;
+  const int64_t d = pool->head_dim, hkv = pool->num_kv_heads;
+  const T16* base = static_cast<const T16*>(qkv);
+  DecodeParams p{};
+  p.q = base;
+  p.q_sb = qkv_stride;
+  p.q_sh = d;
+  p.k_new = base + num_q_heads * d;
+  p.v_new = base + (num_q_heads + hkv) * d;
+  p.kv_sb = qkv_stride;
+  p.kv_sh = d;
+  p.rope_cos = cos_table;
+  p.rope_sin = sin_table;
+  p.rope_max_pos = max_positions;
+  return decode_launch(pool, layer, tables, batch, num_q_heads, out, out_stride_b, out_stride_h, slot_mapping,
+                       context_lens, scale, flags, workspace, workspace_bytes, status_dev, stream, p);
 }

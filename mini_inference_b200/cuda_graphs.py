@@ -68,20 +68,14 @@ class _GraphDecodeContext:
 
     def attend_qkv(self, layer_idx: int, qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                    num_q_heads: int) -> torch.Tensor:
-        """RoPE fused with the append, then paged attention (as ``PagedDecodeContext.attend_qkv``)."""
+        """RoPE, append and paged attention in one kernel (as ``PagedDecodeContext.attend_qkv``)."""
         batch = qkv.shape[0]
         rows = qkv.reshape(batch, -1)
-        hkv, d = self.cache.num_kv_heads, self.cache.head_dim
-        k_store = torch.empty_like(rows)  # rotated keys with the v columns' row stride
-        k_rot = k_store[:, :hkv * d].view(batch, hkv, d)
-        q_rot, _ = ops.rope_append(self.cache.pool, layer_idx, rows, self.positions, cos, sin, num_q_heads,
-                                   k_out=k_rot, status=self.cache.status)
-        v_new = rows[:, (num_q_heads + hkv) * d:].view(batch, hkv, d)
         ws = self.cache.workspace(self.cache.max_seqs, num_q_heads)
-        out = torch.empty(batch, 1, num_q_heads, d, dtype=qkv.dtype, device=qkv.device)
-        ops.decode_attention(self.cache.pool, layer_idx, self.tables, q_rot, self.context_lens, ws, k_new=k_rot,
-                             v_new=v_new, slot_mapping=self.slot_mapping, out=out[:, 0], status=self.cache.status,
-                             inputs_ready=self._attends > 0)
+        out = torch.empty(batch, 1, num_q_heads, self.cache.head_dim, dtype=qkv.dtype, device=qkv.device)
+        ops.decode_attention_rope(self.cache.pool, layer_idx, self.tables, rows, cos, sin, self.context_lens, ws,
+                                  self.slot_mapping, out=out[:, 0], status=self.cache.status,
+                                  inputs_ready=self._attends > 0)
         self._attends += 1
         return out.transpose(1, 2)
 

@@ -144,6 +144,41 @@ def rope_append(pool: PkvPool, layer: int, qkv: torch.Tensor, positions: torch.T
     return q_out, k_out
 
 
+def decode_attention_rope(pool: PkvPool, layer: int, tables: PkvTables, qkv: torch.Tensor, cos: torch.Tensor,
+                          sin: torch.Tensor, context_lens: torch.Tensor, workspace: torch.Tensor,
+                          slot_mapping: torch.Tensor, out: torch.Tensor | None = None, scale: float | None = None,
+                          status: torch.Tensor | None = None, inputs_ready: bool = False) -> torch.Tensor:
+    """One decode step on one layer from the ``qkv_proj`` rows ``[B, (Hq + 2 Hkv) * d]``, RoPE included.
+
+    q and the new k are rotated in the kernel at position ``context_lens[b] - 1`` on the
+    ``cos`` / ``sin`` tables of :func:`rope_tables` (bit-identical to :func:`rope_append`),
+    the rotated k and the v columns are appended at ``slot_mapping``, and attention runs:
+    one launch for what :func:`rope_append` then :func:`decode_attention` do in two.
+    Returns ``out`` ``[B, Hq, d]``.
+    """
+    _require_cuda(qkv, cos, sin, context_lens, workspace, slot_mapping, out)
+    batch = qkv.shape[0]
+    hkv, d = pool.num_kv_heads, pool.head_dim
+    if qkv.dim() != 2 or qkv.stride(1) != 1 or qkv.shape[1] % d or qkv.shape[1] // d <= 2 * hkv:
+        raise ValueError("qkv must be [B, (Hq + 2 Hkv) * head_dim] with a contiguous last dimension")
+    hq = qkv.shape[1] // d - 2 * hkv
+    if cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] != d or not (cos.is_contiguous() and sin.is_contiguous()):
+        raise ValueError("cos / sin must be contiguous [max_positions, head_dim] tables")
+    if cos.dtype != qkv.dtype or sin.dtype != qkv.dtype or pkv_dtype(qkv.dtype) != pool.dtype:
+        raise ValueError("qkv, the tables and the pool must share one dtype")
+    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be a contiguous int64 tensor")
+    if out is None:
+        out = torch.empty(batch, hq, d, dtype=qkv.dtype, device=qkv.device)
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    check(lib.pkv_decode_attention_rope(
+        ctypes.byref(pool), layer, ctypes.byref(tables), batch, hq, out.data_ptr(), out.stride(0), out.stride(1),
+        qkv.data_ptr(), qkv.stride(0), cos.data_ptr(), sin.data_ptr(), cos.shape[0], slot_mapping.data_ptr(),
+        context_lens.data_ptr(), scale, PKV_DECODE_INPUTS_READY if inputs_ready else 0, workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _ptr(status), _stream()), "decode_attention_rope")
+    return out
+
+
 def decode_workspace_bytes(batch: int, num_kv_heads: int, max_blocks: int, block_size: int, head_dim: int,
                            num_q_heads: int) -> int:
     return int(lib.pkv_decode_workspace_bytes(batch, num_kv_heads, max_blocks, block_size, head_dim, num_q_heads))

@@ -221,3 +221,61 @@ def test_contexts_attend_qkv_equals_rope_then_attend(dev, dtype, hq, hkv, d):
         da.commit(), db.commit()
     ca.raise_device_errors(), cb.raise_device_errors()
     assert torch.equal(ca.k, cb.k) and torch.equal(ca.v, cb.v)
+
+
+@pytest.mark.parametrize("dtype,hq,hkv,d", SHAPES)
+def test_decode_attention_rope_equals_rope_then_decode(dev, dtype, hq, hkv, d):
+    """pkv_decode_attention_rope (rotation inside the decode kernel) = pkv_rope_append then
+    pkv_decode_attention, bit for bit: outputs and the appended rows alike, on the config-2
+    micro-benchmark's batch (64 sequences of 128..2048 tokens, rows of a wider buffer)."""
+    from mini_inference_b200 import ops
+    from tests.test_kernels_gpu import micro_bench_case
+
+    batch = 64 if d == 64 else 16
+    ctx, tables, k_pool, v_pool, _, _, _ = micro_bench_case(dev, seed=4, batch=batch, dtype=dtype, hq=hq, hkv=hkv, d=d,
+                                                            num_blocks=8192 if d == 128 else 16384, layers=1)
+    bs = 16
+    cols = max(len(t) for t in tables)
+    tab = torch.zeros(batch, cols, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        tab[i, :len(t)] = torch.tensor(t)
+    tabs = ops.make_tables(tab.to(dev))
+    slot = torch.tensor([tables[i][c // bs] * bs + c % bs for i, c in enumerate(ctx)], dtype=torch.int64, device=dev)
+    lens = torch.tensor([c + 1 for c in ctx], dtype=torch.int32, device=dev)
+    positions = lens.to(torch.int64) - 1
+    g = torch.Generator(device=dev).manual_seed(8)
+    width = (hq + 2 * hkv) * d
+    qkv = (torch.randn(batch, width + 8, generator=g, device=dev) * 2).to(dtype)[:, :width]
+    cos, sin = ops.rope_tables(d, 4096, 1e6, dtype, dev)
+    k2, v2 = k_pool.clone(), v_pool.clone()
+    pool_a, pool_b = ops.make_pool(k_pool, v_pool), ops.make_pool(k2, v2)
+    ws_a = torch.zeros(ops.decode_workspace_bytes(batch, hkv, cols, bs, d, hq), dtype=torch.uint8, device=dev)
+    ws_b = torch.zeros_like(ws_a)
+    status = torch.zeros(2, dtype=torch.int32, device=dev)
+    fused = ops.decode_attention_rope(pool_a, 0, tabs, qkv, cos, sin, lens, ws_a, slot, status=status[0:1])
+    q_rot, k_rot = ops.rope_append(pool_b, 0, qkv, positions, cos, sin, hq, k_out=True, status=status[1:2])
+    v_new = qkv[:, (hq + hkv) * d:].view(batch, hkv, d)
+    split = ops.decode_attention(pool_b, 0, tabs, q_rot, lens, ws_b, k_new=k_rot, v_new=v_new, slot_mapping=slot,
+                                 status=status[1:2])
+    ops.raise_device_errors(status[0:1])
+    ops.raise_device_errors(status[1:2])
+    assert torch.equal(_bits(fused), _bits(split))
+    assert torch.equal(_bits(k_pool), _bits(k2)) and torch.equal(_bits(v_pool), _bits(v2))
+
+
+def test_decode_attention_rope_reports_a_position_past_the_tables(dev):
+    from mini_inference_b200 import PkvError, ops
+
+    hq, hkv, d, bs = 14, 2, 64, 16
+    k = torch.zeros(1, 9, hkv, bs, d, dtype=torch.float16, device=dev)
+    pool = ops.make_pool(k, torch.zeros_like(k))
+    tab = torch.arange(8, dtype=torch.int32, device=dev).view(1, 8)
+    lens = torch.tensor([100], dtype=torch.int32, device=dev)  # position 99, tables of 64 positions
+    cos, sin = ops.rope_tables(d, 64, 1e6, torch.float16, dev)
+    qkv = torch.randn(1, (hq + 2 * hkv) * d, device=dev).half()
+    ws = torch.zeros(ops.decode_workspace_bytes(1, hkv, 8, bs, d, hq), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    slot = torch.tensor([6 * bs + 3], dtype=torch.int64, device=dev)
+    ops.decode_attention_rope(pool, 0, ops.make_tables(tab), qkv, cos, sin, lens, ws, slot, status=status)
+    with pytest.raises((IndexError, PkvError)):
+        ops.raise_device_errors(status)
