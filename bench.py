@@ -195,6 +195,78 @@ def run_long_context(dev, seed: int, reps: int = 10) -> dict:
                          "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": f"{kind} copy bandwidth"}}
 
 
+def run_long_step(dev, seed: int, steps: int = 32, warmup: int = 3) -> dict:
+    """Config 5's decode step through the whole Qwen2.5-7B-shaped model (bf16, random N(0, 0.02)
+    weights drawn on the GPU): 64 sequences with contexts U{8192..32768}, every layer's
+    qkv_proj / o_proj / MLP GEMMs and RMSNorms on torch, RoPE + append + paged attention in
+    one kernel per layer, the LM head fused with greedy argmax, replayed as one CUDA graph.
+
+    The task builds the contexts by a seeded prefill of uniform token ids (~10^16 FLOP); here
+    the pool's K/V are seeded N(0, 1) values written directly, which costs the decode step
+    the same bytes. Bytes per step = every weight once (the embedding table only for the
+    step's rows) + every context token's K and V in every layer.
+    """
+    from mini_inference_b200 import PagedKVCache
+    from mini_inference_b200.engine import ModelRunner
+    from mini_inference_b200.model import Qwen2Config, Qwen2Model, init_random
+
+    cfg = Qwen2Config.qwen2_7b()
+    model = Qwen2Model(cfg, init_random(cfg, seed=0, std=0.02, dtype=torch.bfloat16, device=dev,
+                                        generator_device="cuda"))
+    batch = 64
+    g = torch.Generator().manual_seed(seed + 5)
+    ctx = torch.randint(8192, 32769, (batch,), generator=g).tolist()
+    extra = steps + warmup + 4  # room for the generated tokens
+    max_len = max(ctx) + extra + 16
+    nblk = sum((c + extra + BS - 1) // BS for c in ctx)
+    cache = PagedKVCache(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, num_blocks=nblk + 8, block_size=BS,
+                         max_seqs=batch, max_len=max_len, dtype=torch.bfloat16, device=dev)
+    gd = torch.Generator(device=dev).manual_seed(seed + 17)
+    for layer in range(cfg.num_layers):  # the "prefilled" contexts, layer by layer
+        cache.k[layer].normal_(generator=gd)
+        cache.v[layer].normal_(generator=gd)
+    slots = [cache.allocate(c + extra) for c in ctx]
+    for s_, c in zip(slots, ctx):
+        cache.lengths[s_] = c
+    runner = ModelRunner(model, cache, max_batch=batch)
+    runner.enable_cuda_graphs(batch)
+    tokens = torch.randint(0, cfg.vocab_size, (batch,), generator=g).tolist()
+    for _ in range(warmup):
+        tokens = runner.decode_tokens(slots, tokens)
+    torch.cuda.synchronize()
+    start_ctx = sum(cache.lengths[s_] for s_ in slots)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(steps):
+        tokens = runner.decode_tokens(slots, tokens)
+    e1.record()
+    torch.cuda.synchronize()
+    host_s = time.perf_counter() - t0
+    cache.raise_device_errors()
+    ms = e0.elapsed_time(e1) / steps
+    kv_per_token = cfg.num_layers * 2 * cfg.num_kv_heads * cfg.head_dim * 2
+    ctx_tokens = sum(start_ctx + batch * (i + 1) for i in range(steps)) / steps  # keys attended per step
+    embed_bytes = cfg.vocab_size * cfg.hidden_size * 2
+    weight_bytes = model.weight_bytes() - embed_bytes + batch * cfg.hidden_size * 2
+    step_bytes = weight_bytes + ctx_tokens * kv_per_token
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    peaks, kind = measured_peaks()
+    pool_gb = (cache.k.numel() + cache.v.numel()) * 2 / 1e9
+    del runner, cache, model
+    torch.cuda.empty_cache()
+    return {"workload": "config 5 decode step: Qwen2.5-7B shape (28 layers, hidden 3584, 28 / 4 heads of 128, MLP "
+                        "18944, vocab 152064), bf16 random-init weights, 64 sequences with contexts U{8192..32768} "
+                        "(K/V seeded directly in the pool), greedy",
+            "steps": steps, "ms_per_step": round(ms, 3), "tok_s": round(batch / (ms * 1e-3), 1),
+            "host_ms_per_step": round(host_s / steps * 1e3, 3),
+            "bytes_per_step": int(step_bytes), "weight_bytes": int(weight_bytes),
+            "kv_bytes_per_step": int(ctx_tokens * kv_per_token),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": f"{kind} copy bandwidth"},
+            "pool_gb": round(pool_gb, 1)}
+
+
 def run_qkv_post(dev, seed: int, reps: int = 50) -> dict:
     """``pkv_rope_append`` at 0.5B shapes (Hq 14 / Hkv 2 / d 64, fp16), beside the reference's
     eager path for the same work on the same GPU: the split and head views, ``apply_rope``
@@ -745,6 +817,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     else:
         line["prefill"] = run_prefill(dev, seed=rank)
         line["long_context"] = run_long_context(dev, seed=rank)
+        if not args.no_long_step:
+            line["long_context_step"] = run_long_step(dev, seed=rank)
         line["qkv_post"] = run_qkv_post(dev, seed=rank)
         line["lm_head"] = run_lm_head(dev, seed=rank)
         line["scheduler"] = run_scheduler(seed=rank)
@@ -1230,6 +1304,8 @@ def main() -> None:
     ap.add_argument("--serving-cpu-budget", type=float, default=20.0, help="seconds for the CPU serving sample")
     ap.add_argument("--serving-check", action="store_true", help="check device errors after every serving run")
     ap.add_argument("--no-serving", action="store_true", help="skip the config-3 serving leg")
+    ap.add_argument("--no-long-step", action="store_true", help="skip config 5's whole-model decode step")
+    ap.add_argument("--long-step-only", action="store_true", help="only config 5's whole-model decode step")
     ap.add_argument("--decode-only", action="store_true",
                     help="only the config-2 decode step and its e2e leg (no other legs, no CPU baseline)")
     ap.add_argument("--serving-only", action="store_true",
@@ -1242,12 +1318,13 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args)
         return
-    if args.prefill_only or args.long_only or args.lm_head_only or args.qkv_only:
+    if args.prefill_only or args.long_only or args.lm_head_only or args.qkv_only or args.long_step_only:
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         torch.cuda.set_device(dev)
         run = (run_prefill if args.prefill_only else run_long_context if args.long_only
-               else run_lm_head if args.lm_head_only else run_qkv_post)
-        print(json.dumps(run(dev, seed=0, reps=args.steps)), flush=True)
+               else run_lm_head if args.lm_head_only else run_long_step if args.long_step_only else run_qkv_post)
+        res = run(dev, seed=0) if args.long_step_only else run(dev, seed=0, reps=args.steps)
+        print(json.dumps(res), flush=True)
         return
     rank, world, local = dist_setup(args.gpus)
     try:
