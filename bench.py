@@ -22,10 +22,18 @@ q / new k / new v and tables copied from pinned host memory, the outputs
 copied back, all inside the timed region; the step is one CUDA graph, as the
 reference engine runs decode, with the copies chunked to overlap the kernels).
 
+The same line carries the other legs as keys: ``serving`` (config 3: 200 requests
+through ``LLMEngine`` at the 0.5B shape, output tok/s, TTFT / TPOT, with a CPU sample of
+the reference's loop beside it), ``prefix_serving`` (config 4 with prefix caching and its
+``prefix_hit_tokens``), ``long_context`` / ``long_context_step`` (config 5's attention
+call and its whole 28-layer 7B-shaped decode step), ``decode_with_rope`` (RoPE fused into
+the decode kernel against a separate rotation launch), ``prefill``, ``qkv_post``,
+``lm_head`` and ``scheduler``.
+
 Multi-GPU: one process per GPU, each with its own batch and pool (weak scaling,
 requests sharded by rank, no collective on the data path); the timed region is
 bracketed by barriers and timed on each device with CUDA events, and the job
-time is the maximum over ranks.
+time is the maximum over ranks. Barriers and the max run on a host ``gloo`` group.
 
 ``--impl reference`` times the reference's own algorithm on the host cores:
 ``oracle/paged_kv_torch.py``, the reference's PyTorch ops for this step
