@@ -283,6 +283,33 @@ PKV_API int pkv_lm_head_argmax(const void* hidden, int64_t hidden_stride, int32_
                        int64_t* token_ids, float* max_logits, void* workspace, int64_t workspace_bytes,
                        int32_t flags, int32_t* status_dev, pkv_stream_t stream);
 
+/* ------------------------------------------------------------------ decoder-layer glue */
+/*
+ * The elementwise steps of the Qwen2 decoder layer around the attention call, one launch
+ * each instead of the reference's eager chains (engine/model.py:162-166 RMSNorm,
+ * :262-264 the MLP's silu(gate) * up, :278-280 the residual adds).
+ *
+ * pkv_add_rms_norm, per row of [rows, hidden] (strides in elements):
+ *   h   = residual_in ? round(x + residual_in) : x      (the residual add, x = the block output)
+ *   residual_out (NULL = not written) receives h; it may be residual_in itself (in place)
+ *   out = round(weight * round(h * rsqrt(mean(h^2) + eps)))   (statistics in float32)
+ * The add and every rounding are the reference's; the float32 sum of squares runs in its
+ * own order. out may alias x. hidden <= 8192 (any multiple of 8 up to 65536 when every
+ * row start is 16-byte aligned).
+ *
+ * pkv_silu_mul, per row of gate_up = [rows, 2 * intermediate] (gate | up):
+ *   out[:, j] = round(round(silu(gate[:, j])) * up[:, j]),  silu(g) = g / (1 + exp(-g)) in float32
+ *
+ * dtype: PKV_F16 or PKV_BF16 for every operand. 16-byte accesses when the rows allow
+ * them, 2-byte ones otherwise.
+ */
+PKV_API int pkv_add_rms_norm(int32_t dtype, const void* x, int64_t x_stride, const void* residual_in,
+                             int64_t residual_in_stride, void* residual_out, int64_t residual_out_stride,
+                             const void* weight, void* out, int64_t out_stride, int64_t rows, int32_t hidden,
+                             float eps, pkv_stream_t stream);
+PKV_API int pkv_silu_mul(int32_t dtype, const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
+                         int64_t rows, int32_t intermediate, pkv_stream_t stream);
+
 /* ------------------------------------------------------------------ metadata builder (GPU) */
 /*
  * Decode metadata from a device-resident table mirror, instead of host lists

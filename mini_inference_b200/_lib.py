@@ -71,6 +71,9 @@ SIGNATURES: dict[str, tuple] = {
     "pkv_lm_head_argmax_workspace_bytes": (c_int64, [c_int32]),
     "pkv_lm_head_argmax": (c_int32, [c_void_p, c_int64, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int32,
                                      c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_void_p, c_void_p]),
+    "pkv_add_rms_norm": (c_int32, [c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+                                   c_void_p, c_int64, c_int64, c_int32, c_float, c_void_p]),
+    "pkv_silu_mul": (c_int32, [c_int32, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int32, c_void_p]),
     "pkv_decode_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64, c_int64,
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                        c_void_p, c_float, c_int32, c_void_p, c_int64, c_void_p, c_void_p]),

@@ -5,8 +5,10 @@ This is the caller side of the hot path: the reference's ``Qwen2ForCausalLM``
 parameters and the same tensor operations for everything around attention (embedding
 lookup, RMSNorm with float32 statistics, the fused ``qkv_proj`` with bias, ``o_proj``,
 the SwiGLU MLP with the fused ``gate_up_proj``, residual adds, the final norm and the
-tied or separate LM head). Those dense operations stay on PyTorch / cuBLAS; they are not
-part of the paged-KV path. Attention goes through the context the runner passes in:
+tied or separate LM head). The projections stay on cuBLAS through PyTorch; the residual
+adds, the RMSNorms and the MLP's ``silu(gate) * up`` are this package's kernels, one launch
+each (``ops.add_rms_norm``, ``ops.silu_mul``) where the reference runs eager chains of
+eight or more. Attention goes through the context the runner passes in:
 with this package's contexts the layer hands the raw ``qkv_proj`` output to
 ``ctx.attend_qkv``, which applies RoPE fused with the KV append (bit-identical to the
 reference's ``apply_rope``) and runs the paged attention kernels. A context without
@@ -123,13 +125,6 @@ def init_random(cfg: Qwen2Config, seed: int = 0, std: float = 0.02, dtype: torch
     return params
 
 
-def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """The reference's RMSNorm (engine/model.py:150-166): float32 statistics, then the model dtype."""
-    x32 = x.float()
-    x32 = x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + eps)
-    return weight * x32.to(x.dtype)
-
-
 def _rotate_half(x: torch.Tensor) -> torch.Tensor:
     x1, x2 = x.chunk(2, dim=-1)
     return torch.cat([-x2, x1], dim=-1)
@@ -186,13 +181,21 @@ class Qwen2Model:
         return self.forward(input_ids, positions, ctx)
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, ctx) -> torch.Tensor:
+        """engine/model.py:266-318: ``x = x + attn(norm(x)); x = x + mlp(norm(x))`` per layer, then the norm.
+
+        ``h`` is the residual stream ``x``; each block's output ``y`` is added into it by the
+        next norm's launch (``ops.add_rms_norm``, the reference's rounding), and the MLP's
+        ``silu(gate) * up`` is one launch (``ops.silu_mul``).
+        """
         eps = self.cfg.rms_norm_eps
-        x = F.embedding(input_ids, self.embed)
+        h = F.embedding(input_ids, self.embed)  # a fresh tensor: updated in place below
+        y = None
         for i, (n1, wqkv, bqkv, wo, n2, wgu, wd) in enumerate(self.layers):
-            x = x + self._attention(i, rms_norm(x, n1, eps), positions, ctx, wqkv, bqkv, wo)
-            gate, up = F.linear(rms_norm(x, n2, eps), wgu).chunk(2, dim=-1)
-            x = x + F.linear(F.silu(gate) * up, wd)
-        return rms_norm(x, self.norm, eps)
+            x = ops.add_rms_norm(h, n1, eps) if y is None else ops.add_rms_norm(y, n1, eps, residual=h)
+            y = self._attention(i, x, positions, ctx, wqkv, bqkv, wo)
+            x = ops.add_rms_norm(y, n2, eps, residual=h)
+            y = F.linear(ops.silu_mul(F.linear(x, wgu)), wd)
+        return ops.add_rms_norm(y, self.norm, eps, residual=h)
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         return F.linear(hidden, self.lm_head_weight)

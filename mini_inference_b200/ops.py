@@ -328,6 +328,63 @@ def lm_head_argmax(hidden: torch.Tensor, weight: torch.Tensor, workspace: torch.
     return out[:batch]
 
 
+def _rows2d(t: torch.Tensor, what: str) -> torch.Tensor:
+    """``t`` viewed as ``[rows, last]`` without a copy (its rows equally strided, the last dim contiguous)."""
+    if t.stride(-1) != 1:
+        raise ValueError(f"{what} must have a contiguous last dimension")
+    try:
+        return t.view(-1, t.shape[-1])
+    except RuntimeError as e:
+        raise ValueError(f"{what}'s leading dimensions must flatten to one row stride") from e
+
+
+def add_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's ``RMSNorm`` (engine/model.py:162-166), after an optional residual add, in one launch.
+
+    With ``residual``: ``residual`` becomes ``residual + x`` (in place, rounded to the dtype, as
+    the reference's ``x = x + block(x)``) and the result is the norm of that sum; without it,
+    the norm of ``x``. Returns ``out`` (a new tensor shaped like ``x`` unless given).
+    """
+    _require_cuda(x, weight, residual, out)
+    hidden = x.shape[-1]
+    if weight.shape != (hidden,) or weight.dtype != x.dtype or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [hidden] tensor of x's dtype")
+    x2 = _rows2d(x, "x")
+    r2 = None
+    if residual is not None:
+        if residual.shape != x.shape or residual.dtype != x.dtype:
+            raise ValueError("residual must match x in shape and dtype")
+        r2 = _rows2d(residual, "residual")
+    if out is None:
+        out = torch.empty_like(x)
+    if out.shape != x.shape or out.dtype != x.dtype:
+        raise ValueError("out must match x in shape and dtype")
+    o2 = _rows2d(out, "out")
+    check(lib.pkv_add_rms_norm(
+        pkv_dtype(x.dtype), x2.data_ptr(), x2.stride(0), _ptr(r2), r2.stride(0) if r2 is not None else 0, _ptr(r2),
+        r2.stride(0) if r2 is not None else 0, weight.data_ptr(), o2.data_ptr(), o2.stride(0), x2.shape[0], hidden,
+        float(eps), _stream()), "add_rms_norm")
+    return out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(gate) * up`` of ``gate_up = [..., 2 I]`` (engine/model.py:262-264) in one launch -> ``[..., I]``."""
+    _require_cuda(gate_up, out)
+    inter = gate_up.shape[-1] // 2
+    if gate_up.shape[-1] != 2 * inter:
+        raise ValueError("gate_up's last dimension must be even (gate | up)")
+    g2 = _rows2d(gate_up, "gate_up")
+    if out is None:
+        out = torch.empty(*gate_up.shape[:-1], inter, dtype=gate_up.dtype, device=gate_up.device)
+    if out.shape != (*gate_up.shape[:-1], inter) or out.dtype != gate_up.dtype:
+        raise ValueError("out must be [..., I] of gate_up's dtype")
+    o2 = _rows2d(out, "out")
+    check(lib.pkv_silu_mul(pkv_dtype(gate_up.dtype), g2.data_ptr(), g2.stride(0), o2.data_ptr(), o2.stride(0),
+                           g2.shape[0], inter, _stream()), "silu_mul")
+    return out
+
+
 def build_decode_metadata(tables: PkvTables, lengths: torch.Tensor, block_size: int, scratch_block: int,
                           positions: torch.Tensor, slot_mapping: torch.Tensor, context_lens: torch.Tensor,
                           status: torch.Tensor | None = None) -> None:

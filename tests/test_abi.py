@@ -112,3 +112,19 @@ def test_workspace_reset_validates_before_any_cuda_call():
 
     assert _lib.lib.pkv_decode_reset_workspace(None, 1 << 20, None) == _lib.PKV_ERR_INVALID_ARGUMENT
     assert _lib.lib.pkv_decode_static_scratch(None, None, None) == _lib.PKV_ERR_INVALID_ARGUMENT
+
+
+def test_layer_ops_validate_before_any_cuda_call():
+    from mini_inference_b200 import _lib
+
+    L, bad, uns = _lib.lib, _lib.PKV_ERR_INVALID_ARGUMENT, _lib.PKV_ERR_UNSUPPORTED
+    fake = 1 << 20  # never dereferenced: every case below is refused on the host
+    assert L.pkv_add_rms_norm(_lib.PKV_F16, None, 896, None, 0, None, 0, fake, fake, 896, 4, 896, 1e-6, None) == bad
+    assert L.pkv_add_rms_norm(_lib.PKV_F16, fake, 64, None, 0, None, 0, fake, fake, 896, 4, 896, 1e-6, None) == bad
+    assert L.pkv_add_rms_norm(_lib.PKV_F16, fake, 896, None, 0, None, 0, fake, fake, 896, 4, 896, -1.0, None) == bad
+    assert L.pkv_add_rms_norm(99, fake, 896, None, 0, None, 0, fake, fake, 896, 4, 896, 1e-6, None) == uns
+    assert L.pkv_add_rms_norm(_lib.PKV_F16, fake, 896, None, 0, None, 0, fake, fake, 896, 0, 896, 1e-6, None) == 0
+    assert L.pkv_silu_mul(_lib.PKV_F16, None, 9728, fake, 4864, 4, 4864, None) == bad
+    assert L.pkv_silu_mul(_lib.PKV_F16, fake, 4864, fake, 4864, 4, 4864, None) == bad  # gate_up row too short
+    assert L.pkv_silu_mul(99, fake, 9728, fake, 4864, 4, 4864, None) == uns
+    assert L.pkv_silu_mul(_lib.PKV_BF16, fake, 9728, fake, 4864, 0, 4864, None) == 0
