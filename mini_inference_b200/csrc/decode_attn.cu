@@ -289,19 +289,37 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   grid_dep_launch_dependents();
   if (!p.inputs_ready) grid_dep_wait();
 
-  for (int i = tid; i < B; i += blockDim.x) {
-    int ctx = p.context_lens[i];
-    int row = p.seq_rows ? p.seq_rows[i] : i;
-    if (ctx > cap_tokens) {
-      report(p.status, PKV_ERR_OUT_OF_RANGE);
-      ctx = cap_tokens;
+  // The split's per-sequence sums in three barrier-separated passes over chunks of 32
+  // sequences, chunk c held by warp c % 9 (one chunk per warp up to 288 sequences):
+  // (1) load lengths and table rows, chunk sums of blocks and non-empty sequences;
+  // (2) the rule and the cap from the totals, chunk-local scans of units / blocks;
+  // (3) add the chunks' carries. Each warp works on its own chunks in parallel.
+  __shared__ int s_ct[32], s_ci[32], s_ca[32], s_cb[32];
+  const int nchunks = (B + 31) / 32;
+  for (int base = warp * 32; base < B; base += kThreads) {
+    const int i = base + lane;
+    int n = 0;
+    if (i < B) {
+      int ctx = p.context_lens[i];
+      int row = p.seq_rows ? p.seq_rows[i] : i;
+      if (ctx > cap_tokens) {
+        report(p.status, PKV_ERR_OUT_OF_RANGE);
+        ctx = cap_tokens;
+      }
+      if (row >= p.table_rows) {
+        report(p.status, PKV_ERR_OUT_OF_RANGE);
+        row = -1;
+      }
+      ctx = max(ctx, 0);
+      sCtx[i] = ctx;
+      sRow[i] = row;
+      n = (ctx + kBS - 1) / kBS;
     }
-    if (row >= p.table_rows) {
-      report(p.status, PKV_ERR_OUT_OF_RANGE);
-      row = -1;
+    const int ct = warp_sum(n), ci = warp_sum(n > 0);
+    if (lane == 0) {
+      s_ct[base / 32] = ct;
+      s_ci[base / 32] = ci;
     }
-    sCtx[i] = max(ctx, 0);
-    sRow[i] = row;
   }
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -313,36 +331,48 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
     s_npend = 0;
   }
   __syncthreads();
-  if (warp == 0) {  // the split: which rule, then its per-sequence prefix sums
-    int tiles = 0, items = 0;
-    for (int i = lane; i < B; i += 32) {
-      const int n = (sCtx[i] + kBS - 1) / kBS;
-      tiles += n;
-      items += n > 0;
-    }
-    tiles = warp_sum(tiles);
-    items = warp_sum(items);
+  {
+    const int tiles = warp_sum(lane < nchunks ? s_ct[lane] : 0);
+    const int items = warp_sum(lane < nchunks ? s_ci[lane] : 0);
     const int flat = FLAT_OK && p.cap_override <= 0 && tiles >= p.flat_min * C;
     const int free_ctas = max(C - items, max(C / 4, 1));
     const int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
-    int carry_a = 0, carry_b = 0;
-    for (int base = 0; base < B; base += 32) {
+    for (int base = warp * 32; base < B; base += kThreads) {
       const int i = base + lane;
       const int n = i < B ? (sCtx[i] + kBS - 1) / kBS : 0;
       const int nch = n == 0 ? 0 : (n <= cap ? 1 : (n + cap - 1) / cap);
       const int pa = warp_scan(flat ? n : nch, lane), pb = warp_scan(nch > 1 ? nch : 0, lane);
       if (i < B) {
-        sA[i + 1] = carry_a + pa;
-        sB[i + 1] = carry_b + pb;
+        sA[i + 1] = pa;
+        sB[i + 1] = pb;
       }
-      carry_a += __shfl_sync(0xffffffffu, pa, 31);
-      carry_b += __shfl_sync(0xffffffffu, pb, 31);
+      if (lane == 31) {
+        s_ca[base / 32] = pa;
+        s_cb[base / 32] = pb;
+      }
     }
-    if (lane == 0) {
-      sA[0] = sB[0] = 0;
+    if (tid == 0) {
       s_flat = flat;
-      s_total = carry_a;
       s_q = max(p.min_quota, (tiles + C - 1) / C);
+    }
+  }
+  __syncthreads();
+  {
+    const int va = lane < nchunks ? s_ca[lane] : 0, vb = lane < nchunks ? s_cb[lane] : 0;
+    const int ia = warp_scan(va, lane), ib = warp_scan(vb, lane);
+    const int ea = ia - va, eb = ib - vb;  // units / blocks before chunk `lane`
+    for (int base = warp * 32; base < B; base += kThreads) {
+      const int i = base + lane;
+      const int ca = __shfl_sync(0xffffffffu, ea, base / 32), cb = __shfl_sync(0xffffffffu, eb, base / 32);
+      if (i < B) {
+        sA[i + 1] += ca;
+        sB[i + 1] += cb;
+      }
+    }
+    const int total = __shfl_sync(0xffffffffu, ia, 31);
+    if (tid == 0) {
+      sA[0] = sB[0] = 0;
+      s_total = total;
     }
   }
   __syncthreads();
