@@ -41,8 +41,7 @@ class _GraphDecodeContext:
         self.cache = cache
         self.batch = batch
         dev = cache.device
-        self.seq_rows = owner.rows[:batch]
-        self.lengths_in = owner.lengths[:batch]
+        self.ids, self.seq_rows, self.lengths_in = owner.staged_views(batch)
         self.tables = ops.make_tables(cache.tables_dev, self.seq_rows)
         # Written inside the graph on every replay; allocated here so the graph owns them.
         self.positions = torch.empty(batch, dtype=torch.int64, device=dev)
@@ -94,9 +93,13 @@ class GraphedDecoder:
         self.device = cache.device
         self.batch_buckets = _batch_buckets(min(max_batch, cache.max_seqs))
         top = self.batch_buckets[-1]
-        self.ids = torch.zeros(top, 1, dtype=torch.long, device=self.device)
-        self.rows = torch.full((top,), -1, dtype=torch.int32, device=self.device)  # -1: a padding row
-        self.lengths = torch.zeros(top, dtype=torch.int32, device=self.device)
+        # A step's inputs, read in place by its graph: for a bucket of b rows, b int64 token
+        # ids, then b int32 table rows (-1: a padding row) and b int32 lengths, 16 b bytes in
+        # all, filled in pinned host memory and sent with one copy per step.
+        self._staged_dev = torch.zeros(16 * top, dtype=torch.uint8, device=self.device)
+        self._staged_host = torch.zeros(16 * top, dtype=torch.uint8).pin_memory()
+        self._staged_np = self._staged_host.numpy()
+        self._staged_sent = torch.cuda.Event()  # the last copy out of the pinned buffer
         # batch -> (graph, its logits, its context); the context stays alive with its graph.
         self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, torch.Tensor, _GraphDecodeContext]] = {}
         self._pool = None
@@ -104,6 +107,16 @@ class GraphedDecoder:
         # When a list, every decode() appends a (start, end) pair of CUDA events around its
         # copies and replay, for device-side timing of the steps.
         self.timing: list | None = None
+
+    def staged_views(self, batch: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """The device inputs of a ``batch``-row graph: ids ``[batch, 1]`` int64, table rows and lengths int32."""
+        buf = self._staged_dev[:16 * batch]
+        return (buf[:8 * batch].view(torch.int64).view(batch, 1), buf[8 * batch:12 * batch].view(torch.int32),
+                buf[12 * batch:].view(torch.int32))
+
+    def _host_views(self, batch: int) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        buf = self._staged_np[:16 * batch]
+        return buf[:8 * batch].view(np.int64), buf[8 * batch:12 * batch].view(np.int32), buf[12 * batch:].view(np.int32)
 
     @torch.inference_mode()
     def capture(self) -> None:
@@ -117,13 +130,15 @@ class GraphedDecoder:
 
         def step() -> torch.Tensor:
             ctx.prepare()
-            hidden = self.model(self.ids[:batch], ctx.positions.unsqueeze(1), ctx)
+            hidden = self.model(ctx.ids, ctx.positions.unsqueeze(1), ctx)
             if self.head is not None:
                 return self.head(hidden[:, -1])
             return self.model.compute_logits(hidden[:, -1]).float()
 
-        self.rows.fill_(-1)  # every row reads and writes the scratch block while recording
-        self.lengths.zero_()
+        ids, rows, lengths = ctx.ids, ctx.seq_rows, ctx.lengths_in
+        ids.zero_()
+        rows.fill_(-1)  # every row reads and writes the scratch block while recording
+        lengths.zero_()
         self.cache.sync_tables()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -154,18 +169,21 @@ class GraphedDecoder:
         if self.cache.enable_copy_on_write:
             self.cache.copy_on_write([(s, int(p), 1) for s, p in zip(slots_np.tolist(), positions.tolist())])
         self.cache.sync_tables()
-        host = np.zeros((3, batch), dtype=np.int64)
-        host[0, :n] = np.asarray(list(last_tokens), dtype=np.int64)
-        host[1, :] = -1
-        host[1, :n] = slots_np
-        host[2, :n] = positions
+        # The pinned buffer is rewritten only after the previous step's copy out of it ran
+        # (already so when the caller read that step's tokens).
+        self._staged_sent.synchronize()
+        h_ids, h_rows, h_len = self._host_views(batch)
+        h_ids[:n] = last_tokens
+        h_ids[n:] = 0
+        h_rows[:n] = slots_np
+        h_rows[n:] = -1
+        h_len[:n] = positions
+        h_len[n:] = 0
         if self.timing is not None:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
-        staged = torch.from_numpy(host).pin_memory().to(self.device, non_blocking=True)
-        self.ids[:batch, 0].copy_(staged[0])
-        self.rows[:batch].copy_(staged[1])
-        self.lengths[:batch].copy_(staged[2])
+        self._staged_dev[:16 * batch].copy_(self._staged_host[:16 * batch], non_blocking=True)
+        self._staged_sent.record()
         graph.replay()
         if self.timing is not None:
             end.record()

@@ -280,18 +280,18 @@ class LLMEngine:
             new_tokens.extend((s.seq_id, t) for s, t in done)
         ctx_tokens = 0
         if batch.decodes:
-            ctx_tokens = sum(s.num_tokens for s in batch.decodes)
+            ctx_tokens = sum(len(s.prompt_token_ids) + len(s.output_token_ids) for s in batch.decodes)
             # The token at the sequence's last position: its last output, or (chunked prefill)
             # the last prompt token when the final chunk left exactly that one.
             tokens = self.runner.decode_tokens([s.slot for s in batch.decodes],
-                                               [s.token_ids[-1] for s in batch.decodes])
+                                               [(s.output_token_ids or s.prompt_token_ids)[-1] for s in batch.decodes])
             self.scheduler.append_tokens(batch.decodes, tokens, time.perf_counter())
             new_tokens.extend((s.seq_id, t) for s, t in zip(batch.decodes, tokens))
         self.step_stats.append(StepStats(
             step=len(self.step_stats), time=time.perf_counter(), num_prefills=len(batch.prefills),
             num_prefill_tokens=n_prefill_tokens, num_decodes=len(batch.decodes), decode_context_tokens=ctx_tokens,
             num_finished=sum(s.is_finished for s in batch.prefills + batch.decodes),
-            num_running=len(self.scheduler.running), num_waiting=len(self.scheduler.waiting)))
+            num_running=self.scheduler.num_running, num_waiting=self.scheduler.num_waiting))
         return new_tokens
 
     def abort_request(self, request_id: int) -> None:

@@ -133,6 +133,20 @@ class Scheduler:
         return [self._seqs[i] for i in self._queues()[1]]
 
     @property
+    def num_waiting(self) -> int:
+        """``len(self.waiting)`` without building the queue."""
+        _check(lib.pkv_sched_counts(self._h, ctypes.byref(self._i32a), ctypes.byref(self._i32b),
+                                    ctypes.byref(self._i64)), "scheduler counts")
+        return self._i32a.value
+
+    @property
+    def num_running(self) -> int:
+        """``len(self.running)`` without building the list."""
+        _check(lib.pkv_sched_counts(self._h, ctypes.byref(self._i32a), ctypes.byref(self._i32b),
+                                    ctypes.byref(self._i64)), "scheduler counts")
+        return self._i32b.value
+
+    @property
     def num_preemptions(self) -> int:
         _check(lib.pkv_sched_counts(self._h, ctypes.byref(self._i32a), ctypes.byref(self._i32b),
                                     ctypes.byref(self._i64)), "scheduler counts")
