@@ -41,6 +41,7 @@ struct NormParams {
 template <typename T, int EW, int P>
 __global__ void __launch_bounds__(1024) add_rms_norm_kernel(const NormParams p) {
   __shared__ float s_part[32];
+  grid_dep_launch_dependents();  // a kernel that reads only weights may start early
   const int64_t row = blockIdx.x;
   const int packs = p.hidden / EW;
   const T* x = static_cast<const T*>(p.x) + row * p.x_stride;

@@ -279,18 +279,19 @@ class LLMEngine:
             self.scheduler.append_tokens([s for s, _ in done], [t for _, t in done], time.perf_counter())
             new_tokens.extend((s.seq_id, t) for s, t in done)
         ctx_tokens = 0
+        n_finished = sum(s.is_finished for s in batch.prefills)
         if batch.decodes:
             ctx_tokens = sum(len(s.prompt_token_ids) + len(s.output_token_ids) for s in batch.decodes)
             # The token at the sequence's last position: its last output, or (chunked prefill)
             # the last prompt token when the final chunk left exactly that one.
             tokens = self.runner.decode_tokens([s.slot for s in batch.decodes],
                                                [(s.output_token_ids or s.prompt_token_ids)[-1] for s in batch.decodes])
-            self.scheduler.append_tokens(batch.decodes, tokens, time.perf_counter())
-            new_tokens.extend((s.seq_id, t) for s, t in zip(batch.decodes, tokens))
+            n_finished += self.scheduler.append_tokens(batch.decodes, tokens, time.perf_counter())
+            new_tokens.extend(zip((s.seq_id for s in batch.decodes), tokens))
         self.step_stats.append(StepStats(
             step=len(self.step_stats), time=time.perf_counter(), num_prefills=len(batch.prefills),
             num_prefill_tokens=n_prefill_tokens, num_decodes=len(batch.decodes), decode_context_tokens=ctx_tokens,
-            num_finished=sum(s.is_finished for s in batch.prefills + batch.decodes),
+            num_finished=n_finished,
             num_running=self.scheduler.num_running, num_waiting=self.scheduler.num_waiting))
         return new_tokens
 

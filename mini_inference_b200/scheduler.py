@@ -199,17 +199,21 @@ class Scheduler:
         """Record a newly sampled token and finish the sequence if it is done."""
         self.append_tokens([seq], [token], now)
 
-    def append_tokens(self, seqs: SequenceOf, tokens: SequenceOf[int], now: float) -> None:
-        """``append_token`` for a whole step's sequences in one call (same order, same effects)."""
+    def append_tokens(self, seqs: SequenceOf, tokens: SequenceOf[int], now: float) -> int:
+        """``append_token`` for a whole step's sequences in one call (same order, same effects).
+
+        Returns how many of them finished.
+        """
         n = len(seqs)
         if n == 0:
-            return
+            return 0
         ids = np.fromiter((s.seq_id for s in seqs), dtype=np.int64, count=n)
         toks = np.asarray(tokens, dtype=np.int64)
         reasons = np.zeros(n, np.int32)
         _check(lib.pkv_sched_append_tokens(self._h, ids.ctypes.data, toks.ctypes.data, n, reasons.ctypes.data),
                "scheduler append")
         finished = self._status.FINISHED
+        n_done = 0
         for seq, token, why in zip(seqs, toks.tolist(), reasons.tolist()):
             seq.output_token_ids.append(token)
             if seq.first_token_time is None:
@@ -220,6 +224,8 @@ class Scheduler:
                 seq.finish_time = now
                 seq.slot = None
                 del self._seqs[seq.seq_id]
+                n_done += 1
+        return n_done
 
     def abort(self, seq, now: float) -> None:
         """Cancel a request wherever it is: drop it from the queue, or finish it and free its slot."""
