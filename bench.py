@@ -1169,6 +1169,32 @@ def run_prefix_serving(args, rank: int, world: int, local: int, model=None) -> d
             "ttft_p95_s": round(float(np.percentile(ttft, 95)), 4)}
 
 
+def profile_serving_step(warm_steps: int = 40, steps: int = 5) -> None:
+    """Per-kernel device time of config 3's graphed decode step once the batch has formed."""
+    from torch.profiler import ProfilerActivity, profile
+
+    from mini_inference_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from mini_inference_b200.model import Qwen2Config, Qwen2Model, init_random
+
+    dev = torch.device("cuda", 0)
+    cfg = Qwen2Config.qwen2_0_5b()
+    model = Qwen2Model(cfg, init_random(cfg, seed=0, std=0.02, dtype=torch.float16, device=dev,
+                                        generator_device="cuda"))
+    engine = LLMEngine(model, EngineConfig(max_num_seqs=SERVE_MAX_SEQS, max_model_len=SERVE_MAX_LEN,
+                                           max_num_batched_tokens=SERVE_BUDGET, kv_cache_tokens=SERVE_KV_TOKENS))
+    for prompt, n in serving_workload(seed=0, vocab=cfg.vocab_size):
+        engine.add_request(prompt, SamplingParams(max_tokens=n, ignore_eos=True))
+    for _ in range(warm_steps):
+        engine.step()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            engine.step()
+        torch.cuda.synchronize()
+    print(f"{steps} decode steps at {engine.step_stats[-1].num_decodes} sequences")
+    print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=20, max_name_column_width=70))
+
+
 def sum_over_ranks(value: int, world: int) -> int:
     if world == 1:
         return value
@@ -1320,6 +1346,8 @@ def main() -> None:
                     help="only the config-3 serving leg (under torchrun: every rank its share)")
     ap.add_argument("--profile-case", action="store_true",
                     help="small case for ncu captures: 4 layer pools (536 MB, still above L2), no e2e / CPU legs")
+    ap.add_argument("--serving-profile", action="store_true",
+                    help="print the kernels of 5 graphed config-3 decode steps (torch profiler device times)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
     args.layers = 4 if args.profile_case else LAYERS
@@ -1333,6 +1361,9 @@ def main() -> None:
                else run_lm_head if args.lm_head_only else run_long_step if args.long_step_only else run_qkv_post)
         res = run(dev, seed=0) if args.long_step_only else run(dev, seed=0, reps=args.steps)
         print(json.dumps(res), flush=True)
+        return
+    if args.serving_profile:
+        profile_serving_step()
         return
     rank, world, local = dist_setup(args.gpus)
     try:
