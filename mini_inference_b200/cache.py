@@ -57,7 +57,7 @@ class NativeBlockManager:
 
     def __del__(self) -> None:
         h = getattr(self, "_h", None)
-        if h is not None and h.value:
+        if h is not None and h.value and lib is not None:  # lib is gone at interpreter exit
             lib.pkv_bm_destroy(h)
             self._h = None
 
@@ -311,7 +311,13 @@ class PagedKVCache:
                                          device=self.device)
             self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.pool = ops.make_pool(self.k, self.v)
-            self._edits = np.zeros((max(1024, 2 * num_blocks), 3), np.int32)
+            # The allocator's table edits are drained straight into pinned memory and sent
+            # with one copy per sync; the buffer is refilled only after that copy ran.
+            cap = max(1024, 2 * num_blocks)
+            self._edits_host = torch.zeros((cap, 3), dtype=torch.int32).pin_memory()
+            self._edits = self._edits_host.numpy()
+            self._edits_dev = torch.empty((cap, 3), dtype=torch.int32, device=self.device)
+            self._edits_sent = torch.cuda.Event()
             self._bm.set_journal(True)
             self._workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
@@ -396,12 +402,15 @@ class PagedKVCache:
         """Push the allocator's table edits since the last sync to the device mirror."""
         if not self.on_gpu:
             return
+        self._edits_sent.synchronize()
         n, overflow = self._bm.drain_edits(self._edits)
         if overflow:
             self._rebuild_mirror()
             return
         if n:
-            upd = torch.from_numpy(self._edits[:n].copy()).pin_memory().to(self.device, non_blocking=True)
+            upd = self._edits_dev[:n]
+            upd.copy_(self._edits_host[:n], non_blocking=True)
+            self._edits_sent.record()
             ops.update_tables(self.tables_dev, upd, self.status)
 
     def _rebuild_mirror(self) -> None:

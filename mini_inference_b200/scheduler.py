@@ -110,7 +110,7 @@ class Scheduler:
 
     def __del__(self) -> None:
         h = getattr(self, "_h", None)
-        if h is not None and h.value:
+        if h is not None and h.value and lib is not None:  # lib is gone at interpreter exit
             lib.pkv_sched_destroy(h)
             self._h = None
 
