@@ -46,13 +46,13 @@ template <int D, bool SPLIT> struct PrefillShape {
   static constexpr int KSB = DC * kNK * 128;         // one stage of K (or V): [DC][NK keys][64], 128B-swizzled
   static constexpr int QB = DC * 128 * 128;          // Q tile in shared memory: [DC][128 rows][64]
   // TMEM columns: two S buffers at 0 and NK, O at 2 NK, then Q (packed 16-bit pairs, when
-  // it fits), then P (32 columns of packed pairs; bf16 adds its lo half in 32 more). At
-  // head_dim 64 with bf16, Q stays in shared memory so that a CTA needs 256 columns.
+  // it fits). P(j) is written over S(j) in S(j)'s own buffer (32 columns of packed pairs;
+  // bf16 adds its lo half in the next 32). At head_dim 64 with bf16, Q stays in shared
+  // memory.
   static constexpr bool QT = !(SPLIT && D == 64);
   static constexpr int OCOL = 2 * kNK;
   static constexpr int QCOL = OCOL + D;
-  static constexpr int PCOL = QCOL + (QT ? D / 2 : 0);
-  static constexpr int COLS = PCOL + (SPLIT ? 2 : 1) * (kNK / 2);
+  static constexpr int COLS = QCOL + (QT ? D / 2 : 0);
   static constexpr int NCOLS = COLS <= 128 ? 128 : (COLS <= 256 ? 256 : 512);
   static constexpr int MIN_BLOCKS = NCOLS <= 256 ? 2 : 1;
   // Softmax warps: one per TMEM lane quarter (a whole row per thread) when two CTAs share an
@@ -80,11 +80,12 @@ struct PrefillParams {
 };
 
 // Pipeline (stage i = keys 64 i .. 64 i + 63). The MMA thread issues S(0) and S(1), then
-// for each i, as one burst once the softmax warps stored P(i): O += P(i) V(i), then
-// S(i+2) = Q K(i+2)^T into the S buffer that P(i) was made from. The softmax warps turn
-// S(i) into P(i) while the tensor cores compute O(i-1) and S(i+1). P (and Q where it
-// fits) is the A operand straight from TMEM, so most MMAs read only K or V from shared
-// memory. An MMA burst costs several hundred cycles to issue however small it is
+// for each i, once the softmax warps stored P(i): O += P(i) V(i), then (after that MMA
+// completed) S(i+2) = Q K(i+2)^T into the buffer that held S(i) and P(i). The softmax warps
+// turn S(i) into P(i) in place, in S(i)'s buffer, while the tensor cores compute O(i-1)
+// and S(i+1): P(i) never waits for O(i-1), which reads P(i-1) from the other buffer. P (and
+// Q where it fits) is the A operand straight from TMEM, so most MMAs read only K or V from
+// shared memory. An MMA burst costs several hundred cycles to issue however small it is
 // (measured), which is why each stage has one burst rather than two.
 template <typename T, int D, int TQ>
 __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, PrefillShape<D, !Dt<T>::kExactP>::MIN_BLOCKS)
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
       // the MMAs of a group issue back to back (a probe measured ~45 cycles per MMA that way
       // against ~120 with each descriptor computed just before its MMA).
       auto pin = [](uint64_t& x) { asm volatile("" : "+l"(x)); };
-      auto issue_s = [&](int j) -> bool {  // S(j) into buffer j % 2, whose S(j - 2) P(j - 2) was made from
+      auto issue_s = [&](int j, bool after_o) -> bool {  // S(j) into buffer j % 2, over P(j - 2)
         const int st = j % kKS, b = j % 2;
         uint64_t bk[D / 16], aq[D / 16];
 #pragma unroll
@@ -281,6 +282,8 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
           pin(aq[kk]);
         }
         if (!mbar_wait_until(&k_full[st], (j / kKS) & 1, deadline)) return false;
+        // Within an item, P(j - 2) lives in this buffer until O(j - 2) has read it.
+        if (after_o && !mbar_wait_until(&o_done[(j - 2) % kVS], ((j - 2) / kVS) & 1, deadline)) return false;
         tc_fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -308,21 +311,22 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
         for (int h = 0; h < NP; ++h) {
 #pragma unroll
           for (int kb = 0; kb < kNK / 16; ++kb)
-            umma_f16_ts(tmem + S::OCOL, tmem + S::PCOL + h * (kNK / 2) + kb * 8, bv[kb], idesc_o,
+            umma_f16_ts(tmem + S::OCOL, tmem + s_col(b) + h * (kNK / 2) + kb * 8, bv[kb], idesc_o,
                         !first || h > 0 || kb > 0);
         }
         umma_commit(&o_done[st]);
         return true;
       };
-      // p_full(j) also means the softmax warps have read S(j), so S(j + 2) may overwrite it.
-      // q_ready(k) comes after the softmax warps read item k - 1's O and waited for all its
-      // S: item k's first S and its O-overwriting first P V may go.
+      // S(j + 2) overwrites P(j) once O(j) has read it. q_ready(k) comes after the softmax
+      // warps read item k - 1's O (so every O of that item completed) and waited for all its
+      // S: item k's first two S and its O-overwriting first P V may go.
       bool ok = true;
       int gs = 0, k = 0;
       for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x, ++k) {
         const int nst = item_at(w).nst;
-        ok = mbar_wait_until(q_ready, k & 1, deadline) && issue_s(gs) && (nst < 2 || issue_s(gs + 1));
-        for (int i = 0; i < nst && ok; ++i) ok = issue_o(gs + i, i == 0) && (i + 2 >= nst || issue_s(gs + i + 2));
+        ok = mbar_wait_until(q_ready, k & 1, deadline) && issue_s(gs, false) && (nst < 2 || issue_s(gs + 1, false));
+        for (int i = 0; i < nst && ok; ++i)
+          ok = issue_o(gs + i, i == 0) && (i + 2 >= nst || issue_s(gs + i + 2, true));
         gs += nst;
       }
       if (!ok) report(p.status, PKV_ERR_TIMEOUT);
@@ -466,15 +470,17 @@ __global__ void __launch_bounds__(PrefillShape<D, !Dt<T>::kExactP>::THREADS, Pre
         }
         lsum[(e / 2) % 2] = fadd2(lsum[(e / 2) % 2], make_float2(p0, p1));
       }
-      // P(i) replaces P(i - 1), which O(i - 1) must have consumed: keys KH hf .. + KH - 1
-      // are packed columns KH / 2 hf .. + KH / 2 - 1 (lo half NK / 2 further).
-      if (i > 0) confirm(j - 1);  // the item's first P follows the previous item's last O, confirmed
+      // P(i) goes over S(i), in its buffer: keys KH hf .. + KH - 1 are packed columns
+      // KH / 2 hf .. + KH / 2 - 1 (lo half NK / 2 further). This thread's S loads completed
+      // above and, with two halves per row, the pair barrier ordered the other half's too;
+      // O(i - 2), which read the buffer's previous P, completed before S(i) was written.
       tc_fence_after_sync();
 #pragma unroll
       for (int c = 0; c < KH / 32; ++c) {
-        tmem_st16(tl + S::PCOL + hf * (KH / 2) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + c * 16));
+        tmem_st16(tl + s_col(b) + hf * (KH / 2) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + c * 16));
         if (kSplit)
-          tmem_st16(tl + S::PCOL + kNK / 2 + hf * (KH / 2) + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(pl + c * 16));
+          tmem_st16(tl + s_col(b) + kNK / 2 + hf * (KH / 2) + c * 16,
+                    *reinterpret_cast<const uint32_t(*)[16]>(pl + c * 16));
       }
       tmem_wait_st();
       tc_fence_before_sync();
