@@ -413,6 +413,19 @@ class PagedKVCache:
             self._edits_sent.record()
             ops.update_tables(self.tables_dev, upd, self.status)
 
+    def drain_table_edits(self, buf: np.ndarray) -> int:
+        """Move the allocator's pending table edits into ``buf`` (int32 ``[cap, 3]``); returns how many.
+
+        The caller applies them to ``tables_dev`` (``ops.update_tables``) before its next
+        kernel reads the tables. If more were pending than ``buf`` holds, the device mirror
+        is rebuilt from the allocator here instead and 0 is returned.
+        """
+        n, overflow = self._bm.drain_edits(buf)
+        if overflow:
+            self._rebuild_mirror()
+            return 0
+        return n
+
     def _rebuild_mirror(self) -> None:
         rows = torch.full((self.max_seqs, self.max_blocks_per_seq), -1, dtype=torch.int32)
         for s in self._bm.live_slots():

@@ -96,8 +96,11 @@ class GraphedDecoder:
         # A step's inputs, read in place by its graph: for a bucket of b rows, b int64 token
         # ids, then b int32 table rows (-1: a padding row) and b int32 lengths, 16 b bytes in
         # all, filled in pinned host memory and sent with one copy per step.
-        self._staged_dev = torch.zeros(16 * top, dtype=torch.uint8, device=self.device)
-        self._staged_host = torch.zeros(16 * top, dtype=torch.uint8).pin_memory()
+        # The step's table edits (int32 triples) follow the inputs in the same copy.
+        self._edit_cap = max(1024, 2 * cache.max_seqs * cache.max_blocks_per_seq)
+        nbytes = 16 * top + 12 * self._edit_cap
+        self._staged_dev = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        self._staged_host = torch.zeros(nbytes, dtype=torch.uint8).pin_memory()
         self._staged_np = self._staged_host.numpy()
         self._staged_sent = torch.cuda.Event()  # the last copy out of the pinned buffer
         # batch -> (graph, its logits, its context); the context stays alive with its graph.
@@ -168,10 +171,11 @@ class GraphedDecoder:
         positions = self.cache._bm.decode_positions(slots_np)  # raises the reference's ValueError
         if self.cache.enable_copy_on_write:
             self.cache.copy_on_write([(s, int(p), 1) for s, p in zip(slots_np.tolist(), positions.tolist())])
-        self.cache.sync_tables()
         # The pinned buffer is rewritten only after the previous step's copy out of it ran
         # (already so when the caller read that step's tokens).
         self._staged_sent.synchronize()
+        edits = self._staged_np[16 * batch:16 * batch + 12 * self._edit_cap].view(np.int32).reshape(-1, 3)
+        n_edits = self.cache.drain_table_edits(edits)
         h_ids, h_rows, h_len = self._host_views(batch)
         h_ids[:n] = last_tokens
         h_ids[n:] = 0
@@ -182,8 +186,12 @@ class GraphedDecoder:
         if self.timing is not None:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
-        self._staged_dev[:16 * batch].copy_(self._staged_host[:16 * batch], non_blocking=True)
+        nbytes = 16 * batch + 12 * n_edits
+        self._staged_dev[:nbytes].copy_(self._staged_host[:nbytes], non_blocking=True)
         self._staged_sent.record()
+        if n_edits:  # the allocator's new blocks, before the graph reads the tables
+            dev_edits = self._staged_dev[16 * batch:nbytes].view(torch.int32).view(n_edits, 3)
+            ops.update_tables(self.cache.tables_dev, dev_edits, self.cache.status)
         graph.replay()
         if self.timing is not None:
             end.record()
