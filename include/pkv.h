@@ -307,6 +307,19 @@ PKV_API int pkv_add_rms_norm(int32_t dtype, const void* x, int64_t x_stride, con
                              int64_t residual_in_stride, void* residual_out, int64_t residual_out_stride,
                              const void* weight, void* out, int64_t out_stride, int64_t rows, int32_t hidden,
                              float eps, pkv_stream_t stream);
+/*
+ * pkv_add_rms_norm with x given as split-K partial sums of the block's output projection:
+ * partials[s][r][c] at partials + s*split_stride + r*row_stride + c (float32, splits >= 1),
+ * as a GEMM cut along K leaves them (e.g. a batched GEMM with float32 output). x = round(sum
+ * of the splits in order), the projection's output as F.linear would round it; the rest is
+ * pkv_add_rms_norm's. Lets a long-K projection of a decode batch (down_proj, K = 4864) run on
+ * more SMs without a separate reduction launch.
+ */
+PKV_API int pkv_add_rms_norm_partials(int32_t dtype, const float* partials, int64_t row_stride, int32_t splits,
+                                      int64_t split_stride, const void* residual_in, int64_t residual_in_stride,
+                                      void* residual_out, int64_t residual_out_stride, const void* weight,
+                                      void* out, int64_t out_stride, int64_t rows, int32_t hidden, float eps,
+                                      pkv_stream_t stream);
 PKV_API int pkv_silu_mul(int32_t dtype, const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
                          int64_t rows, int32_t intermediate, pkv_stream_t stream);
 

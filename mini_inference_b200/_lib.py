@@ -73,6 +73,9 @@ SIGNATURES: dict[str, tuple] = {
                                      c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_void_p, c_void_p]),
     "pkv_add_rms_norm": (c_int32, [c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
                                    c_void_p, c_int64, c_int64, c_int32, c_float, c_void_p]),
+    "pkv_add_rms_norm_partials": (c_int32, [c_int32, c_void_p, c_int64, c_int32, c_int64, c_void_p, c_int64,
+                                            c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_float,
+                                            c_void_p]),
     "pkv_silu_mul": (c_int32, [c_int32, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int32, c_void_p]),
     "pkv_decode_attention": (c_int32, [P_POOL, c_int32, P_TABLES, c_int32, c_int32, c_void_p, c_int64, c_int64,
                                        c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,

@@ -28,7 +28,9 @@ template <typename T, int EW> struct alignas(EW * sizeof(T)) Vec {
 };
 
 struct NormParams {
-  const void* x;
+  const void* x;            // [rows, hidden] of T, or with splits > 0: float partials [splits][rows][hidden]
+  int64_t split_stride;     // elements between the partials of consecutive splits
+  int32_t splits;
   const void* residual_in;
   void* residual_out;
   const void* weight;
@@ -38,13 +40,16 @@ struct NormParams {
   float eps;
 };
 
-template <typename T, int EW, int P>
+// PART: x arrives as split-K partial sums in float32 (a GEMM cut along K); their sum,
+// slice by slice in order and rounded to T, is the projection's output the reference's
+// F.linear would have rounded.
+template <typename T, int EW, int P, bool PART>
 __global__ void __launch_bounds__(1024) add_rms_norm_kernel(const NormParams p) {
   __shared__ float s_part[32];
   grid_dep_launch_dependents();  // a kernel that reads only weights may start early
   const int64_t row = blockIdx.x;
   const int packs = p.hidden / EW;
-  const T* x = static_cast<const T*>(p.x) + row * p.x_stride;
+  const T* x = PART ? nullptr : static_cast<const T*>(p.x) + row * p.x_stride;
   const T* rin = p.residual_in ? static_cast<const T*>(p.residual_in) + row * p.rin_stride : nullptr;
   T* rout = p.residual_out ? static_cast<T*>(p.residual_out) + row * p.rout_stride : nullptr;
   float h[P][EW];
@@ -53,7 +58,29 @@ __global__ void __launch_bounds__(1024) add_rms_norm_kernel(const NormParams p) 
   for (int k = 0; k < P; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
     if (c < packs) {
-      Vec<T, EW> a = reinterpret_cast<const Vec<T, EW>*>(x)[c];
+      Vec<T, EW> a;
+      if constexpr (PART) {
+        const float* xp = static_cast<const float*>(p.x) + row * p.x_stride + (int64_t)c * EW;
+        float acc[EW];
+#pragma unroll
+        for (int e = 0; e < EW; ++e) acc[e] = 0.f;
+        for (int sp = 0; sp < p.splits; ++sp) {
+          const float* q = xp + sp * p.split_stride;
+#pragma unroll
+          for (int e = 0; e < EW; e += (EW >= 4 ? 4 : 1)) {
+            if constexpr (EW >= 4) {
+              const float4 v = *reinterpret_cast<const float4*>(q + e);
+              acc[e] += v.x, acc[e + 1] += v.y, acc[e + 2] += v.z, acc[e + 3] += v.w;
+            } else {
+              acc[e] += q[e];
+            }
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < EW; ++e) a.v[e] = Dt<T>::from_f(acc[e]);
+      } else {
+        a = reinterpret_cast<const Vec<T, EW>*>(x)[c];
+      }
       if (rin) {
         const Vec<T, EW> b = reinterpret_cast<const Vec<T, EW>*>(rin)[c];
 #pragma unroll
@@ -94,7 +121,7 @@ __global__ void __launch_bounds__(1024) add_rms_norm_kernel(const NormParams p) 
   }
 }
 
-template <typename T, int EW>
+template <typename T, int EW, bool PART>
 int launch_norm(const NormParams& p, int64_t rows, cudaStream_t st) {
   const int packs = p.hidden / EW;
   // Fewest packs per thread that keep the CTA at or below 1024 threads.
@@ -104,10 +131,10 @@ int launch_norm(const NormParams& p, int64_t rows, cudaStream_t st) {
   const int threads = (((packs + P - 1) / P) + 31) / 32 * 32;
   const unsigned grid = (unsigned)rows;
   switch (P) {
-    case 1: add_rms_norm_kernel<T, EW, 1><<<grid, threads, 0, st>>>(p); break;
-    case 2: add_rms_norm_kernel<T, EW, 2><<<grid, threads, 0, st>>>(p); break;
-    case 4: add_rms_norm_kernel<T, EW, 4><<<grid, threads, 0, st>>>(p); break;
-    default: add_rms_norm_kernel<T, EW, 8><<<grid, threads, 0, st>>>(p); break;
+    case 1: add_rms_norm_kernel<T, EW, 1, PART><<<grid, threads, 0, st>>>(p); break;
+    case 2: add_rms_norm_kernel<T, EW, 2, PART><<<grid, threads, 0, st>>>(p); break;
+    case 4: add_rms_norm_kernel<T, EW, 4, PART><<<grid, threads, 0, st>>>(p); break;
+    default: add_rms_norm_kernel<T, EW, 8, PART><<<grid, threads, 0, st>>>(p); break;
   }
   return launch_status();
 }
@@ -164,19 +191,26 @@ bool aligned(const void* ptr, int bytes) { return (reinterpret_cast<uintptr_t>(p
 
 using namespace pkv;
 
-extern "C" int pkv_add_rms_norm(int32_t dtype, const void* x, int64_t x_stride, const void* residual_in,
-                                int64_t residual_in_stride, void* residual_out, int64_t residual_out_stride,
-                                const void* weight, void* out, int64_t out_stride, int64_t rows, int32_t hidden,
-                                float eps, pkv_stream_t stream) {
-  if (!x || !weight || !out || rows < 0 || hidden <= 0 || !(eps >= 0.f)) return PKV_ERR_INVALID_ARGUMENT;
+namespace pkv {
+namespace {
+
+// splits == 0: x is [rows, hidden] of the model dtype; else float32 partials [splits][rows][hidden].
+int norm_entry(int32_t dtype, const void* x, int64_t x_stride, int32_t splits, int64_t split_stride,
+               const void* residual_in, int64_t residual_in_stride, void* residual_out, int64_t residual_out_stride,
+               const void* weight, void* out, int64_t out_stride, int64_t rows, int32_t hidden, float eps,
+               pkv_stream_t stream) {
+  if (!x || !weight || !out || rows < 0 || hidden <= 0 || !(eps >= 0.f) || splits < 0) return PKV_ERR_INVALID_ARGUMENT;
   if (dtype != PKV_F16 && dtype != PKV_BF16) return PKV_ERR_UNSUPPORTED;
   if (x_stride < hidden || out_stride < hidden || (residual_in && residual_in_stride < hidden) ||
       (residual_out && residual_out_stride < hidden))
     return PKV_ERR_INVALID_ARGUMENT;
+  if (splits > 0 && split_stride < rows * x_stride) return PKV_ERR_INVALID_ARGUMENT;
   if (rows == 0) return PKV_OK;
   if (rows > 0x7fffffff) return PKV_ERR_INVALID_ARGUMENT;
   NormParams p;
   p.x = x;
+  p.split_stride = split_stride;
+  p.splits = splits;
   p.residual_in = residual_in;
   p.residual_out = residual_out;
   p.weight = weight;
@@ -188,14 +222,40 @@ extern "C" int pkv_add_rms_norm(int32_t dtype, const void* x, int64_t x_stride, 
   p.hidden = hidden;
   p.eps = eps;
   // 16-byte packs when every row start is 16-byte aligned, else one element per pack.
-  const int64_t strides = x_stride | out_stride | p.rin_stride | p.rout_stride;
+  const int64_t strides = x_stride | out_stride | p.rin_stride | p.rout_stride | (splits ? split_stride : 0);
   const bool vec = hidden % 8 == 0 && strides % 8 == 0 && aligned(x, 16) && aligned(weight, 16) && aligned(out, 16) &&
                    (!residual_in || aligned(residual_in, 16)) && (!residual_out || aligned(residual_out, 16));
-  if (!vec && (!aligned(x, 2) || !aligned(weight, 2) || !aligned(out, 2))) return PKV_ERR_INVALID_ARGUMENT;
+  if (!vec && (!aligned(x, splits ? 4 : 2) || !aligned(weight, 2) || !aligned(out, 2))) return PKV_ERR_INVALID_ARGUMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (splits > 0) {
+    if (dtype == PKV_F16)
+      return vec ? launch_norm<__half, 8, true>(p, rows, st) : launch_norm<__half, 1, true>(p, rows, st);
+    return vec ? launch_norm<__nv_bfloat16, 8, true>(p, rows, st) : launch_norm<__nv_bfloat16, 1, true>(p, rows, st);
+  }
   if (dtype == PKV_F16)
-    return vec ? launch_norm<__half, 8>(p, rows, st) : launch_norm<__half, 1>(p, rows, st);
-  return vec ? launch_norm<__nv_bfloat16, 8>(p, rows, st) : launch_norm<__nv_bfloat16, 1>(p, rows, st);
+    return vec ? launch_norm<__half, 8, false>(p, rows, st) : launch_norm<__half, 1, false>(p, rows, st);
+  return vec ? launch_norm<__nv_bfloat16, 8, false>(p, rows, st) : launch_norm<__nv_bfloat16, 1, false>(p, rows, st);
+}
+
+}  // namespace
+}  // namespace pkv
+
+extern "C" int pkv_add_rms_norm(int32_t dtype, const void* x, int64_t x_stride, const void* residual_in,
+                                int64_t residual_in_stride, void* residual_out, int64_t residual_out_stride,
+                                const void* weight, void* out, int64_t out_stride, int64_t rows, int32_t hidden,
+                                float eps, pkv_stream_t stream) {
+  return norm_entry(dtype, x, x_stride, 0, 0, residual_in, residual_in_stride, residual_out, residual_out_stride,
+                    weight, out, out_stride, rows, hidden, eps, stream);
+}
+
+extern "C" int pkv_add_rms_norm_partials(int32_t dtype, const float* partials, int64_t row_stride, int32_t splits,
+                                         int64_t split_stride, const void* residual_in, int64_t residual_in_stride,
+                                         void* residual_out, int64_t residual_out_stride, const void* weight,
+                                         void* out, int64_t out_stride, int64_t rows, int32_t hidden, float eps,
+                                         pkv_stream_t stream) {
+  if (splits <= 0) return PKV_ERR_INVALID_ARGUMENT;
+  return norm_entry(dtype, partials, row_stride, splits, split_stride, residual_in, residual_in_stride, residual_out,
+                    residual_out_stride, weight, out, out_stride, rows, hidden, eps, stream);
 }
 
 extern "C" int pkv_silu_mul(int32_t dtype, const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,

@@ -348,6 +348,8 @@ def add_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: to
     """
     _require_cuda(x, weight, residual, out)
     hidden = x.shape[-1]
+    if x.dtype == torch.float32:  # split-K partials [splits, rows, hidden] of the block's projection
+        return _add_rms_norm_partials(x, weight, eps, residual, out)
     if weight.shape != (hidden,) or weight.dtype != x.dtype or not weight.is_contiguous():
         raise ValueError("weight must be a contiguous [hidden] tensor of x's dtype")
     x2 = _rows2d(x, "x")
@@ -365,6 +367,32 @@ def add_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: to
         pkv_dtype(x.dtype), x2.data_ptr(), x2.stride(0), _ptr(r2), r2.stride(0) if r2 is not None else 0, _ptr(r2),
         r2.stride(0) if r2 is not None else 0, weight.data_ptr(), o2.data_ptr(), o2.stride(0), x2.shape[0], hidden,
         float(eps), _stream()), "add_rms_norm")
+    return out
+
+
+def _add_rms_norm_partials(parts: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None,
+                           out: torch.Tensor | None) -> torch.Tensor:
+    """``add_rms_norm`` of ``x = parts.sum(0)`` rounded to the weight's dtype (float32 ``[S, rows, hidden]``)."""
+    if parts.dim() != 3 or parts.stride(-1) != 1:
+        raise ValueError("partials must be float32 [splits, rows, hidden] with a contiguous last dimension")
+    splits, rows, hidden = parts.shape
+    if weight.shape != (hidden,) or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [hidden] tensor")
+    dt = weight.dtype
+    r2 = None
+    if residual is not None:
+        if residual.shape[-1] != hidden or residual.numel() != rows * hidden or residual.dtype != dt:
+            raise ValueError("residual must hold [rows, hidden] of the weight's dtype")
+        r2 = _rows2d(residual, "residual")
+    if out is None:
+        out = torch.empty(rows, hidden, dtype=dt, device=parts.device)
+    if out.numel() != rows * hidden or out.dtype != dt:
+        raise ValueError("out must hold [rows, hidden] of the weight's dtype")
+    o2 = _rows2d(out, "out")
+    check(lib.pkv_add_rms_norm_partials(
+        pkv_dtype(dt), parts.data_ptr(), parts.stride(1), splits, parts.stride(0), _ptr(r2),
+        r2.stride(0) if r2 is not None else 0, _ptr(r2), r2.stride(0) if r2 is not None else 0, weight.data_ptr(),
+        o2.data_ptr(), o2.stride(0), rows, hidden, float(eps), _stream()), "add_rms_norm_partials")
     return out
 
 

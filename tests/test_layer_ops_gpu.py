@@ -118,3 +118,40 @@ def test_layer_ops_reject_bad_arguments(dev):
         ops.silu_mul(torch.randn(4, 7, device=dev).half())
     with pytest.raises(ValueError):
         ops.add_rms_norm(x.t(), torch.ones(4, device=dev).half(), 1e-6)  # strided last dim
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("splits,rows", [(1, 5), (4, 190), (8, 64)])
+def test_add_rms_norm_of_split_k_partials(dev, dtype, splits, rows):
+    """x given as float32 split-K partials: summed slice by slice in order and rounded to the
+    dtype (where F.linear rounds), then the same residual add and norm, bit for bit."""
+    from mini_inference_b200 import ops
+
+    g = torch.Generator(device=dev).manual_seed(splits * 100 + rows)
+    parts = torch.randn(splits, rows, 896, generator=g, device=dev)
+    w = (1 + 0.1 * torch.randn(896, generator=g, device=dev)).to(dtype)
+    h0 = torch.randn(rows, 896, generator=g, device=dev).to(dtype)
+    acc = parts[0].clone()
+    for s in range(1, splits):
+        acc += parts[s]
+    x = acc.to(dtype)
+    h_want, h_got = h0.clone(), h0.clone()
+    want = ops.add_rms_norm(x, w, 1e-6, residual=h_want)
+    got = ops.add_rms_norm(parts, w, 1e-6, residual=h_got)
+    assert torch.equal(h_got, h_want)
+    assert torch.equal(got, want)
+
+
+def test_split_k_projection_matches_one_gemm(dev):
+    """The model's split-K down_proj (a batched cuBLAS GEMM with float32 partials) against the
+    single GEMM the reference runs: the same float32 dot products in another order."""
+    from mini_inference_b200.model import _linear_split_k, _split_k
+
+    g = torch.Generator(device=dev).manual_seed(5)
+    act = torch.randn(190, 4864, generator=g, device=dev).half()
+    wd = (0.02 * torch.randn(896, 4864, generator=g, device=dev)).half()
+    s = _split_k(190, wd)
+    assert s == 4 and _split_k(64, wd) == 8 and _split_k(4096, wd) == 0
+    parts = _linear_split_k(act, wd, s)
+    ref = act.double() @ wd.double().t()
+    assert (parts.double().sum(0) - ref).abs().max().item() < 1e-3
