@@ -128,3 +128,19 @@ def test_layer_ops_validate_before_any_cuda_call():
     assert L.pkv_silu_mul(_lib.PKV_F16, fake, 4864, fake, 4864, 4, 4864, None) == bad  # gate_up row too short
     assert L.pkv_silu_mul(99, fake, 9728, fake, 4864, 4, 4864, None) == uns
     assert L.pkv_silu_mul(_lib.PKV_BF16, fake, 9728, fake, 4864, 0, 4864, None) == 0
+
+
+def test_norm_partials_validate_before_any_cuda_call():
+    from mini_inference_b200 import _lib
+
+    L, bad, uns = _lib.lib, _lib.PKV_ERR_INVALID_ARGUMENT, _lib.PKV_ERR_UNSUPPORTED
+    fake = 1 << 20  # never dereferenced: every case below is refused (or empty) on the host
+    def call(dtype=_lib.PKV_F16, row_stride=896, splits=4, split_stride=4 * 896, rows=4, hidden=896):
+        return L.pkv_add_rms_norm_partials(dtype, fake, row_stride, splits, split_stride, None, 0, None, 0, fake,
+                                           fake, 896, rows, hidden, 1e-6, None)
+
+    assert call(splits=0) == bad
+    assert call(row_stride=64) == bad
+    assert call(split_stride=896) == bad  # slices would overlap
+    assert call(dtype=99) == uns
+    assert call(rows=0, split_stride=0) == 0
