@@ -29,21 +29,31 @@ class GreedyLMHead:
     same stream.
     """
 
+    KERNEL_ROWS = 256  # rows one pkv_lm_head_argmax call takes; larger batches go in slices
+
     def __init__(self, weight: torch.Tensor, max_batch: int = 256) -> None:
         if weight.dim() != 2 or not weight.is_cuda:
             raise ValueError("weight must be a [vocab, hidden] CUDA tensor")
         self.weight = weight
         self.max_batch = max_batch
-        self.workspace = ops.lm_head_argmax_workspace(max_batch, weight.device)
+        self.workspace = ops.lm_head_argmax_workspace(min(max_batch, self.KERNEL_ROWS), weight.device)
         self.ids = torch.empty(max_batch, dtype=torch.int64, device=weight.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=weight.device)
 
     def __call__(self, hidden: torch.Tensor, max_logits: torch.Tensor | None = None) -> torch.Tensor:
         """Token ids (int64 ``[B]``, on the device) of the hidden rows ``[B, hidden]``."""
-        if hidden.shape[0] > self.max_batch:
-            raise ValueError(f"batch {hidden.shape[0]} exceeds max_batch {self.max_batch}")
-        return ops.lm_head_argmax(hidden, self.weight, self.workspace, out=self.ids, max_logits=max_logits,
-                                  status=self.status, weight_ready=True)
+        n = hidden.shape[0]
+        if n > self.max_batch:
+            raise ValueError(f"batch {n} exceeds max_batch {self.max_batch}")
+        if n <= self.KERNEL_ROWS:
+            return ops.lm_head_argmax(hidden, self.weight, self.workspace, out=self.ids, max_logits=max_logits,
+                                      status=self.status, weight_ready=True)
+        for a in range(0, n, self.KERNEL_ROWS):  # each slice streams the weight once more
+            b = min(n, a + self.KERNEL_ROWS)
+            ops.lm_head_argmax(hidden[a:b], self.weight, self.workspace, out=self.ids[a:b],
+                               max_logits=None if max_logits is None else max_logits[a:b], status=self.status,
+                               weight_ready=True)
+        return self.ids[:n]
 
     def tokens(self, hidden: torch.Tensor, params: Sequence | None = None) -> list[int]:
         """``Sampler(...)(compute_logits(hidden).float(), params)`` for an all-greedy batch."""

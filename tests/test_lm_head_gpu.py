@@ -188,6 +188,18 @@ def test_greedy_lm_head_tokens(dev):
     _check(torch.tensor(toks), None, h, w, torch.float16)
 
 
+def test_greedy_lm_head_slices_batches_above_the_kernel_limit(dev):
+    """A batch of 300 rows (max_num_seqs above 256) goes through the kernel in slices of 256."""
+    from mini_inference_b200.sampler import GreedyLMHead
+    h, w = _case(4099, 256, 300, torch.float16, dev, seed=23)
+    head = GreedyLMHead(w, max_batch=320)
+    top = torch.empty(300, dtype=torch.float32, device=dev)
+    ids = head(h, max_logits=top)
+    torch.cuda.synchronize()
+    _check(ids, top, h, w, torch.float16)
+    assert int(head.workspace.abs().sum()) == 0
+
+
 def test_rejects_unsupported_shapes(dev, ops):
     from mini_inference_b200 import PkvError
     ws = ops.lm_head_argmax_workspace(300, dev)
