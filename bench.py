@@ -203,6 +203,48 @@ def run_long_context(dev, seed: int, reps: int = 10) -> dict:
                          "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": f"{kind} copy bandwidth"}}
 
 
+def long_context_cpu_sample(seed: int, n_seq: int = 2, reps: int = 3) -> dict:
+    """Config 5's layer call on the host cores: the reference's PyTorch ops (``oracle/paged_kv_torch.py``)
+    at the 7B dims, bf16, on the first ``n_seq`` sequences of the same seeded contexts (a full
+    64-sequence call at these contexts would hold ~2.7 GB of gathered K/V per layer). GB/s of
+    the sample's algorithmic bytes; the full call's time at that rate is stated beside it."""
+    from oracle.paged_kv_torch import decode_attend_torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    hq, hkv, d, batch = 28, 4, 128, 64
+    g = torch.Generator().manual_seed(seed + 5)
+    ctx_all = torch.randint(8192, 32769, (batch,), generator=g).tolist()
+    ctx = ctx_all[:n_seq]
+    nblk = [(c + 1 + BS - 1) // BS for c in ctx]
+    tables, at = [], 0
+    for n in nblk:
+        tables.append(list(range(at, at + n)))
+        at += n
+    gc = torch.Generator().manual_seed(seed + 17)
+    k = torch.randn(at + 1, hkv, BS, d, generator=gc).bfloat16()
+    v = torch.randn(at + 1, hkv, BS, d, generator=gc).bfloat16()
+    q = torch.randn(n_seq, hq, d, generator=gc).bfloat16()
+    kn = torch.randn(n_seq, hkv, d, generator=gc).bfloat16()
+    decode_attend_torch(k, v, tables, ctx, q, kn, kn)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        decode_attend_torch(k, v, tables, ctx, q, kn, kn)
+    dt = (time.perf_counter() - t0) / reps
+    elt = 2
+
+    def nbytes(cs: list[int]) -> int:
+        return (sum(c + 1 for c in cs) * hkv * d * elt * 2 + len(cs) * (hq + hkv) * d * elt * 2
+                + sum((c + 1 + BS - 1) // BS for c in cs) * 4)
+
+    gbs = nbytes(ctx) / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"one config-5 layer call over the first {n_seq} of the 64 sequences ({sum(ctx)} cached "
+                      f"tokens, bf16, Hq 28 / Hkv 4 / d 128), reference PyTorch ops on the host "
+                      f"(oracle/paged_kv_torch.py), {reps} calls; {dt:.3f} s per call, so ~"
+                      f"{nbytes(ctx_all) / (gbs * 1e9):.1f} s for the full 64-sequence call at this rate",
+            "seconds": round(dt * reps, 2)}
+
+
 def run_long_step(dev, seed: int, steps: int = 32, warmup: int = 3) -> dict:
     """Config 5's decode step through the whole Qwen2.5-7B-shaped model (bf16, random N(0, 0.02)
     weights drawn on the GPU): 64 sequences with contexts U{8192..32768}, every layer's
@@ -825,6 +867,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     else:
         line["prefill"] = run_prefill(dev, seed=rank)
         line["long_context"] = run_long_context(dev, seed=rank)
+        if world == 1:
+            line["long_context"]["cpu_baseline"] = long_context_cpu_sample(seed=rank)
         if not args.no_long_step:
             line["long_context_step"] = run_long_step(dev, seed=rank)
         line["qkv_post"] = run_qkv_post(dev, seed=rank)
