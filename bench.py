@@ -1210,7 +1210,43 @@ def run_prefix_serving(args, rank: int, world: int, local: int, model=None) -> d
             "prefix_hit_tokens_every_run_equal": len(set(hits)) == 1, "prompt_tokens": prompt_tokens,
             "hit_rate": round(hits[0] / prompt_tokens, 4), "requests_without_hit": misses,
             "ttft_p50_s": round(float(np.percentile(ttft, 50)), 4),
-            "ttft_p95_s": round(float(np.percentile(ttft, 95)), 4)}
+            "ttft_p95_s": round(float(np.percentile(ttft, 95)), 4),
+            **({"cpu_baseline": prefix_cpu_sample(budget_s=args.serving_cpu_budget)} if world == 1 else {})}
+
+
+def prefix_cpu_sample(budget_s: float = 20.0, max_tokens: int = 8) -> dict:
+    """Config 4 on the host cores: the reference's engine loop and PyTorch ops in float32
+    (``oracle/engine_torch.py``) with prefix caching, on its first requests with outputs capped.
+
+    The first step admits requests up to the 4096-token budget and misses (the prefix is
+    registered after its prefill); later admissions hit the 64 prefix blocks, as on the GPU.
+    The number of requests is set from a timed probe so the sample fits ``budget_s``.
+    """
+    from mini_inference_b200.model import Qwen2Config, init_random
+    from oracle.engine_torch import TorchPagedCache, TorchQwen2, serve
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = Qwen2Config.qwen2_0_5b()
+    w = init_random(cfg, seed=0, std=0.02, dtype=torch.float32, device="cpu")
+    model = TorchQwen2(w, cfg.num_layers, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim, cfg.rms_norm_eps,
+                       cfg.rope_theta, cfg.max_position_embeddings)
+    reqs = [(p, min(m, max_tokens)) for p, m in prefix_workload(vocab=cfg.vocab_size)]
+
+    def run(rs):
+        cache = TorchPagedCache(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, len(rs) * (SERVE_MAX_LEN // BS), BS,
+                                len(rs), SERVE_MAX_LEN, torch.float32, enable_prefix_caching=True)
+        t0 = time.perf_counter()
+        seqs = serve(model, cache, rs, len(rs), SERVE_BUDGET, SERVE_MAX_LEN)
+        return time.perf_counter() - t0, sum(len(s.output_token_ids) for s in seqs), cache.prefix_hit_tokens
+
+    probe_s, _, _ = run(reqs[:1])  # one prefix-length prefill and its decodes
+    n = max(1, min(16, int(budget_s / max(probe_s, 1e-3))))
+    dt, tokens, hits = run(reqs[:n])
+    return {"value": round(tokens / dt, 2), "unit": "output tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"config 4's first {n} requests with outputs capped at {max_tokens} tokens, prefix caching on, "
+                      f"the reference's engine loop and PyTorch ops in float32 on the host (oracle/engine_torch.py); "
+                      f"{tokens} tokens in {dt:.2f} s, {hits} prefix-hit tokens",
+            "seconds": round(dt, 2)}
 
 
 def profile_serving_step(warm_steps: int = 40, steps: int = 5) -> None:
