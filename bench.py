@@ -203,7 +203,7 @@ def run_long_context(dev, seed: int, reps: int = 10) -> dict:
                          "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": f"{kind} copy bandwidth"}}
 
 
-def long_context_cpu_sample(seed: int, n_seq: int = 2, reps: int = 3) -> dict:
+def long_context_cpu_sample(seed: int, n_seq: int = 8, reps: int = 5) -> dict:
     """Config 5's layer call on the host cores: the reference's PyTorch ops (``oracle/paged_kv_torch.py``)
     at the 7B dims, bf16, on the first ``n_seq`` sequences of the same seeded contexts (a full
     64-sequence call at these contexts would hold ~2.7 GB of gathered K/V per layer). GB/s of
