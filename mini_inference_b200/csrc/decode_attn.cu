@@ -176,8 +176,9 @@ struct SegIter {
       const int f = first / q;
       s.parts = (last - 1) / q - f + 1;
       s.part = g - f;
-      // A CTA keeps its first segment's state in slot 2g and its last one's in 2g + 1.
-      s.slot = 2 * g + (first < k0 || (first == k0 && s.i1 == last - first) ? 0 : 1);
+      // A CTA keeps its first segment's state (a sequence that starts at or before k0) in
+      // slot 2g and its last one's in 2g + 1; slot_of() reads them back by the same rule.
+      s.slot = 2 * g + (first <= k0 ? 0 : 1);
       return true;
     }
     const int u = cur + C;
@@ -736,11 +737,14 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
 
 template <typename T, int D, int NH, int RK>
 int launch_split(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
-  // The batch holds at most batch * table_cols blocks: below the equal-range threshold
-  // for every CTA count this GPU launches, the chunk rule alone is compiled in.
-  const int64_t bound = (int64_t)p.batch * p.table_cols;
+  // The batch attends to at most batch * table_cols blocks, and (unless sequences share
+  // blocks) to no more than the pool holds: below the equal-range threshold for the CTAs
+  // this shape launches, the chunk rule alone is compiled in. The bound only picks the
+  // faster instance; the chunk rule is correct for any lengths.
+  using S = DecodeShape<D, NH, RK>;
+  const int64_t bound = std::min<int64_t>((int64_t)p.batch * p.table_cols, pool.num_blocks_total);
   const int flat_min = knobs().flat_min > 0 ? knobs().flat_min : kFlatMin;
-  const bool may_flat = knobs().cap <= 0 && bound >= (int64_t)flat_min * num_sms();
+  const bool may_flat = knobs().cap <= 0 && bound >= (int64_t)flat_min * num_sms() * S::MIN_BLOCKS;
   return may_flat ? launch_decode<T, D, NH, RK, true>(pool, p, ws, wsb, st)
                   : launch_decode<T, D, NH, RK, false>(pool, p, ws, wsb, st);
 }

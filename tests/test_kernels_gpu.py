@@ -627,3 +627,56 @@ def test_decode_many_short_sequences_beside_long_ones_twice(dev):
     assert int(ws[:4096].view(torch.int32).abs().sum()) == 0
     ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
     assert excess(to_np(out), round_to(ref, "float16"), "float16") <= 0
+
+
+# Equal-range layouts at the 7B shape. "ragged": eight 36-41 K-token sequences. "on_bounds":
+# 19240 blocks = 148 ranges of 130, sequences 1 and 2 starting exactly on range starts
+# (blocks 1300 and 3900) and last blocks partly filled.
+_ON_BOUNDS = [1300, 2600, 2500, 2400, 2600, 2500, 2700, 2640]
+EQUAL_RANGE_LAYOUTS = {
+    "ragged": [40000, 38000, 39000, 41000, 37000, 40000, 36000, 39500],
+    "on_bounds": [16 * n - 1 - (3 * i) % 16 for i, n in enumerate(_ON_BOUNDS)],
+}
+
+
+@pytest.mark.parametrize("layout", sorted(EQUAL_RANGE_LAYOUTS))
+def test_decode_equal_ranges_at_the_7b_shape(dev, layout):
+    """Enough blocks (at least 128 per CTA) for the equal-range split at the 7B shape (bf16,
+    Hq 28 / Hkv 4 / d 128): every CTA a range that cuts sequences anywhere, sequences that
+    start on a range's first block among them (block 0 always does); twice on one workspace
+    (the counters come back to zero), against the oracle."""
+    from mini_inference_b200 import ops
+
+    bs, hq, hkv, d = 16, 28, 4, 128
+    ctx = EQUAL_RANGE_LAYOUTS[layout]
+    g = torch.Generator().manual_seed(29)
+    nb = sum((c + 1 + bs - 1) // bs for c in ctx) + 1
+    assert nb >= 128 * torch.cuda.get_device_properties(dev).multi_processor_count  # the rule's threshold
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, at = [], 0
+    for c in ctx:
+        n = (c + 1 + bs - 1) // bs
+        tables.append(perm[at: at + n])
+        at += n
+    shape = (1, nb + 1, hkv, bs, d)
+    k_pool = torch.randn(shape, generator=g).bfloat16().to(dev)
+    v_pool = torch.randn(shape, generator=g).bfloat16().to(dev)
+    q = torch.randn(len(ctx), hq, d, generator=g).bfloat16().to(dev)
+    kn = torch.randn(len(ctx), hkv, d, generator=g).bfloat16().to(dev)
+    vn = torch.randn(len(ctx), hkv, d, generator=g).bfloat16().to(dev)
+    meta = decode_metadata(tables, ctx, bs, max(len(t) for t in tables), pad_block=0)
+    tab = torch.from_numpy(meta["block_tables"].astype(np.int32)).to(dev)
+    ws = torch.zeros(ops.decode_workspace_bytes(len(ctx), hkv, tab.shape[1], bs, d, hq), dtype=torch.uint8,
+                     device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    kp, vp = to_np(k_pool[0]), to_np(v_pool[0])
+    args = (ops.make_pool(k_pool, v_pool), 0, ops.make_tables(tab), q,
+            torch.from_numpy(meta["context_lens"].astype(np.int32)).to(dev), ws)
+    kw = dict(k_new=kn, v_new=vn, slot_mapping=torch.from_numpy(meta["slot_mapping"]).to(dev), status=status)
+    out = ops.decode_attention(*args, **kw)
+    out2 = ops.decode_attention(*args, **kw)
+    ops.raise_device_errors(status)
+    assert torch.equal(out, out2)
+    assert int(ws[:4096].view(torch.int32).abs().sum()) == 0
+    ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
+    assert excess(to_np(out), round_to(ref, "bfloat16"), "bfloat16") <= 0
