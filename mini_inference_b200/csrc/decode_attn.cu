@@ -671,17 +671,19 @@ int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (in
 
 // Tuning knobs, read once from the environment (0 / unset = built-in choice):
 //   PKV_DECODE_CTAS_PER_SM  CTAs per SM (at most what the shared memory allows)
+//   PKV_DECODE_CTAS         CTAs in all (at most CTAs per SM x SMs)
 //   PKV_DECODE_PDL          0 = launch without programmatic stream serialization
 //   PKV_DECODE_CAP          chunks of at most this many blocks (no equal ranges)
 //   PKV_DECODE_FLAT_MIN     blocks per CTA from which the ranges are equal
 struct DecodeKnobs {
-  int ctas_per_sm = 0, pdl = 1, cap = 0, flat_min = 0;
+  int ctas_per_sm = 0, ctas = 0, pdl = 1, cap = 0, flat_min = 0;
   DecodeKnobs() {
     auto env = [](const char* k, int dflt) {
       const char* v = getenv(k);
       return v && *v ? atoi(v) : dflt;
     };
     ctas_per_sm = env("PKV_DECODE_CTAS_PER_SM", 0);
+    ctas = env("PKV_DECODE_CTAS", 0);
     pdl = env("PKV_DECODE_PDL", 1);
     cap = env("PKV_DECODE_CAP", 0);
     flat_min = env("PKV_DECODE_FLAT_MIN", 0);
@@ -707,7 +709,8 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
     per_sm = std::max(1, occ);
   }
   const int want = knobs().ctas_per_sm > 0 ? std::min(knobs().ctas_per_sm, per_sm) : per_sm;
-  const int ctas = std::min(num_sms() * want, kMaxCtas);
+  int ctas = std::min(num_sms() * want, kMaxCtas);
+  if (knobs().ctas > 0) ctas = std::min(ctas, knobs().ctas);
   if (!workspace || workspace_bytes < ws_bytes(ctas, NH, RK, D)) return PKV_ERR_WORKSPACE;
   // With chunks a CTA holds at most ceil((batch + 2 * ctas) / ctas) units (whole sequences
   // plus the cut units' slots), so every cut unit's ticket fits its list (148+ SMs: always).
