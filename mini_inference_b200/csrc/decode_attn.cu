@@ -53,6 +53,7 @@ constexpr int kBS = 16;  // tokens per block handled by this kernel
 constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
 constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared memory
+constexpr int kSmallBatch = 256;   // batches up to this size take tables a quarter as large
 constexpr int kMinCap = 16;        // chunks: sequences of up to 16 blocks are never cut
 constexpr int kFlatMin = 128;      // blocks per CTA from which the ranges are equal
 constexpr int kMinQuota = 4;       // equal ranges: never fewer blocks per CTA than this
@@ -62,22 +63,40 @@ constexpr int kMaxPending = 32;    // cut segments of one CTA whose tickets are 
 constexpr int kTicketBatch = 8;    // tickets thread 0 keeps in flight at once
 constexpr float kLog2e = 1.4426950408889634f;
 
-// D: head_dim, NH: KV heads (all in one tile), RK: rows kept per head (8 or 16 >= group).
-template <int D, int NH, int RK> struct DecodeShape {
+// Stages per consumer warp for `fixed` bytes of shared memory besides the ring: two CTAs
+// per SM when each warp keeps 2+ stages in half the shared memory and the fragments of 8
+// rows fit half the registers, else one CTA with up to 4 stages per warp.
+constexpr bool ring_two(int fixed, int stage, int wph, int rk) {
+  return (113 * 1024 - fixed) / (2 * stage * wph) >= 2 && rk <= 8;
+}
+constexpr int ring_pw(int fixed, int stage, int wph, int rk) {
+  return ring_two(fixed, stage, wph, rk) ? std::min((113 * 1024 - fixed) / (2 * stage * wph), 3)
+                                         : std::min((226 * 1024 - fixed) / (2 * stage * wph), 4);
+}
+
+// D: head_dim, NH: KV heads (all in one tile), RK: rows kept per head (8 or 16 >= group),
+// MAXB: sequences the shared-memory tables hold.
+template <int D, int NH, int RK, int MAXB> struct DecodeShape {
   static constexpr int TILE = kBS * D * 2;             // one head's K (or V) of one block
   static constexpr int STAGE = NH * TILE;              // K (or V) of all heads of one block
   static constexpr int WPH = kNC / NH;                 // consumer warps per KV head
   static constexpr int DP = D + 4;                     // padded combine row (no bank conflicts)
   static constexpr int WARP_STATE = 2 * RK + RK * DP;  // floats: m[RK], l[RK], O[RK][DP]
-  static constexpr int COMB = kNC * WARP_STATE * 4;
-  static constexpr int TABLES = 4 * (kMaxBatch + 1) * 4;  // lengths, table rows, two prefix sums
+  static constexpr int TABLES = 4 * (MAXB + 1) * 4;  // lengths, table rows, two prefix sums
+  // A head's warps merge their states at the end of a segment either all at once (every
+  // warp's state in shared memory, all warps combining) or pairwise (half of them hand
+  // their state to the other half, down to one: WPH / 2 states per head). Pairwise takes
+  // more barriers and is used only where its smaller buffer deepens a two-per-SM ring.
+  static constexpr int COMB_ALL = kNC * WARP_STATE * 4;
+  static constexpr int COMB_PAIR = NH * (WPH / 2) * WARP_STATE * 4;
+  static constexpr bool PAIR =
+      ring_two(1024 + COMB_PAIR + TABLES + 256, STAGE, WPH, RK) &&
+      ring_two(1024 + COMB_ALL + TABLES + 256, STAGE, WPH, RK) &&
+      ring_pw(1024 + COMB_PAIR + TABLES + 256, STAGE, WPH, RK) > ring_pw(1024 + COMB_ALL + TABLES + 256, STAGE, WPH, RK);
+  static constexpr int COMB = PAIR ? COMB_PAIR : COMB_ALL;
   static constexpr int FIXED = 1024 + COMB + TABLES + 256;
-  // Two CTAs per SM when each consumer warp keeps 2+ stages in half the shared memory,
-  // else one CTA with up to 4 stages per warp.
-  static constexpr int PW_HALF = (113 * 1024 - FIXED) / (2 * STAGE * WPH);
-  static constexpr int PW_FULL = (226 * 1024 - FIXED) / (2 * STAGE * WPH);
-  static constexpr bool TWO = PW_HALF >= 2;
-  static constexpr int PW = TWO ? (PW_HALF > 3 ? 3 : PW_HALF) : (PW_FULL > 4 ? 4 : PW_FULL);
+  static constexpr bool TWO = ring_two(FIXED, STAGE, WPH, RK);
+  static constexpr int PW = ring_pw(FIXED, STAGE, WPH, RK);
   static constexpr int S = WPH * PW;
   static constexpr int RING = 2 * S * STAGE;
   static constexpr int SMEM = 1024 + RING + COMB + TABLES + 2 * S * 8;
@@ -250,11 +269,11 @@ __device__ inline void rope_q(uint32_t (&qa)[D / 16][4], const T* crow, const T*
   }
 }
 
-template <typename T, int D, int NH, int RK, bool FLAT_OK>
-__global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
+template <typename T, int D, int NH, int RK, int MAXB, bool FLAT_OK>
+__global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BLOCKS)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                   const DecodeParams p) {
-  using S = DecodeShape<D, NH, RK>;
+  using S = DecodeShape<D, NH, RK, MAXB>;
   constexpr int TILE = S::TILE, STAGE = S::STAGE, NS = S::S, WPH = S::WPH, DP = S::DP, WS = S::WARP_STATE;
   constexpr int LANES = kIssueLanes < NS ? kIssueLanes : NS;  // the copies of one issue use distinct stages
   constexpr int ROW = D + 4;            // partial row: m, l, 2 pad floats, O[D] (O 16-byte aligned)
@@ -267,9 +286,9 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::RING + S::COMB);
   uint64_t* empty = full + NS;
   int* sCtx = reinterpret_cast<int*>(empty + NS);  // [batch] clamped context lengths
-  int* sRow = sCtx + kMaxBatch + 1;                // [batch] block-table row of each sequence
-  int* sA = sRow + kMaxBatch + 1;                  // [batch + 1] blocks (ranges) or units (chunks) before b
-  int* sB = sA + kMaxBatch + 1;                    // [batch + 1] cut units before b (chunks)
+  int* sRow = sCtx + MAXB + 1;                     // [batch] block-table row of each sequence
+  int* sA = sRow + MAXB + 1;                       // [batch + 1] blocks (ranges) or units (chunks) before b
+  int* sB = sA + MAXB + 1;                         // [batch + 1] cut units before b (chunks)
   __shared__ int s_bad, s_npend, s_flat, s_q, s_total;
   __shared__ int2 s_pend[kMaxPending];  // (sequence, parts) of cut segments
   __shared__ int s_last[kMaxPending];
@@ -456,8 +475,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
       }
     }
     const int h = warp / WPH, w = warp % WPH;  // this warp's KV head and its rank among the head's warps
-    float* head_comb = comb + h * WPH * WS;
-    float* cw_state = head_comb + w * WS;
+    float* head_comb = comb + h * (S::PAIR ? WPH / 2 : WPH) * WS;  // this head's merge states
     bool ok = true;
     int j = 0;  // blocks of this CTA consumed so far (by all warps)
     Seg sg;
@@ -539,57 +557,133 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK>::MIN_BLOCKS)
         if (lane == 0) mbar_arrive(&empty[st]);
       }
       finish_row_sums(l_r);
-      // Merge the head's warps through shared memory.
-      float* cm = cw_state;
-      float* cl = cm + RK;
-      float* co = cl + RK;
-      if (t4 == 0) {
-        cm[g_lane] = m_r[0];
-        cl[g_lane] = l_r[0];
-        if (RK > 8) {
-          cm[g_lane + 8] = m_r[1];
-          cl[g_lane + 8] = l_r[1];
-        }
-      }
-#pragma unroll
-      for (int jj = 0; jj < D / 8; ++jj) {
-        const int col = 8 * jj + 2 * t4;
-        *reinterpret_cast<float2*>(&co[g_lane * DP + col]) = make_float2(o[jj][0], o[jj][1]);
-        if (RK > 8) *reinterpret_cast<float2*>(&co[(g_lane + 8) * DP + col]) = make_float2(o[jj][2], o[jj][3]);
-      }
-      named_bar(1 + h, WPH * 32);
       const bool whole = sg.parts == 1;
       float* part = p.partials + (int64_t)sg.slot * SLOT + h * RK * ROW;
       T* outp = reinterpret_cast<T*>(p.out) + b * p.out_sb + (int64_t)h * G * p.out_sh;
-      for (int it = w * 32 + lane; it < G * (D / 2); it += WPH * 32) {
-        const int r = it / (D / 2), col = 2 * (it % (D / 2));
-        float mm = -INFINITY;
+      if constexpr (S::PAIR) {
+        // Merge the head's warps pairwise: in each round the upper half of the remaining
+        // warps hands its state (m, l and O of rows g_lane, g_lane + 8 in the MMA fragment
+        // layout) through a slot to the lower half, which folds it into its registers. Warp 0
+        // of the head ends with the segment's state.
 #pragma unroll
-        for (int ww = 0; ww < WPH; ++ww) mm = fmaxf(mm, head_comb[ww * WS + r]);
-        float ll = 0.f, o0 = 0.f, o1 = 0.f;
+        for (int half = WPH / 2; half >= 1; half >>= 1) {
+          if (w >= half && w < 2 * half) {
+            float* c = head_comb + (w - half) * WS;
+            if (t4 == 0) {
+              c[g_lane] = m_r[0];
+              c[RK + g_lane] = l_r[0];
+              if (RK > 8) {
+                c[g_lane + 8] = m_r[1];
+                c[RK + g_lane + 8] = l_r[1];
+              }
+            }
 #pragma unroll
-        for (int ww = 0; ww < WPH; ++ww) {
-          const float* c = head_comb + ww * WS;
-          const float f = ex2(c[r] - mm);  // a warp without tiles has m = -inf: f = 0
-          ll += c[RK + r] * f;
-          const float2 v = *reinterpret_cast<const float2*>(&c[2 * RK + r * DP + col]);
-          o0 += v.x * f;
-          o1 += v.y * f;
+            for (int jj = 0; jj < D / 8; ++jj) {
+              const int col = 8 * jj + 2 * t4;
+              *reinterpret_cast<float2*>(&c[2 * RK + g_lane * DP + col]) = make_float2(o[jj][0], o[jj][1]);
+              if (RK > 8) *reinterpret_cast<float2*>(&c[2 * RK + (g_lane + 8) * DP + col]) = make_float2(o[jj][2], o[jj][3]);
+            }
+          }
+          named_bar(1 + h, WPH * 32);
+          if (w < half) {
+            const float* c = head_comb + w * WS;
+            float fa[2], fb[2];
+#pragma unroll
+            for (int i = 0; i < (RK > 8 ? 2 : 1); ++i) {
+              const float mb = c[g_lane + 8 * i], lb = c[RK + g_lane + 8 * i];
+              const float mn = fmaxf(m_r[i], mb);
+              const float mref = mn == -INFINITY ? 0.f : mn;  // both empty: weights 0, not NaN
+              fa[i] = ex2(m_r[i] - mref);
+              fb[i] = ex2(mb - mref);
+              m_r[i] = mn;
+              l_r[i] = l_r[i] * fa[i] + lb * fb[i];
+            }
+#pragma unroll
+            for (int jj = 0; jj < D / 8; ++jj) {
+              const int col = 8 * jj + 2 * t4;
+              const float2 v = *reinterpret_cast<const float2*>(&c[2 * RK + g_lane * DP + col]);
+              o[jj][0] = o[jj][0] * fa[0] + v.x * fb[0];
+              o[jj][1] = o[jj][1] * fa[0] + v.y * fb[0];
+              if (RK > 8) {
+                const float2 u = *reinterpret_cast<const float2*>(&c[2 * RK + (g_lane + 8) * DP + col]);
+                o[jj][2] = o[jj][2] * fa[1] + u.x * fb[1];
+                o[jj][3] = o[jj][3] * fa[1] + u.y * fb[1];
+              }
+            }
+          }
+          named_bar(1 + h, WPH * 32);  // the slots are written again by the next round or segment
         }
-        if (whole) {
-          const float inv = 1.f / ll;
-          *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + col) = Dt<T>::pack(o0 * inv, o1 * inv);
-        } else {
-          __stcg(reinterpret_cast<float2*>(part + r * ROW + 4 + col), make_float2(o0, o1));
-          if (col == 0) __stcg(reinterpret_cast<float2*>(part + r * ROW), make_float2(mm, ll));
+        if (w == 0) {
+#pragma unroll
+          for (int i = 0; i < (RK > 8 ? 2 : 1); ++i) {
+            const int r = g_lane + 8 * i;
+            if (r >= G) continue;
+            if (whole) {
+              const float inv = 1.f / l_r[i];
+#pragma unroll
+              for (int jj = 0; jj < D / 8; ++jj)
+                *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + 8 * jj + 2 * t4) =
+                    Dt<T>::pack(o[jj][2 * i] * inv, o[jj][2 * i + 1] * inv);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < D / 8; ++jj)
+                __stcg(reinterpret_cast<float2*>(part + r * ROW + 4 + 8 * jj + 2 * t4),
+                       make_float2(o[jj][2 * i], o[jj][2 * i + 1]));
+              if (t4 == 0) __stcg(reinterpret_cast<float2*>(part + r * ROW), make_float2(m_r[i], l_r[i]));
+            }
+          }
         }
+      } else {
+        // Every warp of the head puts its state in shared memory; all of them then combine
+        // the states column by column.
+        float* cm = head_comb + w * WS;
+        float* cl = cm + RK;
+        float* co = cl + RK;
+        if (t4 == 0) {
+          cm[g_lane] = m_r[0];
+          cl[g_lane] = l_r[0];
+          if (RK > 8) {
+            cm[g_lane + 8] = m_r[1];
+            cl[g_lane + 8] = l_r[1];
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < D / 8; ++jj) {
+          const int col = 8 * jj + 2 * t4;
+          *reinterpret_cast<float2*>(&co[g_lane * DP + col]) = make_float2(o[jj][0], o[jj][1]);
+          if (RK > 8) *reinterpret_cast<float2*>(&co[(g_lane + 8) * DP + col]) = make_float2(o[jj][2], o[jj][3]);
+        }
+        named_bar(1 + h, WPH * 32);
+        for (int it = w * 32 + lane; it < G * (D / 2); it += WPH * 32) {
+          const int r = it / (D / 2), col = 2 * (it % (D / 2));
+          float mm = -INFINITY;
+#pragma unroll
+          for (int ww = 0; ww < WPH; ++ww) mm = fmaxf(mm, head_comb[ww * WS + r]);
+          float ll = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+          for (int ww = 0; ww < WPH; ++ww) {
+            const float* c = head_comb + ww * WS;
+            const float f = ex2(c[r] - mm);  // a warp without tiles has m = -inf: f = 0
+            ll += c[RK + r] * f;
+            const float2 v = *reinterpret_cast<const float2*>(&c[2 * RK + r * DP + col]);
+            o0 += v.x * f;
+            o1 += v.y * f;
+          }
+          if (whole) {
+            const float inv = 1.f / ll;
+            *reinterpret_cast<uint32_t*>(outp + r * p.out_sh + col) = Dt<T>::pack(o0 * inv, o1 * inv);
+          } else {
+            __stcg(reinterpret_cast<float2*>(part + r * ROW + 4 + col), make_float2(o0, o1));
+            if (col == 0) __stcg(reinterpret_cast<float2*>(part + r * ROW), make_float2(mm, ll));
+          }
+        }
+        named_bar(1 + h, WPH * 32);  // the states are written again by the next segment
       }
       if (!whole && warp == 0 && lane == 0) {
         // The launcher refuses launches where a CTA could hold more cut segments than this.
         if (s_npend < kMaxPending) s_pend[s_npend++] = make_int2(b, sg.parts);
         else report(p.status, PKV_ERR_WORKSPACE);
       }
-      named_bar(1 + h, WPH * 32);  // the combine buffer is reused by the next segment
       j += n_i;
     }
     if (!ok) s_bad = 1;
@@ -675,8 +769,9 @@ int64_t ws_bytes(int ctas, int nh, int rk, int d) { return kPartialsOffset + (in
 //   PKV_DECODE_PDL          0 = launch without programmatic stream serialization
 //   PKV_DECODE_CAP          chunks of at most this many blocks (no equal ranges)
 //   PKV_DECODE_FLAT_MIN     blocks per CTA from which the ranges are equal
+//   PKV_DECODE_SMALL_TABLES 0 = every batch takes the instance with tables for kMaxBatch
 struct DecodeKnobs {
-  int ctas_per_sm = 0, ctas = 0, pdl = 1, cap = 0, flat_min = 0;
+  int ctas_per_sm = 0, ctas = 0, pdl = 1, cap = 0, flat_min = 0, small_tables = 1;
   DecodeKnobs() {
     auto env = [](const char* k, int dflt) {
       const char* v = getenv(k);
@@ -687,6 +782,7 @@ struct DecodeKnobs {
     pdl = env("PKV_DECODE_PDL", 1);
     cap = env("PKV_DECODE_CAP", 0);
     flat_min = env("PKV_DECODE_FLAT_MIN", 0);
+    small_tables = env("PKV_DECODE_SMALL_TABLES", 1);
   }
 };
 const DecodeKnobs& knobs() {
@@ -694,17 +790,18 @@ const DecodeKnobs& knobs() {
   return k;
 }
 
-template <typename T, int D, int NH, int RK, bool FLAT_OK>
+template <typename T, int D, int NH, int RK, int MAXB, bool FLAT_OK>
 int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace, int64_t workspace_bytes,
                   cudaStream_t stream) {
-  using S = DecodeShape<D, NH, RK>;
+  using S = DecodeShape<D, NH, RK, MAXB>;
+  if (p0.batch > MAXB) return PKV_ERR_UNSUPPORTED;
   static int per_sm = 0;
   if (per_sm == 0) {
     cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<T, D, NH, RK, FLAT_OK>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        cudaFuncSetAttribute(decode_kernel<T, D, NH, RK, MAXB, FLAT_OK>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK, FLAT_OK>, kThreads, S::SMEM);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK, MAXB, FLAT_OK>, kThreads, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     per_sm = std::max(1, occ);
   }
@@ -735,27 +832,35 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = knobs().pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, FLAT_OK>, tk, tv, p));
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, MAXB, FLAT_OK>, tk, tv, p));
 }
 
-template <typename T, int D, int NH, int RK>
+template <typename T, int D, int NH, int RK, int MAXB>
 int launch_split(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
   // The batch attends to at most batch * table_cols blocks, and (unless sequences share
   // blocks) to no more than the pool holds: below the equal-range threshold for the CTAs
   // this shape launches, the chunk rule alone is compiled in. The bound only picks the
   // faster instance; the chunk rule is correct for any lengths.
-  using S = DecodeShape<D, NH, RK>;
+  using S = DecodeShape<D, NH, RK, MAXB>;
   const int64_t bound = std::min<int64_t>((int64_t)p.batch * p.table_cols, pool.num_blocks_total);
   const int flat_min = knobs().flat_min > 0 ? knobs().flat_min : kFlatMin;
   const bool may_flat = knobs().cap <= 0 && bound >= (int64_t)flat_min * num_sms() * S::MIN_BLOCKS;
-  return may_flat ? launch_decode<T, D, NH, RK, true>(pool, p, ws, wsb, st)
-                  : launch_decode<T, D, NH, RK, false>(pool, p, ws, wsb, st);
+  return may_flat ? launch_decode<T, D, NH, RK, MAXB, true>(pool, p, ws, wsb, st)
+                  : launch_decode<T, D, NH, RK, MAXB, false>(pool, p, ws, wsb, st);
+}
+
+// Batches of up to kSmallBatch sequences take the instance with small per-sequence tables,
+// whose freed shared memory deepens the ring where the shape allows.
+template <typename T, int D, int NH, int RK>
+int launch_tables(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
+  return p.batch <= kSmallBatch && knobs().small_tables ? launch_split<T, D, NH, RK, kSmallBatch>(pool, p, ws, wsb, st)
+                                : launch_split<T, D, NH, RK, kMaxBatch>(pool, p, ws, wsb, st);
 }
 
 template <typename T, int D, int NH>
 int launch_rows(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t wsb, cudaStream_t st) {
-  return p.group <= 8 ? launch_split<T, D, NH, 8>(pool, p, ws, wsb, st)
-                      : launch_split<T, D, NH, 16>(pool, p, ws, wsb, st);
+  return p.group <= 8 ? launch_tables<T, D, NH, 8>(pool, p, ws, wsb, st)
+                      : launch_tables<T, D, NH, 16>(pool, p, ws, wsb, st);
 }
 
 template <typename T, int D>

@@ -680,3 +680,52 @@ def test_decode_equal_ranges_at_the_7b_shape(dev, layout):
     assert int(ws[:4096].view(torch.int32).abs().sum()) == 0
     ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
     assert excess(to_np(out), round_to(ref, "bfloat16"), "bfloat16") <= 0
+
+
+# Head layouts beyond the configs' 7-query groups: one KV head (8 warps per head, three
+# pairwise merge rounds), eight (one warp per head, no merge), groups of 16 (16 MMA rows)
+# and of 1.
+HEAD_LAYOUTS = [(torch.float16, 16, 1, 64), (torch.bfloat16, 8, 1, 128), (torch.bfloat16, 64, 8, 128),
+                (torch.float16, 8, 8, 64), (torch.float16, 32, 2, 128), (torch.bfloat16, 64, 4, 64)]
+
+
+@pytest.mark.parametrize("dtype,hq,hkv,d", HEAD_LAYOUTS)
+def test_decode_head_layouts(dev, dtype, hq, hkv, d):
+    """Every KV-head count and group size the kernel takes, on short and cut sequences (the
+    warps of a head merge, then the CTAs of a sequence), twice on one workspace, against the
+    oracle."""
+    from mini_inference_b200 import ops
+
+    bs = 16
+    ctx = [1, 15, 16, 17, 40, 100, 333, 700, 1500, 3000]
+    g = torch.Generator().manual_seed(hq * 31 + hkv * 7 + d)
+    nb = sum((c + 1 + bs - 1) // bs for c in ctx) + 2
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, at = [], 0
+    for c in ctx:
+        n = (c + 1 + bs - 1) // bs
+        tables.append(perm[at: at + n])
+        at += n
+    shape = (1, nb + 1, hkv, bs, d)
+    k_pool = torch.randn(shape, generator=g).to(dtype).to(dev)
+    v_pool = torch.randn(shape, generator=g).to(dtype).to(dev)
+    q = torch.randn(len(ctx), hq, d, generator=g).to(dtype).to(dev)
+    kn = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(dev)
+    vn = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(dev)
+    meta = decode_metadata(tables, ctx, bs, max(len(t) for t in tables), pad_block=0)
+    tab = torch.from_numpy(meta["block_tables"].astype(np.int32)).to(dev)
+    ws = torch.zeros(ops.decode_workspace_bytes(len(ctx), hkv, tab.shape[1], bs, d, hq), dtype=torch.uint8,
+                     device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    kp, vp = to_np(k_pool[0]), to_np(v_pool[0])
+    args = (ops.make_pool(k_pool, v_pool), 0, ops.make_tables(tab), q,
+            torch.from_numpy(meta["context_lens"].astype(np.int32)).to(dev), ws)
+    kw = dict(k_new=kn, v_new=vn, slot_mapping=torch.from_numpy(meta["slot_mapping"]).to(dev), status=status)
+    out = ops.decode_attention(*args, **kw)
+    out2 = ops.decode_attention(*args, **kw)
+    ops.raise_device_errors(status)
+    assert torch.equal(out, out2)
+    assert int(ws[:4096].view(torch.int32).abs().sum()) == 0
+    name = "float16" if dtype == torch.float16 else "bfloat16"
+    ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
+    assert excess(to_np(out), round_to(ref, name), name) <= 0
