@@ -840,7 +840,9 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_kind": f"{peak_kind} copy bandwidth",
                      "traffic": traffic, "algorithmic_bytes_per_launch": call_bytes,
-                     "kernel": "pkv decode_kernel<half,64,2,8,false> (fused append + paged attention, split items merged)",
+                     "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture of this "
+                                       "kernel (profiles/decode_attention_config2.md)",
+                     "kernel": "pkv decode_kernel<half,64,2,8,256,false> (fused append + paged attention, split items merged)",
                      "launch_us": round(per_launch_ms * 1e3, 3)},
         "e2e": {"value": round(world * step_bytes * args.e2e_steps / (ms_e2e_job * 1e-3) / 1e9, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
