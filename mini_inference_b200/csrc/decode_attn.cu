@@ -15,9 +15,11 @@
 //    blocks, C CTAs). Every CTA streams the same bytes whatever the mix of lengths; its
 //    range covers the tail of one sequence, whole sequences and the head of another, and
 //    holds at most two cut pieces (its first and its last).
-//  * short ranges: sequences longer than cap = max(kMinCap, ceil(T / max(C - I, C / 4)))
-//    blocks (I: sequences) are cut into ceil(n / cap) balanced chunks so that all units
-//    fit one wave when the batch allows, and CTA g takes units g, g + C, ... Units then
+//  * short ranges: sequences longer than a cap are cut into ceil(n / cap) balanced chunks,
+//    and CTA g takes units g, g + C, ... The cap is max(kMinCap, ceil(T / max(C - I,
+//    C / 4))) (I: sequences), which fits all units in one wave when the batch allows; for
+//    batches of more than C / 2 sequences, the smallest of a fixed list of candidates
+//    (12 .. 64 blocks) whose units fill at most 27 / 32 of the CTAs, where one does. Units then
 //    differ in length, and the CTAs that finish early make room for the next launch's
 //    CTAs, which fill their rings while this launch ends; with equal ranges every CTA
 //    would end at once and nothing of the next launch could start early (measured slower
@@ -54,7 +56,17 @@ constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
 constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared memory
 constexpr int kSmallBatch = 256;   // batches up to this size take tables a quarter as large
-constexpr int kMinCap = 16;        // chunks: sequences of up to 16 blocks are never cut
+constexpr int kMinCap = 16;        // chunks: the fallback rule never cuts sequences of up to 16 blocks
+// Chunk caps (blocks) the split tries, smallest first, for batches of more than C / 2
+// sequences: it takes the smallest whose units fill at most 27/32 of the C CTAs, so that
+// every unit starts in the first wave and the longest units stay short, while a few CTAs
+// are left to the next launch's ring fill. (The fallback rule divides by C - I, which such
+// batches make small, so its cap grows far beyond what fills the CTAs.)
+constexpr int kNumCaps = 16;
+__host__ __device__ constexpr int cap_candidate(int k) {
+  constexpr int caps[kNumCaps] = {12, 13, 14, 15, 16, 18, 20, 22, 24, 26, 28, 32, 36, 40, 48, 64};
+  return caps[k];
+}
 constexpr int kFlatMin = 128;      // blocks per CTA from which the ranges are equal
 constexpr int kMinQuota = 4;       // equal ranges: never fewer blocks per CTA than this
 constexpr int kIssueLanes = 4;     // producer lanes issuing copies together
@@ -269,7 +281,9 @@ __device__ inline void rope_q(uint32_t (&qa)[D / 16][4], const T* crow, const T*
   }
 }
 
-template <typename T, int D, int NH, int RK, int MAXB, bool FLAT_OK>
+// CAPS: the instance for batches of more than C / 2 sequences, which tries the candidate
+// chunk caps; the others keep the fallback rule alone (a prologue as short as it can be).
+template <typename T, int D, int NH, int RK, int MAXB, bool FLAT_OK, bool CAPS>
 __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BLOCKS)
     decode_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                   const DecodeParams p) {
@@ -311,11 +325,14 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BL
 
   // The split's per-sequence sums in three barrier-separated passes over chunks of 32
   // sequences, chunk c held by warp c % 9 (one chunk per warp up to 288 sequences):
-  // (1) load lengths and table rows, chunk sums of blocks and non-empty sequences;
+  // (1) load lengths and table rows, chunk sums of blocks and non-empty sequences, and the
+  //     units each candidate cap would make (lane k of a warp keeps candidate k's count);
   // (2) the rule and the cap from the totals, chunk-local scans of units / blocks;
   // (3) add the chunks' carries. Each warp works on its own chunks in parallel.
   __shared__ int s_ct[32], s_ci[32], s_ca[32], s_cb[32];
+  __shared__ int s_cand[CAPS ? kNC + 1 : 1][kNumCaps];
   const int nchunks = (B + 31) / 32;
+  int cand = 0;
   for (int base = warp * 32; base < B; base += kThreads) {
     const int i = base + lane;
     int n = 0;
@@ -340,6 +357,16 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BL
       s_ct[base / 32] = ct;
       s_ci[base / 32] = ci;
     }
+    if constexpr (CAPS) {
+#pragma unroll
+      for (int k = 0; k < kNumCaps; ++k) {
+        const int u = __reduce_add_sync(0xffffffffu, (n + cap_candidate(k) - 1) / cap_candidate(k));
+        if (lane == k) cand += u;
+      }
+    }
+  }
+  if constexpr (CAPS) {
+    if (lane < kNumCaps) s_cand[warp][lane] = cand;
   }
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -356,7 +383,18 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BL
     const int items = warp_sum(lane < nchunks ? s_ci[lane] : 0);
     const int flat = FLAT_OK && p.cap_override <= 0 && tiles >= p.flat_min * C;
     const int free_ctas = max(C - items, max(C / 4, 1));
-    const int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
+    int cap = p.cap_override > 0 ? p.cap_override : max(kMinCap, (tiles + free_ctas - 1) / free_ctas);
+    if constexpr (CAPS) {
+      int units = 0, my_cap = 0;
+#pragma unroll
+      for (int k = 0; k < kNumCaps; ++k) my_cap = lane == k ? cap_candidate(k) : my_cap;
+      if (lane < kNumCaps) {
+#pragma unroll
+        for (int w = 0; w <= kNC; ++w) units += s_cand[w][lane];
+      }
+      const unsigned fits = __ballot_sync(0xffffffffu, lane < kNumCaps && units <= C * 27 / 32);
+      if (p.cap_override <= 0 && fits) cap = __shfl_sync(0xffffffffu, my_cap, __ffs(fits) - 1);
+    }
     for (int base = warp * 32; base < B; base += kThreads) {
       const int i = base + lane;
       const int n = i < B ? (sCtx[i] + kBS - 1) / kBS : 0;
@@ -397,8 +435,9 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BL
   }
   __syncthreads();
   const int flat = s_flat, q = s_q;
-  // Cut units never exceed 2 * max(C - I, C / 4) <= 2 * C and cut ranges 2 * C, the slots
-  // the host provides (an overriding cap may ask for more).
+  // Cut units never exceed 2 * C (a candidate cap keeps all units within 27 / 32 of the
+  // CTAs, the fallback rule cut units within 2 * max(C - I, C / 4)) and cut ranges 2 * C,
+  // the slots the host provides (an overriding cap may ask for more).
   if (!flat && sB[B] > p.max_slots) {
     if (tid == 0) report(p.status, PKV_ERR_WORKSPACE);
     return;
@@ -790,7 +829,7 @@ const DecodeKnobs& knobs() {
   return k;
 }
 
-template <typename T, int D, int NH, int RK, int MAXB, bool FLAT_OK>
+template <typename T, int D, int NH, int RK, int MAXB, bool FLAT_OK, bool CAPS>
 int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace, int64_t workspace_bytes,
                   cudaStream_t stream) {
   using S = DecodeShape<D, NH, RK, MAXB>;
@@ -798,10 +837,10 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   static int per_sm = 0;
   if (per_sm == 0) {
     cudaError_t e =
-        cudaFuncSetAttribute(decode_kernel<T, D, NH, RK, MAXB, FLAT_OK>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+        cudaFuncSetAttribute(decode_kernel<T, D, NH, RK, MAXB, FLAT_OK, CAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK, MAXB, FLAT_OK>, kThreads, S::SMEM);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<T, D, NH, RK, MAXB, FLAT_OK, CAPS>, kThreads, S::SMEM);
     if (e != cudaSuccess) return cuda_status(e);
     per_sm = std::max(1, occ);
   }
@@ -832,7 +871,7 @@ int launch_decode(const pkv_pool& pool, const DecodeParams& p0, void* workspace,
   attr[0].val.programmaticStreamSerializationAllowed = knobs().pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, MAXB, FLAT_OK>, tk, tv, p));
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_kernel<T, D, NH, RK, MAXB, FLAT_OK, CAPS>, tk, tv, p));
 }
 
 template <typename T, int D, int NH, int RK, int MAXB>
@@ -845,8 +884,14 @@ int launch_split(const pkv_pool& pool, const DecodeParams& p, void* ws, int64_t 
   const int64_t bound = std::min<int64_t>((int64_t)p.batch * p.table_cols, pool.num_blocks_total);
   const int flat_min = knobs().flat_min > 0 ? knobs().flat_min : kFlatMin;
   const bool may_flat = knobs().cap <= 0 && bound >= (int64_t)flat_min * num_sms() * S::MIN_BLOCKS;
-  return may_flat ? launch_decode<T, D, NH, RK, MAXB, true>(pool, p, ws, wsb, st)
-                  : launch_decode<T, D, NH, RK, MAXB, false>(pool, p, ws, wsb, st);
+  if (may_flat) return launch_decode<T, D, NH, RK, MAXB, true, false>(pool, p, ws, wsb, st);
+  // More sequences than half the CTAs this shape launches (two per SM at most): the
+  // instance that tries the candidate chunk caps. Any instance is correct for any batch.
+  if constexpr (MAXB == kSmallBatch) {
+    if (knobs().cap <= 0 && (int64_t)p.batch * 2 > (int64_t)num_sms() * S::MIN_BLOCKS)
+      return launch_decode<T, D, NH, RK, MAXB, false, true>(pool, p, ws, wsb, st);
+  }
+  return launch_decode<T, D, NH, RK, MAXB, false, false>(pool, p, ws, wsb, st);
 }
 
 // Batches of up to kSmallBatch sequences take the instance with small per-sequence tables,

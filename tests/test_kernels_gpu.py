@@ -729,3 +729,47 @@ def test_decode_head_layouts(dev, dtype, hq, hkv, d):
     name = "float16" if dtype == torch.float16 else "bfloat16"
     ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
     assert excess(to_np(out), round_to(ref, name), name) <= 0
+
+
+def test_decode_serving_batch_takes_a_candidate_cap(dev):
+    """190 sequences of log-uniform 56..1064 tokens (config 3's decode batch early on): more
+    sequences than half the CTAs, where the split takes the smallest listed chunk cap whose
+    units fill at most 27/32 of the CTAs. The same rule restated here must pick one (so the
+    test covers that path); two calls on one workspace give the same bits and match the oracle."""
+    from mini_inference_b200 import ops
+
+    bs, hq, hkv, d, batch = 16, 14, 2, 64, 190
+    g = torch.Generator().manual_seed(23)
+    ctx = torch.exp(torch.empty(batch).uniform_(np.log(56.0), np.log(1064.0), generator=g)).long().tolist()
+    nblk = [(c + 1 + bs - 1) // bs for c in ctx]
+    ctas = 2 * torch.cuda.get_device_properties(dev).multi_processor_count
+    caps = [12, 13, 14, 15, 16, 18, 20, 22, 24, 26, 28, 32, 36, 40, 48, 64]
+    fit = [c for c in caps if sum(-(-n // c) for n in nblk) <= ctas * 27 // 32]
+    assert batch > ctas // 2 and fit and any(n > fit[0] for n in nblk)  # a candidate is taken and cuts
+    nb = sum(nblk) + 1
+    perm = torch.randperm(nb, generator=g).tolist()
+    tables, at = [], 0
+    for n in nblk:
+        tables.append(perm[at: at + n])
+        at += n
+    shape = (1, nb + 1, hkv, bs, d)
+    k_pool = torch.randn(shape, generator=g).half().to(dev)
+    v_pool = torch.randn(shape, generator=g).half().to(dev)
+    q = torch.randn(batch, hq, d, generator=g).half().to(dev)
+    kn = torch.randn(batch, hkv, d, generator=g).half().to(dev)
+    vn = torch.randn(batch, hkv, d, generator=g).half().to(dev)
+    meta = decode_metadata(tables, ctx, bs, max(nblk), pad_block=0)
+    tab = torch.from_numpy(meta["block_tables"].astype(np.int32)).to(dev)
+    ws = torch.zeros(ops.decode_workspace_bytes(batch, hkv, tab.shape[1], bs, d, hq), dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    kp, vp = to_np(k_pool[0]), to_np(v_pool[0])
+    args = (ops.make_pool(k_pool, v_pool), 0, ops.make_tables(tab), q,
+            torch.from_numpy(meta["context_lens"].astype(np.int32)).to(dev), ws)
+    kw = dict(k_new=kn, v_new=vn, slot_mapping=torch.from_numpy(meta["slot_mapping"]).to(dev), status=status)
+    out = ops.decode_attention(*args, **kw)
+    out2 = ops.decode_attention(*args, **kw)
+    ops.raise_device_errors(status)
+    assert torch.equal(out, out2)
+    assert int(ws[:4096].view(torch.int32).abs().sum()) == 0
+    ref = decode_attend(kp, vp, tables, ctx, to_np(q), to_np(kn), to_np(vn))
+    assert excess(to_np(out), round_to(ref, "float16"), "float16") <= 0
