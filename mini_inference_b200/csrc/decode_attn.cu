@@ -19,7 +19,7 @@
 //    and CTA g takes units g, g + C, ... The cap is max(kMinCap, ceil(T / max(C - I,
 //    C / 4))) (I: sequences), which fits all units in one wave when the batch allows; for
 //    batches of more than C / 2 sequences, the smallest of a fixed list of candidates
-//    (12 .. 64 blocks) whose units fill at most 27 / 32 of the CTAs, where one does. Units then
+//    (12 .. 64 blocks) whose units fill at most 29 / 32 of the CTAs, where one does. Units then
 //    differ in length, and the CTAs that finish early make room for the next launch's
 //    CTAs, which fill their rings while this launch ends; with equal ranges every CTA
 //    would end at once and nothing of the next launch could start early (measured slower
@@ -58,7 +58,7 @@ constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared mem
 constexpr int kSmallBatch = 256;   // batches up to this size take tables a quarter as large
 constexpr int kMinCap = 16;        // chunks: the fallback rule never cuts sequences of up to 16 blocks
 // Chunk caps (blocks) the split tries, smallest first, for batches of more than C / 2
-// sequences: it takes the smallest whose units fill at most 27/32 of the C CTAs, so that
+// sequences: it takes the smallest whose units fill at most 29/32 of the C CTAs, so that
 // every unit starts in the first wave and the longest units stay short, while a few CTAs
 // are left to the next launch's ring fill. (The fallback rule divides by C - I, which such
 // batches make small, so its cap grows far beyond what fills the CTAs.)
@@ -392,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BL
 #pragma unroll
         for (int w = 0; w <= kNC; ++w) units += s_cand[w][lane];
       }
-      const unsigned fits = __ballot_sync(0xffffffffu, lane < kNumCaps && units <= C * 27 / 32);
+      const unsigned fits = __ballot_sync(0xffffffffu, lane < kNumCaps && units <= C * 29 / 32);
       if (p.cap_override <= 0 && fits) cap = __shfl_sync(0xffffffffu, my_cap, __ffs(fits) - 1);
     }
     for (int base = warp * 32; base < B; base += kThreads) {
@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, DecodeShape<D, NH, RK, MAXB>::MIN_BL
   }
   __syncthreads();
   const int flat = s_flat, q = s_q;
-  // Cut units never exceed 2 * C (a candidate cap keeps all units within 27 / 32 of the
+  // Cut units never exceed 2 * C (a candidate cap keeps all units within 29 / 32 of the
   // CTAs, the fallback rule cut units within 2 * max(C - I, C / 4)) and cut ranges 2 * C,
   // the slots the host provides (an overriding cap may ask for more).
   if (!flat && sB[B] > p.max_slots) {
