@@ -167,7 +167,8 @@ class GraphedDecoder:
         if batch is None or batch not in self.graphs:
             return None
         graph, logits, _ = self.graphs[batch]
-        slots_np = np.asarray(list(slots), dtype=np.int32)
+        slots_np = (slots if isinstance(slots, np.ndarray) and slots.dtype == np.int32
+                    else np.asarray(list(slots), dtype=np.int32))
         positions = self.cache._bm.decode_positions(slots_np)  # raises the reference's ValueError
         if self.cache.enable_copy_on_write:
             self.cache.copy_on_write([(s, int(p), 1) for s, p in zip(slots_np.tolist(), positions.tolist())])

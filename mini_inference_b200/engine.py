@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import enum
 import time
-from collections.abc import Sequence as SequenceOf
+from collections.abc import Callable, Sequence as SequenceOf
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -187,16 +187,26 @@ class ModelRunner:
         return self._tokens(hidden[0, ctx.last_index])
 
     @torch.inference_mode()
-    def decode_tokens(self, slots: SequenceOf[int], last_tokens: SequenceOf[int]) -> list[int]:
-        """One decode step for every sequence; the next token of each (engine/engine.py:108-123)."""
+    def decode_tokens(self, slots: SequenceOf[int], last_tokens: SequenceOf[int],
+                      while_running: Callable[[], None] | None = None) -> list[int]:
+        """One decode step for every sequence; the next token of each (engine/engine.py:108-123).
+
+        ``slots`` may be an int32 numpy array. ``while_running`` is called once the step's
+        GPU work is queued and before its tokens are read back, so that host bookkeeping
+        overlaps the GPU.
+        """
         if self.graphs is not None:
             ids = self.graphs.decode(slots, last_tokens)
             if ids is not None:
+                if while_running is not None:
+                    while_running()
                 return ids.tolist()
-        ctx = self.cache.decode_context(slots)
+        ctx = self.cache.decode_context([int(s) for s in slots])
         ids = self._ids_to_device(list(last_tokens)).unsqueeze(1)
         hidden = self.model(ids, ctx.positions.unsqueeze(1), ctx)
         ctx.commit()
+        if while_running is not None:
+            while_running()
         return self._tokens(hidden[:, -1])
 
 
@@ -281,11 +291,17 @@ class LLMEngine:
         ctx_tokens = 0
         n_finished = sum(s.is_finished for s in batch.prefills)
         if batch.decodes:
-            ctx_tokens = sum(len(s.prompt_token_ids) + len(s.output_token_ids) for s in batch.decodes)
+            context = [0]
+
+            def count_context() -> None:  # step statistics, counted while the GPU decodes
+                context[0] = sum(len(s.prompt_token_ids) + len(s.output_token_ids) for s in batch.decodes)
+
             # The token at the sequence's last position: its last output, or (chunked prefill)
             # the last prompt token when the final chunk left exactly that one.
-            tokens = self.runner.decode_tokens([s.slot for s in batch.decodes],
-                                               [(s.output_token_ids or s.prompt_token_ids)[-1] for s in batch.decodes])
+            tokens = self.runner.decode_tokens(self.scheduler.decode_slots(),
+                                               [(s.output_token_ids or s.prompt_token_ids)[-1] for s in batch.decodes],
+                                               while_running=count_context)
+            ctx_tokens = context[0]
             n_finished += self.scheduler.append_tokens(batch.decodes, tokens, time.perf_counter())
             new_tokens.extend(zip((s.seq_id for s in batch.decodes), tokens))
         self.step_stats.append(StepStats(

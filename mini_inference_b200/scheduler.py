@@ -194,6 +194,11 @@ class Scheduler:
             out.prefills.append(seq)
         return out
 
+    def decode_slots(self) -> np.ndarray:
+        """Slots of the last ``schedule()``'s decodes, in ``decodes`` order (int32; a view that
+        the next ``schedule()`` overwrites)."""
+        return self._dec_slots[:self._step.n_decodes]
+
     # ------------------------------------------------------------ engine/scheduler.py:143-169
     def append_token(self, seq, token: int, now: float) -> None:
         """Record a newly sampled token and finish the sequence if it is done."""
