@@ -461,6 +461,9 @@ typedef struct pkv_sched_step {
   int32_t n_prefills, n_decodes, n_preempted;
   int64_t* prefill_new_tokens;     /* tokens each prefill processes this step (NULL: not written); the
                                     * rest of the sequence unless chunked prefill splits it */
+  int64_t* decode_last_tokens;     /* each decode's last token, the one its step feeds the model: its
+                                    * last output, or its last prompt token when a chunked prefill
+                                    * left only that one (NULL: not written) */
 } pkv_sched_step;
 
 /* static_batching: the reference's scheduling == "static" (nobody joins a running batch) */

@@ -50,7 +50,7 @@ class PkvSchedStep(ctypes.Structure):
     _fields_ = [("capacity", c_int32), ("prefill_ids", c_void_p), ("prefill_slots", c_void_p),
                 ("prefill_cached_tokens", c_void_p), ("decode_ids", c_void_p), ("decode_slots", c_void_p),
                 ("preempted_ids", c_void_p), ("n_prefills", c_int32), ("n_decodes", c_int32),
-                ("n_preempted", c_int32), ("prefill_new_tokens", c_void_p)]
+                ("n_preempted", c_int32), ("prefill_new_tokens", c_void_p), ("decode_last_tokens", c_void_p)]
 
 
 P_POOL = POINTER(PkvPool)

@@ -163,6 +163,7 @@ int schedule_chunked(pkv_scheduler* s, pkv_sched_step* out) {
     const int64_t remaining = static_cast<int64_t>(r.tokens.size()) - held;
     if (remaining > 1) { partial.emplace_back(id, remaining); continue; }
     if (out->n_decodes >= cap) return PKV_ERR_WORKSPACE;
+    if (out->decode_last_tokens) out->decode_last_tokens[out->n_decodes] = r.tokens.back();
     out->decode_slots[out->n_decodes] = r.slot;
     out->decode_ids[out->n_decodes++] = id;
     budget -= 1;
@@ -222,7 +223,9 @@ int pkv_sched_schedule(pkv_scheduler* s, pkv_sched_step* out) {  // engine/sched
   for (int64_t id : preempted) out->preempted_ids[out->n_preempted++] = id;
   for (int64_t id : s->running) {
     if (out->n_decodes >= cap) return PKV_ERR_WORKSPACE;
-    out->decode_slots[out->n_decodes] = s->req(id).slot;
+    const Request& r = s->req(id);
+    if (out->decode_last_tokens) out->decode_last_tokens[out->n_decodes] = r.tokens.back();
+    out->decode_slots[out->n_decodes] = r.slot;
     out->decode_ids[out->n_decodes++] = id;
   }
   if (s->static_batching && !s->running.empty()) return PKV_OK;  // nobody joins a running static batch

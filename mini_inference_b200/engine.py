@@ -296,10 +296,10 @@ class LLMEngine:
             def count_context() -> None:  # step statistics, counted while the GPU decodes
                 context[0] = sum(len(s.prompt_token_ids) + len(s.output_token_ids) for s in batch.decodes)
 
-            # The token at the sequence's last position: its last output, or (chunked prefill)
-            # the last prompt token when the final chunk left exactly that one.
-            tokens = self.runner.decode_tokens(self.scheduler.decode_slots(),
-                                               [(s.output_token_ids or s.prompt_token_ids)[-1] for s in batch.decodes],
+            # The token at each sequence's last position (its last output, or with chunked
+            # prefill the last prompt token when the final chunk left exactly that one), as
+            # the native scheduler reports it.
+            tokens = self.runner.decode_tokens(self.scheduler.decode_slots(), self.scheduler.decode_last_tokens(),
                                                while_running=count_context)
             ctx_tokens = context[0]
             n_finished += self.scheduler.append_tokens(batch.decodes, tokens, time.perf_counter())

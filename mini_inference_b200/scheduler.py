@@ -98,10 +98,11 @@ class Scheduler:
         self._dec_slots = np.zeros(cap, np.int32)
         self._preempted = np.zeros(cap, np.int64)
         self._pre_new = np.zeros(cap, np.int64)
+        self._dec_last = np.zeros(cap, np.int64)
         self._step = PkvSchedStep(cap, self._pre_ids.ctypes.data, self._pre_slots.ctypes.data,
                                   self._pre_cached.ctypes.data, self._dec_ids.ctypes.data,
                                   self._dec_slots.ctypes.data, self._preempted.ctypes.data, 0, 0, 0,
-                                  self._pre_new.ctypes.data)
+                                  self._pre_new.ctypes.data, self._dec_last.ctypes.data)
         self.chunked_prefill = bool(getattr(config, "chunked_prefill", False))
         if self.chunked_prefill:
             _check(lib.pkv_sched_set_chunked_prefill(self._h, 1), "chunked prefill")
@@ -198,6 +199,12 @@ class Scheduler:
         """Slots of the last ``schedule()``'s decodes, in ``decodes`` order (int32; a view that
         the next ``schedule()`` overwrites)."""
         return self._dec_slots[:self._step.n_decodes]
+
+    def decode_last_tokens(self) -> np.ndarray:
+        """The token each of the last ``schedule()``'s decodes feeds the model: its last output,
+        or its last prompt token after a chunked prefill that left only that one (int64, in
+        ``decodes`` order; a view that the next ``schedule()`` overwrites)."""
+        return self._dec_last[:self._step.n_decodes]
 
     # ------------------------------------------------------------ engine/scheduler.py:143-169
     def append_token(self, seq, token: int, now: float) -> None:

@@ -159,22 +159,26 @@ def test_needs_the_native_cache():
                                   scheduling="continuous"), OracleBlockManager(8, 4, 4, 32))
 
 
-def _chunked_engine_loop(prompts, budget, max_seqs=4, blocks=64, max_tokens=3):
-    """The engine's side of chunked prefill on the allocator alone: returns per step
-    (prefills as (id, start, count, final), decode ids)."""
+def _chunked_engine_loop(prompts, budget, max_seqs=4, blocks=64, max_tokens=3, chunked=True):
+    """The engine's side of (chunked) prefill on the allocator alone: returns per step
+    (prefills as (id, start, count, final), decode ids). Every step also checks the decodes'
+    slots and last tokens as the native scheduler reports them for the engine."""
     from mini_inference_b200 import PagedKVCache
     from mini_inference_b200.scheduler import Scheduler, SequenceStatus
 
     cache = PagedKVCache(num_layers=1, num_kv_heads=1, head_dim=4, num_blocks=blocks, block_size=16,
                          max_seqs=max_seqs, max_len=512, dtype=torch.float32, device="cpu")
     sched = Scheduler(SimpleNamespace(max_num_seqs=max_seqs, max_num_batched_tokens=budget, max_model_len=512,
-                                      scheduling="continuous", chunked_prefill=True), cache)
+                                      scheduling="continuous", chunked_prefill=chunked), cache)
     seqs = [Seq(i, list(p), Sampling(max_tokens, True), status=SequenceStatus.WAITING) for i, p in enumerate(prompts)]
     for s in seqs:
         sched.add(s)
     log = []
     while sched.has_work():
         out = sched.schedule()
+        assert sched.decode_slots().tolist() == [s.slot for s in out.decodes]
+        assert sched.decode_last_tokens().tolist() == [(s.output_token_ids or s.prompt_token_ids)[-1]
+                                                       for s in out.decodes]
         step = []
         done = []
         for s, n in zip(out.prefills, out.prefill_tokens):
@@ -184,10 +188,11 @@ def _chunked_engine_loop(prompts, budget, max_seqs=4, blocks=64, max_tokens=3):
             step.append((s.seq_id, a, n, final))
             if final:
                 done.append(s)
-        sched.append_tokens(done, [7] * len(done), 0.0)
+        tok = 7000 + 10 * len(log)  # a different token per step and sequence
+        sched.append_tokens(done, [tok + i for i in range(len(done))], 0.0)
         for s in out.decodes:
             cache.lengths[s.slot] += 1
-        sched.append_tokens(out.decodes, [7] * len(out.decodes), 0.0)
+        sched.append_tokens(out.decodes, [tok + 5 + i for i in range(len(out.decodes))], 0.0)
         log.append((step, [s.seq_id for s in out.decodes]))
         assert len(log) < 100
     return log, seqs
@@ -212,3 +217,12 @@ def test_chunked_prefill_runs_decodes_first_and_finishes_a_one_token_tail_by_dec
     # A 33-token prompt under a 32-token budget leaves one token, which the next step decodes.
     log, _ = _chunked_engine_loop([list(range(33))], budget=32, max_tokens=2)
     assert log[0] == ([(0, 0, 32, False)], []) and log[1] == ([], [0])
+
+
+def test_decode_last_tokens_without_chunked_prefill():
+    """The slots and last tokens the scheduler reports for a step's decodes (checked every
+    step in the loop) with whole-prompt prefills and preemptions in a small pool."""
+    prompts = [list(range(k * 100, k * 100 + 20 + 7 * k)) for k in range(6)]
+    log, seqs = _chunked_engine_loop(prompts, budget=256, max_seqs=4, blocks=8, max_tokens=12, chunked=False)
+    assert any(decodes for _, decodes in log)
+    assert all(len(s.output_token_ids) == 12 for s in seqs)
