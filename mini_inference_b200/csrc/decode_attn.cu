@@ -56,7 +56,7 @@ constexpr int kNC = 8;   // consumer warps
 constexpr int kThreads = (kNC + 1) * 32;
 constexpr int kMaxBatch = 1024;    // the per-sequence tables live in shared memory
 constexpr int kSmallBatch = 256;   // batches up to this size take tables a quarter as large
-constexpr int kMinCap = 16;        // chunks: the fallback rule never cuts sequences of up to 16 blocks
+constexpr int kMinCap = 12;        // chunks: the fallback rule never cuts sequences of up to 12 blocks
 // Chunk caps (blocks) the split tries, smallest first, for batches of more than C / 2
 // sequences: it takes the smallest whose units fill at most 29/32 of the C CTAs, so that
 // every unit starts in the first wave and the longest units stay short, while a few CTAs
